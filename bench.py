@@ -1,0 +1,417 @@
+#!/usr/bin/env python3
+"""Paged-attention decode benchmark (HBM GB/s) for the sm_100a hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one step = one paged-attention launch over one batch): batch 64 per
+GPU, 12 heads, head_dim 64, fp16 K/V and q ~ N(0,1) from a seed, context
+U[128,1024], block size 16, block tables from a random permutation of a
+65536-block pool, scale 1/8, fp32 softmax.  Consecutive steps rotate through
+16 disjoint input sets (~1.8 GB of KV) so no launch is served from the
+126 MB L2.  Under torchrun every rank runs its own batch stream on its own
+GPU (weak scaling, no collective on the data path); the job's time is the
+max over ranks.
+
+The line also carries: the same metric end to end through the C-ABI with
+host buffers (e2e), the roofline of the kernel against the measured HBM copy
+bandwidth, the CPU baseline (the oracle's restatement of the reference CPU
+attention, multi-threaded, on a bounded sample), clocks sampled during the
+timed region, and the number of our kernel launches timed.
+
+--impl reference times the reference's CPU implementation of the path (the
+oracle restatement of gpu-engine/src/reference/cpu_model.cpp:131-162 through
+the block table; the reference exposes no standalone attention call) on the
+host cores, same metric and config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged-attn decode HBM GB/s"
+N_SETS = 16
+BATCH, N_HEAD, HEAD_DIM = 64, 12, 64
+
+
+def import_package(name: str = "lis_b200"):
+    import importlib.util
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg = ROOT / "llm-inference-server_b200"
+    spec = importlib.util.spec_from_file_location(name, pkg / "__init__.py", submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {"workload": "paged-attention decode microbench: batch 64 per GPU, 12 heads, head_dim 64, fp16 K/V and q "
+                        "N(0,1), context U[128,1024], block 16, random permutation of a 65536-block pool, scale 1/8",
+            "global_batch": BATCH * n_gpus, "accumulate": "f32", "out_dtype": "f16",
+            "l2": f"inputs larger than L2: {N_SETS} disjoint input sets (~1.8 GB of KV) rotated between launches",
+            "parallelism": f"sequence-sharded x{n_gpus}, no collective"}
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the attention kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "paged_decode_microbench.md"
+    if not p.exists():
+        return None, None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    n = re.search(r"algorithmic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return (float(m.group(1)) if m else None), (float(n.group(1)) if n else None)
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML while running."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.idx, self.period = device_index, period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.error = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((mhz, rs))
+                    except Exception as e:  # noqa: BLE001
+                        self.error = str(e)
+                        return
+                    time.sleep(self.period)
+
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
+        except Exception as e:  # noqa: BLE001
+            self.error = str(e)
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": self.error or "no samples"}
+        mhz = sorted(s[0] for s in self.samples)
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        reasons = [n for b, n in self.REASONS.items() if bits & b and b != 0x1]
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------- CPU legs
+
+def cpu_attention_rate(wl, budget_s: float, nthreads: int, n_seq=None):
+    """Times the oracle restatement of the reference CPU attention on a host
+    copy of input set 0 (optionally its first n_seq sequences)."""
+    from oracle import oracle as O
+    from lis_b200.workloads import attention_bytes
+    pool, bt, ctx, q = host_subset(wl, 0, n_seq)
+    nbytes = attention_bytes(ctx, N_HEAD, N_HEAD, HEAD_DIM, 2, 2, 2)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.paged_attention(O.F16, q, N_HEAD * HEAD_DIM, pool, bt, ctx, n_head=N_HEAD, n_kv_head=N_HEAD,
+                          head_dim=HEAD_DIM, max_blocks_per_seq=bt.shape[1], layer_idx=0, n_layer=1,
+                          nthreads=nthreads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return nbytes * reps / el / 1e9, reps, len(ctx), nbytes, el
+
+
+def host_subset(wl, i, n_seq):
+    from lis_b200.workloads import host_subset as hs
+    return hs(wl, i, n_seq)
+
+
+# ------------------------------------------------------------------ arms
+
+def run_reference_arm(args, rank: int, world: int) -> None:
+    """CPU reference arm: rank 0 only."""
+    if rank != 0:
+        return
+    import torch
+    from oracle import oracle as O
+    from lis_b200.workloads import attention_bytes
+    b2 = import_package()
+    O.load()
+    nthreads = os.cpu_count() or 1
+    # Inputs are generated exactly as for the GPU arm (host copy of input set 0).
+    if torch.cuda.is_available():
+        wl = b2_workload(b2, torch.device("cuda:0"), seed=0, n_sets=1)
+        pool, bt, ctx, q = host_subset(wl, 0, None)
+        del wl
+        torch.cuda.empty_cache()
+    else:
+        pool, bt, ctx, q = host_workload(seed=0)
+    nbytes_full = attention_bytes(ctx, N_HEAD, N_HEAD, HEAD_DIM, 2, 2, 2)
+    t0 = time.perf_counter()
+    O.paged_attention(O.F16, q, N_HEAD * HEAD_DIM, pool, bt, ctx, n_head=N_HEAD, n_kv_head=N_HEAD, head_dim=HEAD_DIM,
+                      max_blocks_per_seq=bt.shape[1], layer_idx=0, n_layer=1, nthreads=nthreads)
+    t_full = time.perf_counter() - t0
+    # Size each step so K+W steps stay within ~2 minutes.
+    n_seq = len(ctx)
+    budget = 120.0
+    if (args.steps + args.warmup) * t_full > budget:
+        n_seq = max(1, int(len(ctx) * budget / ((args.steps + args.warmup) * t_full)))
+    ctx_s, bt_s, q_s = ctx[:n_seq], bt[:n_seq], q[: n_seq * N_HEAD * HEAD_DIM]
+    nbytes = attention_bytes(ctx_s, N_HEAD, N_HEAD, HEAD_DIM, 2, 2, 2)
+    for _ in range(args.warmup):
+        O.paged_attention(O.F16, q_s, N_HEAD * HEAD_DIM, pool, bt_s, ctx_s, n_head=N_HEAD, n_kv_head=N_HEAD,
+                          head_dim=HEAD_DIM, max_blocks_per_seq=bt.shape[1], layer_idx=0, n_layer=1,
+                          nthreads=nthreads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.paged_attention(O.F16, q_s, N_HEAD * HEAD_DIM, pool, bt_s, ctx_s, n_head=N_HEAD, n_kv_head=N_HEAD,
+                          head_dim=HEAD_DIM, max_blocks_per_seq=bt.shape[1], layer_idx=0, n_layer=1,
+                          nthreads=nthreads)
+    el = time.perf_counter() - t0
+    value = nbytes * args.steps / el / 1e9
+    sample = (f"{n_seq} of {len(ctx)} sequences of one batch per step ({nbytes / 1e6:.1f} MB of "
+              f"{nbytes_full / 1e6:.1f} MB), oracle port of cpu_model.cpp:131-162 through the block table")
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": workload_config(1),
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def host_workload(seed: int):
+    """Host-only generation of one batch (used when no GPU is present)."""
+    from oracle import oracle as O
+    rng = np.random.Generator(np.random.PCG64(seed))
+    ctx = rng.integers(128, 1025, size=BATCH).astype(np.int32)
+    nb = (ctx + 15) // 16
+    bt = np.zeros((BATCH, 64), np.int32)
+    o = 0
+    for b in range(BATCH):
+        bt[b, : nb[b]] = np.arange(o, o + nb[b])
+        o += int(nb[b])
+    pool = O.round_to(O.F16, rng.standard_normal(o * 2 * 16 * N_HEAD * HEAD_DIM, dtype=np.float32))
+    q = O.round_to(O.F16, rng.standard_normal(BATCH * N_HEAD * HEAD_DIM, dtype=np.float32))
+    return pool, bt, ctx, q
+
+
+def b2_workload(b2, device, seed: int, n_sets: int):
+    import torch
+    from lis_b200.workloads import make_attention_workload
+    return make_attention_workload(device, seed=seed, n_sets=n_sets, batch=BATCH, n_head=N_HEAD, n_kv_head=N_HEAD,
+                                   head_dim=HEAD_DIM, dtype=torch.float16)
+
+
+def run_ours(args, rank: int, world: int, dist) -> None:
+    import torch
+    b2 = import_package()
+    b2.load()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    wl = b2_workload(b2, dev, seed=1000 + rank, n_sets=N_SETS)
+    stream = torch.cuda.current_stream(dev)
+    wl.workspace = b2.attention_workspace(wl.sets[0].args)
+    ws = wl.workspace
+    lib = b2.load()
+    import ctypes
+    ws_ptr, ws_n, sptr = ws.data_ptr(), ws.numel(), stream.cuda_stream
+    arg_refs = [ctypes.byref(s.args) for s in wl.sets]
+    nsets = len(wl.sets)
+
+    def launch(i):
+        rc = lib.b2_paged_attention(arg_refs[i % nsets], ws_ptr, ws_n, sptr)
+        if rc != 0:
+            raise RuntimeError(f"b2_paged_attention failed: {rc} {lib.b2_last_error_string().decode()}")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    # --------------------------------------------------- device-resident timing
+    for i in range(args.warmup):
+        launch(i)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            launch(i)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    my_bytes = sum(wl.sets[i % nsets].bytes for i in range(args.steps))
+    t_max = max_over_ranks(ms)
+    tot_bytes = sum_over_ranks(float(my_bytes))
+    value = tot_bytes / (t_max * 1e-3) / 1e9
+    errs = b2.device_errors()
+
+    # ------------------------------------------------ end to end through the C-ABI
+    # Per step, like Engine::decode_step (gpu-engine/src/engine.cu:343-368): upload
+    # q, block tables and seq_lens from pinned host memory, launch, download the
+    # output, synchronise.  The KV cache stays resident (it is the engine's state).
+    hq = [s.d_q.cpu().pin_memory() for s in wl.sets]
+    hbt = [torch.from_numpy(s.block_tables).pin_memory() for s in wl.sets]
+    hsl = [torch.from_numpy(s.seq_lens).pin_memory() for s in wl.sets]
+    hout = torch.empty_like(wl.sets[0].d_out, device="cpu").pin_memory()
+    h2d = hq[0].numel() * hq[0].element_size() + hbt[0].numel() * 4 + hsl[0].numel() * 4
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step(i):
+        s = wl.sets[i % nsets]
+        s.d_q.copy_(hq[i % nsets], non_blocking=True)
+        s.d_block_tables.copy_(hbt[i % nsets], non_blocking=True)
+        s.d_seq_lens.copy_(hsl[i % nsets], non_blocking=True)
+        launch(i)
+        hout.copy_(s.d_out, non_blocking=True)
+        stream.synchronize()
+
+    e2e_steps = min(args.steps, 2000)
+    for i in range(max(3, args.warmup // 10)):
+        e2e_step(i)
+    barrier()
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev2.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    ev3.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(ev2.elapsed_time(ev3))
+    e2e_bytes = sum_over_ranks(float(sum(wl.sets[i % nsets].bytes for i in range(e2e_steps))))
+    e2e_value = e2e_bytes / (e2e_ms * 1e-3) / 1e9
+
+    # --------------------------------------------------------------- CPU baseline
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        nthreads = os.cpu_count() or 1
+        gbs, reps, nseq, nbytes, el = cpu_attention_rate(wl, args.cpu_seconds, nthreads)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
+               "sample": f"input set 0 ({nseq} sequences, {nbytes / 1e6:.1f} MB KV) x {reps} passes in {el:.1f} s; "
+                         f"oracle restatement of cpu_model.cpp:131-162 through the block table"}
+
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    per_launch_bytes = my_bytes / args.steps
+    per_launch_s = ms * 1e-3 / args.steps
+    achieved = per_launch_bytes / per_launch_s / 1e9
+    traffic, traffic_alg = profiled_traffic()
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(t_max / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": workload_config(world),
+        "pct_of_peak": round(100.0 * value / (peak * world), 2),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": traffic, "traffic_note": "dram read+write bytes per launch from the committed ncu "
+                                                         "summary (profiles/paged_decode_microbench.md)"
+                     if traffic else "no ncu summary committed yet",
+                     "algorithmic_bytes_per_launch": int(per_launch_bytes),
+                     "vs_nominal_8TBs": round(achieved / 8000.0, 4)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 5),
+                "path": "b2_paged_attention via ctypes; pinned-host q/block tables/seq_lens up, output down, "
+                        "stream sync every step"},
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps,
+        "device_errors": errs,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist = tdist
+    try:
+        run_ours(args, rank, world, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

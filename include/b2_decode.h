@@ -1,0 +1,205 @@
+/*
+ * b2_decode.h -- C-ABI of the sm_100a decode hot path (libb2decode.so).
+ *
+ * Drop-in for the kernel-launch layer of kanish10/LLM-Inference-Server
+ * (gpu-engine/include/engine/kernels.h:29-93): every entry point below names
+ * the reference function it replaces.  Plain C: no CUDA or torch types in the
+ * signatures, so cgo / ctypes / JNI can bind it directly.
+ *
+ * Conventions kept from the reference:
+ *   - paged KV layout, one block = all layers of 16 token positions:
+ *       [block][layer][2 (K,V)][16][n_kv_head][head_dim]   (kv_cache.h:6-8)
+ *     (n_kv_head == n_head for multi-head attention; the reference calls it
+ *     n_heads.)
+ *   - seq_lens: b2_kv_append takes the PRE-append count (the slot written);
+ *     b2_paged_attention takes the POST-append key count (kernels.h:22-27).
+ *   - q / k / v may live inside a fused QKV row: *_row_stride is the element
+ *     distance between batch rows (kernels.h:51-56, 67-70).
+ *   - attention output is packed [batch, n_head, head_dim] (kernels.h:73).
+ *
+ * Additions over the reference (all optional to use):
+ *   - dtype per call (f32 / f16 / bf16) instead of half only;
+ *   - n_kv_head for grouped-query attention;
+ *   - num_blocks (pool capacity) so kernels can refuse out-of-range block
+ *     ids instead of reading or writing outside the pool;
+ *   - status codes: 0 = OK, < 0 = argument error found on the host before
+ *     any launch, > 0 = the cudaError_t seen right after the launch.
+ *     The reference launchers return void and never check.
+ *
+ * All buffers are caller-owned device memory.  No entry point allocates,
+ * frees or synchronises, so every launch can be captured in a CUDA graph.
+ * All pointers handed to the attention and append kernels must be 16-byte
+ * aligned, and every row stride times the element size a multiple of 16 bytes.
+ */
+#ifndef B2_DECODE_H
+#define B2_DECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2_API __attribute__((visibility("default")))
+#else
+#define B2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t passed as an opaque pointer; NULL is the legacy default stream. */
+typedef void* b2_stream_t;
+
+typedef enum b2_dtype { B2_F32 = 0, B2_F16 = 1, B2_BF16 = 2 } b2_dtype;
+
+#define B2_BLOCK_TOKENS 16 /* gpu-engine/include/engine/kv_cache.h:8 */
+
+#define B2_OK 0
+#define B2_ERR_NULL (-1)        /* a required pointer is NULL */
+#define B2_ERR_DTYPE (-2)       /* unknown or unsupported dtype combination */
+#define B2_ERR_SHAPE (-3)       /* a size is out of range or inconsistent */
+#define B2_ERR_ALIGN (-4)       /* a pointer or stride breaks the 16-byte rule */
+#define B2_ERR_WORKSPACE (-5)   /* workspace missing or too small */
+#define B2_ERR_UNSUPPORTED (-6) /* a shape this build has no kernel for */
+#define B2_ERR_DEVICE (-7)      /* the device query failed */
+
+/* Device-side error bits, accumulated in a per-device word (b2_device_errors). */
+#define B2_DEVERR_BLOCK_ID 1u   /* a block-table entry outside [0, num_blocks) was clamped */
+#define B2_DEVERR_SEQ_LEN 2u    /* a seq_len beyond max_blocks_per_seq*16 (or < 0) was clamped */
+#define B2_DEVERR_TIMEOUT 4u    /* a bounded pipeline wait gave up; the output is invalid */
+#define B2_DEVERR_TOKEN 8u      /* a token id or position outside its table was clamped */
+
+/* Library version string. */
+B2_API const char* b2_version(void);
+
+/* Text of the last host-side error on the calling thread ("" if none). */
+B2_API const char* b2_last_error_string(void);
+
+/* Reads the device error word of the current device and clears it.  This
+ * call synchronises the device; use it in tests and health checks, not per step. */
+B2_API int b2_device_errors(uint32_t* bits_out);
+
+/* ------------------------------------------------------------------------
+ * Paged KV append (reshape-and-cache).
+ * Replaces kernels::launch_kv_append (gpu-engine/include/engine/kernels.h:51-60,
+ * gpu-engine/src/kernels/attention.cu:131-139).
+ * pool[block_tables[b][p/16]][layer][K|V][p%16][h][:] = k|v[b][h][:], p = seq_lens[b]
+ * (pre-append).  A bit copy.  When k_bias / v_bias are non-NULL the bias
+ * ([n_kv_head*head_dim], same dtype) is added first (the reference adds the
+ * QKV bias in a separate add_bias launch, gpu-engine/src/engine.cu:158).
+ * When seq_lens_post is non-NULL it receives seq_lens[b] + 1 (the reference's
+ * launch_add_one, kernels.h:62-65), so one launch does both.
+ * ---------------------------------------------------------------------- */
+typedef struct B2KvAppendArgs {
+    int32_t dtype; /* b2_dtype of k, v, biases and pool */
+    void* kv_pool;
+    const void* k;
+    const void* v;
+    int32_t kv_row_stride; /* elements between batch rows of k and v */
+    const void* k_bias;    /* optional */
+    const void* v_bias;    /* optional */
+    const int32_t* block_tables; /* [batch, max_blocks_per_seq] */
+    const int32_t* seq_lens;     /* [batch], pre-append */
+    int32_t* seq_lens_post;      /* optional [batch] output: seq_lens + 1 */
+    int32_t batch;
+    int32_t n_kv_head;
+    int32_t head_dim;
+    int32_t max_blocks_per_seq;
+    int32_t layer_idx;
+    int32_t n_layer;
+    int32_t num_blocks; /* pool capacity in blocks (bounds check) */
+} B2KvAppendArgs;
+
+B2_API int b2_kv_append(const B2KvAppendArgs* args, b2_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Paged decode attention.
+ * Replaces kernels::launch_paged_attention and PagedAttentionArgs
+ * (gpu-engine/include/engine/kernels.h:67-87, attention.cu:141-149).
+ * out[b,h,:] = sum_j softmax_j(scale * q[b,h,:].k_j) v_j over the seq_lens[b]
+ * keys of sequence b (post-append count), keys of kv head h / (n_head/n_kv_head).
+ * A sequence with seq_lens[b] == 0 gets a zero output, like the reference.
+ *
+ * The work is split over the whole GPU by KV blocks (every CTA gets the same
+ * number of 16-token blocks, whatever the per-sequence lengths); sequences
+ * that span CTAs are merged in-kernel by the last CTA to finish.  That needs
+ * a workspace: size it with b2_paged_attention_workspace_bytes and zero it
+ * once with b2_paged_attention_workspace_init before its first use (the
+ * kernel leaves it zeroed again).  One workspace serves any number of
+ * launches on one stream; launches that may run concurrently need their own.
+ * ---------------------------------------------------------------------- */
+typedef struct B2PagedAttnArgs {
+    int32_t dtype;     /* b2_dtype of q and the pool */
+    int32_t out_dtype; /* B2_F32, or the same as dtype */
+    const void* q;
+    int32_t q_row_stride; /* elements between batch rows of q */
+    const void* q_bias;   /* optional [n_head*head_dim], added to q first */
+    const void* kv_pool;
+    const int32_t* block_tables; /* [batch, max_blocks_per_seq] */
+    const int32_t* seq_lens;     /* [batch], post-append key counts */
+    void* out;                   /* [batch, n_head, head_dim] packed */
+    int32_t batch;
+    int32_t n_head;
+    int32_t n_kv_head;
+    int32_t head_dim; /* 64 or 128 */
+    int32_t max_blocks_per_seq;
+    int32_t layer_idx;
+    int32_t n_layer;
+    int32_t num_blocks; /* pool capacity in blocks (bounds check) */
+    float scale;        /* 0 selects 1/sqrt(head_dim) */
+} B2PagedAttnArgs;
+
+/* Workspace bytes for launches with this batch and head shape on the
+ * current device (depends on the SM count). */
+B2_API size_t b2_paged_attention_workspace_bytes(const B2PagedAttnArgs* args);
+
+/* Zeroes the workspace's merge counters (stream-ordered, no allocation). */
+B2_API int b2_paged_attention_workspace_init(void* workspace, size_t workspace_bytes,
+                                      const B2PagedAttnArgs* args, b2_stream_t stream);
+
+B2_API int b2_paged_attention(const B2PagedAttnArgs* args, void* workspace, size_t workspace_bytes,
+                       b2_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Row kernels around attention.  All take dtype (f32 / f16 / bf16),
+ * compute in fp32, and accept out == x (in place).
+ * ---------------------------------------------------------------------- */
+
+/* Fused residual add + LayerNorm.  Replaces kernels::launch_add_layernorm
+ * (kernels.h:39-44, layernorm.cu:56-63):
+ *   r = x + residual_in (+ bias when bias != NULL);  residual_out = r;
+ *   out = (r - mean(r)) / sqrt(var(r) + eps) * gamma + beta.
+ * Statistics are taken over the unrounded fp32 r.  x may be NULL (adds zero),
+ * replacing the reference's persistent zero buffer (engine.cu:97). */
+B2_API int b2_add_layernorm(int32_t dtype, void* out, void* residual_out, const void* x,
+                     const void* bias, const void* residual_in, const void* gamma,
+                     const void* beta, int32_t batch, int32_t d_model, float eps,
+                     b2_stream_t stream);
+
+/* out = gelu_tanh(x + bias).  Replaces kernels::launch_bias_gelu (kernels.h:46-49). */
+B2_API int b2_bias_gelu(int32_t dtype, void* out, const void* x, const void* bias, int32_t batch,
+                 int32_t d_ff, b2_stream_t stream);
+
+/* out = x + bias.  Replaces kernels::launch_add_bias (kernels.h:35-37). */
+B2_API int b2_add_bias(int32_t dtype, void* out, const void* x, const void* bias, int32_t batch,
+                int32_t dim, b2_stream_t stream);
+
+/* out[b] = in[b] + 1.  Replaces kernels::launch_add_one (kernels.h:62-65). */
+B2_API int b2_add_one(int32_t* out, const int32_t* in, int32_t batch, b2_stream_t stream);
+
+/* out = wte[token_ids[b]] + wpe[positions[b]].  Replaces kernels::launch_embedding
+ * (kernels.h:31-33).  vocab / n_pos bound the lookups (clamped and flagged). */
+B2_API int b2_embedding(int32_t dtype, void* out, const void* wte, const void* wpe,
+                 const int32_t* token_ids, const int32_t* positions, int32_t batch,
+                 int32_t d_model, int32_t vocab, int32_t n_pos, b2_stream_t stream);
+
+/* Greedy argmax per row, ties to the lowest index (cpu_model.cpp:186-195).
+ * Replaces kernels::launch_argmax (kernels.h:89-92). */
+B2_API int b2_argmax(int32_t dtype, int32_t* out_tokens, const void* logits, int32_t batch,
+              int32_t vocab, b2_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2_DECODE_H */

@@ -1,0 +1,514 @@
+// attention.cuh -- paged decode attention for sm_100a.
+//
+// Computes what gpu-engine/src/kernels/attention.cu:49-127 computes
+// (softmax(q.K^T * scale) V over the block-table KV cache, fp32 softmax
+// state), organised for B200 instead of one CTA per (batch, head):
+//
+//  * Work split.  Every sequence b owns nb_b = ceil(seq_len_b / 16) paged
+//    blocks.  All blocks of all sequences form one list of N units, and CTA i
+//    of the G resident CTAs (one per SM) takes units [i*N/G, (i+1)*N/G).  The
+//    split is therefore even whatever the length skew, and a sequence may be
+//    cut into segments handled by several CTAs (flash-decoding split-K with
+//    the split points chosen by load, not by a fixed chunk size).
+//  * Data movement.  For one layer, a block's K rows of ALL kv heads are one
+//    contiguous slab of 16*n_kv_head*head_dim elements (layout
+//    [block][layer][K|V][16][n_kv_head][head_dim], kv_cache.h:6-7), with the V
+//    slab right behind it.  A producer warp streams each unit's K and V slabs
+//    (only the valid token rows) with 1-D bulk async copies (cp.async.bulk,
+//    the TMA engine's untiled path) into a ring of shared-memory stages
+//    guarded by mbarriers; q rows travel the same way at a segment's first
+//    block.  Consumer warps never touch global memory for K/V.
+//  * Math.  Consumer thread (ts, c) owns 16-byte chunk c of the token row
+//    (kv head c / GL, dims (c % GL) * E ...) and the tokens t = ts (mod k) of
+//    each block.  QK^T: 16-byte shared loads, fp32 FMAs, a GL-lane xor-shuffle
+//    reduction.  Softmax: one (head, token) pair per lane, 16-lane max/sum
+//    shuffles, online rescaling in the log2 domain.  PV: the same chunk
+//    ownership, so the accumulator stays in registers.
+//  * Merge.  A sequence finished inside one CTA is normalised and written
+//    directly.  Otherwise each CTA writes (m, l, acc) to the workspace, bumps
+//    the sequence's counter, and the CTA that arrives last merges all
+//    partials and resets the counter to zero (no CTA ever waits for another).
+//
+// Every wait is bounded (b2_common.cuh): on timeout the CTA flags
+// B2_DEVERR_TIMEOUT, drains its own copies in flight and returns.
+#pragma once
+
+#include "b2_common.cuh"
+
+namespace b2 {
+
+struct AttnParams {
+    const void* q;
+    long long q_row_stride;  // elements
+    const void* q_bias;
+    const void* pool;
+    const int* block_tables;
+    const int* seq_lens;
+    void* out;
+    int batch, n_head, n_kv_head, mbps, layer_idx, n_layer, num_blocks;
+    float scale_log2;  // scale * log2(e)
+    int ksplit;        // token subgroups per block (1, 2 or 4)
+    int ncons;         // consumer threads, multiple of 32
+    int stages;
+    int stage_bytes;
+    int slab_bytes;  // 16 * n_kv_head * head_dim * sizeof(T)
+    int q_bytes;     // n_head * head_dim * sizeof(T)
+    int off_meta;    // within a stage
+    int off_scores, off_probs, off_m, off_l, off_corr, off_scratch, off_misc, off_bars;
+    unsigned int* counters;  // [batch] merge counters, zero between launches
+    float2* part_ml;         // [grid + batch][n_head] (m, l)
+    float* part_acc;         // [grid + batch][n_head][head_dim]
+};
+
+// Largest CTA index whose range start floor(i*N/G) is <= u.
+__device__ __forceinline__ int cta_of_unit(long long u, long long N, int G) {
+    return static_cast<int>(((u + 1) * G - 1) / N);
+}
+
+__device__ __forceinline__ int clamp_seq_len(int c, int mbps) {
+    return c < 0 ? 0 : (c > mbps * kBlockTokens ? mbps * kBlockTokens : c);
+}
+
+// Exclusive scan of v over all threads of the CTA; *total gets the sum.
+// warp_sums needs 32 ints of shared memory.  Contains __syncthreads.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nwarps = (blockDim.x + 31) >> 5;
+    int incl = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nwarps ? warp_sums[lane] : 0;
+        int wi = w;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, wi, off);
+            if (lane >= off) wi += y;
+        }
+        warp_sums[lane] = wi - w;  // exclusive prefix of warp totals
+        if (lane == 31) warp_sums[32] = wi;
+    }
+    __syncthreads();
+    *total = warp_sums[32];
+    return warp_sums[warp] + incl - v;
+}
+
+template <typename T, int DH, int QG, typename OutT, int MAXT>
+__global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams p) {
+    constexpr int E = Elem<T>::kPer16B;
+    constexpr int GL = DH / E;  // lanes sharing one head row
+    static_assert(GL >= 2 && GL <= 32 && (32 % GL) == 0, "head_dim / dtype combination");
+    constexpr int ES = static_cast<int>(sizeof(T));
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tid = threadIdx.x;
+    const int H = p.n_head;
+    const int Hkv = p.n_kv_head;
+    const int C = Hkv * GL;  // 16-byte chunks per token row (all kv heads)
+    const int G = gridDim.x;
+    const int cta = blockIdx.x;
+    const int B = p.batch;
+    const int S = p.stages;
+
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
+    uint64_t* empty = full + S;
+    int* misc = reinterpret_cast<int*>(smem + p.off_misc);  // [0..1] start, [2..34] scan, [40] last flag
+    float* sS = reinterpret_cast<float*>(smem + p.off_scores);
+    float* sP = reinterpret_cast<float*>(smem + p.off_probs);
+    float* sM = reinterpret_cast<float*>(smem + p.off_m);
+    float* sL = reinterpret_cast<float*>(smem + p.off_l);
+    float* sCorr = reinterpret_cast<float*>(smem + p.off_corr);
+    float* sScratch = reinterpret_cast<float*>(smem + p.off_scratch);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], static_cast<uint32_t>(p.ncons / 32));
+        }
+        fence_mbar_init();
+    }
+
+    // ---- prologue: per-sequence block counts, global prefix, this CTA's range
+    const int per = (B + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
+    const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
+    int local = 0;
+    for (int b = b_lo; b < b_hi; ++b) local += (clamp_seq_len(__ldg(p.seq_lens + b), p.mbps) + 15) >> 4;
+    int N = 0;
+    const int excl = block_exclusive_scan(local, misc + 2, &N);
+    const long long s_unit = static_cast<long long>(cta) * N / G;
+    const long long e_unit = static_cast<long long>(cta + 1) * N / G;
+    {
+        int run = excl;
+        for (int b = b_lo; b < b_hi; ++b) {
+            const int raw = __ldg(p.seq_lens + b);
+            const int cl = clamp_seq_len(raw, p.mbps);
+            const int nb = (cl + 15) >> 4;
+            if (nb > 0 && run <= s_unit && s_unit < run + nb) {
+                misc[0] = b;
+                misc[1] = run;
+            }
+            run += nb;
+            if (b % G == cta) {
+                if (raw != cl) flag_error(B2_DEVERR_SEQ_LEN);
+                if (nb == 0) {  // no keys: the reference writes 0 (l == 0)
+                    OutT* o = reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(b) * H * DH;
+                    for (int i = 0; i < H * DH; ++i) o[i] = Elem<OutT>::from_f(0.0f);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const int nunits = static_cast<int>(e_unit - s_unit);
+    if (nunits <= 0) return;
+
+    const size_t row_elems = static_cast<size_t>(Hkv) * DH;
+    const size_t slab_elems = row_elems * kBlockTokens;
+    const int row_bytes = static_cast<int>(row_elems) * ES;
+
+    if (tid >= p.ncons) {
+        // ================================================= producer warp
+        const int lane = tid & 31;
+        const char* pool = static_cast<const char*>(p.pool);
+        const size_t block_elems = static_cast<size_t>(p.n_layer) * 2 * slab_elems;
+        const size_t layer_off = static_cast<size_t>(p.layer_idx) * 2 * slab_elems;
+        long long u = s_unit;
+        int bb = misc[0];
+        long long Pb = misc[1];
+        int n = 0;
+        bool failed = false;
+        while (u < e_unit && !failed && bb < B) {
+            const int b = bb + lane;
+            int cl = 0;
+            if (b < B) cl = clamp_seq_len(__ldg(p.seq_lens + b), p.mbps);
+            const int nbl = (cl + 15) >> 4;
+            int incl = nbl;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += y;
+            }
+            const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
+            for (int sidx = 0; sidx < 32 && u < e_unit && !failed; ++sidx) {
+                const int nbs = __shfl_sync(0xffffffffu, nbl, sidx);
+                const int cs = __shfl_sync(0xffffffffu, cl, sidx);
+                const long long Ps = Pb + __shfl_sync(0xffffffffu, incl - nbl, sidx);
+                const int bs = bb + sidx;
+                if (nbs == 0 || Ps + nbs <= u) continue;
+                const int j0 = static_cast<int>(u - Ps);
+                const int j1 = static_cast<int>(min(e_unit, Ps + nbs) - Ps);
+                const int i0 = cta_of_unit(Ps, N, G);
+                const int nseg = cta_of_unit(Ps + nbs - 1, N, G) - i0 + 1;
+                for (int jc = j0; jc < j1 && !failed; jc += 32) {
+                    const int jj = jc + lane;
+                    int blk_l = 0;
+                    if (jj < j1) {
+                        blk_l = __ldg(p.block_tables + static_cast<size_t>(bs) * p.mbps + jj);
+                        if (blk_l < 0 || blk_l >= p.num_blocks) {
+                            flag_error(B2_DEVERR_BLOCK_ID);
+                            blk_l = 0;
+                        }
+                    }
+                    const int cnt = min(32, j1 - jc);
+                    for (int x = 0; x < cnt; ++x) {
+                        const int blk = __shfl_sync(0xffffffffu, blk_l, x);
+                        int ok = 1;
+                        if (lane == 0) {
+                            const int st = n % S;
+                            const uint32_t ph = static_cast<uint32_t>(n / S) & 1u;
+                            if (!mbar_wait_bounded(&empty[st], ph ^ 1u)) {
+                                ok = 0;
+                            } else {
+                                const int j = jc + x;
+                                const int ntok = min(kBlockTokens, cs - j * kBlockTokens);
+                                const int first = (j == j0) ? 1 : 0;
+                                const int lastf = (j == j1 - 1) ? 2 : 0;
+                                unsigned char* stage = smem + static_cast<size_t>(st) * p.stage_bytes;
+                                *reinterpret_cast<int4*>(stage + p.off_meta) =
+                                    make_int4(bs, ntok | ((first | lastf) << 8), nseg, i0);
+                                const uint32_t kv_bytes = static_cast<uint32_t>(ntok * row_bytes);
+                                mbar_arrive_expect_tx(&full[st], 2u * kv_bytes + (first ? p.q_bytes : 0));
+                                const char* src = pool + (static_cast<size_t>(blk) * block_elems + layer_off) * ES;
+                                bulk_g2s(stage, src, kv_bytes, &full[st]);
+                                bulk_g2s(stage + p.slab_bytes, src + slab_elems * ES, kv_bytes, &full[st]);
+                                if (first) {
+                                    const char* qsrc = static_cast<const char*>(p.q) +
+                                                       static_cast<size_t>(bs) * p.q_row_stride * ES;
+                                    bulk_g2s(stage + 2 * p.slab_bytes, qsrc, static_cast<uint32_t>(p.q_bytes),
+                                             &full[st]);
+                                }
+                            }
+                        }
+                        ok = __shfl_sync(0xffffffffu, ok, 0);
+                        if (!ok) {
+                            failed = true;
+                            break;
+                        }
+                        ++n;
+                    }
+                }
+                u = Ps + j1;
+            }
+            bb += 32;
+            Pb += wtotal;
+        }
+        if (lane == 0) {
+            if (failed) flag_error(B2_DEVERR_TIMEOUT);
+            // Never leave with copies in flight: wait (bounded) for the last
+            // issue of every stage to land.
+            for (int m = max(0, n - S); m < n; ++m)
+                if (!mbar_wait_bounded(&full[m % S], static_cast<uint32_t>(m / S) & 1u))
+                    flag_error(B2_DEVERR_TIMEOUT);
+        }
+        return;
+    }
+
+    // ===================================================== consumer threads
+    const int ncons = p.ncons;
+    const int ks = p.ksplit;
+    const int ts = tid / C;
+    const int c = tid - ts * C;
+    const bool active = ts < ks;
+    const int hk = c / GL;
+    const int dg = c - hk * GL;
+    const int lane = tid & 31;
+    const unsigned gmask = (GL == 32) ? 0xffffffffu : (((1u << GL) - 1u) << (lane & ~(GL - 1)));
+    const unsigned hmask = 0xffffu << (lane & 16);
+
+    float qf[QG][E];
+    float acc[QG][E];
+#pragma unroll
+    for (int g = 0; g < QG; ++g)
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            qf[g][e] = 0.0f;
+            acc[g][e] = 0.0f;
+        }
+
+    OutT* out = static_cast<OutT*>(p.out);
+    for (int n = 0; n < nunits; ++n) {
+        const int st = n % S;
+        const uint32_t ph = static_cast<uint32_t>(n / S) & 1u;
+        unsigned char* stage = smem + static_cast<size_t>(st) * p.stage_bytes;
+        const bool timed_out = !mbar_wait_bounded(&full[st], ph);
+        int4 meta = make_int4(0, 0, 1, 0);
+        if (!timed_out) meta = *reinterpret_cast<const int4*>(stage + p.off_meta);
+        const int b = meta.x;
+        const int ntok = timed_out ? 0 : min(meta.y & 0xff, kBlockTokens);
+        const bool first = (meta.y >> 8) & 1;
+        const bool last = (meta.y >> 9) & 1;
+
+        if (first && active) {
+            const unsigned char* qs = stage + 2 * p.slab_bytes;
+#pragma unroll
+            for (int g = 0; g < QG; ++g) {
+                float f[E], bf[E];
+                unpack16<T>(ld_shared16(qs + ((hk * QG + g) * DH + dg * E) * ES), f);
+                if (p.q_bias != nullptr) {
+                    // q + bias rounded to T, as the reference's separate
+                    // add_bias launch stores it (engine.cu:158).
+                    unpack16<T>(__ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.q_bias) +
+                                                                     (hk * QG + g) * DH + dg * E)),
+                                bf);
+#pragma unroll
+                    for (int e = 0; e < E; ++e) f[e] = Elem<T>::to_f(Elem<T>::from_f(__fadd_rn(f[e], bf[e])));
+                }
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    qf[g][e] = f[e] * p.scale_log2;
+                    acc[g][e] = 0.0f;
+                }
+            }
+        }
+
+        // ---- phase A: scores s[h][t] = q_h . k_t (log2 domain)
+        if (active) {
+            const unsigned char* K = stage;
+            for (int t = ts; t < ntok; t += ks) {
+                float kf[E];
+                unpack16<T>(ld_shared16(K + (t * C + c) * 16), kf);
+                float d[QG];
+#pragma unroll
+                for (int g = 0; g < QG; ++g) {
+                    float a = 0.0f;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) a = fmaf(qf[g][e], kf[e], a);
+                    d[g] = a;
+                }
+#pragma unroll
+                for (int off = GL / 2; off > 0; off >>= 1)
+#pragma unroll
+                    for (int g = 0; g < QG; ++g) d[g] += __shfl_xor_sync(gmask, d[g], off);
+                if (dg == 0) {
+#pragma unroll
+                    for (int g = 0; g < QG; ++g) sS[(hk * QG + g) * kBlockTokens + t] = d[g];
+                }
+            }
+        }
+        if (named_sync_or(1, ncons, timed_out)) {
+            if (tid == 0) flag_error(B2_DEVERR_TIMEOUT);
+            break;
+        }
+
+        // ---- phase B: online softmax statistics per head over this block
+        for (int idx = tid; idx < H * kBlockTokens; idx += ncons) {
+            const int h = idx >> 4;
+            const int t = idx & 15;
+            const float sv = t < ntok ? sS[idx] : -INFINITY;
+            float bm = sv;
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) bm = fmaxf(bm, __shfl_xor_sync(hmask, bm, off));
+            const float mo = first ? -INFINITY : sM[h];
+            const float mn = fmaxf(mo, bm);
+            const float pv = t < ntok ? exp2f(sv - mn) : 0.0f;
+            float ps = pv;
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) ps += __shfl_xor_sync(hmask, ps, off);
+            if (t == 0) {
+                const float corr = first ? 0.0f : exp2f(mo - mn);
+                sL[h] = (first ? 0.0f : sL[h] * corr) + ps;
+                sM[h] = mn;
+                sCorr[h] = corr;
+            }
+            sP[idx] = pv;
+        }
+        named_sync(1, ncons);
+
+        // ---- phase C: acc = acc * corr + sum_t p_t v_t
+        if (active) {
+            if (!first) {
+#pragma unroll
+                for (int g = 0; g < QG; ++g) {
+                    const float cr = sCorr[hk * QG + g];
+#pragma unroll
+                    for (int e = 0; e < E; ++e) acc[g][e] *= cr;
+                }
+            }
+            const unsigned char* V = stage + p.slab_bytes;
+            for (int t = ts; t < ntok; t += ks) {
+                float vf[E];
+                unpack16<T>(ld_shared16(V + (t * C + c) * 16), vf);
+#pragma unroll
+                for (int g = 0; g < QG; ++g) {
+                    const float pw = sP[(hk * QG + g) * kBlockTokens + t];
+#pragma unroll
+                    for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pw, vf[e], acc[g][e]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+
+        if (!last) continue;
+
+        // ---- segment end: combine token subgroups, then write or merge
+        const int nseg = meta.z;
+        const int i0 = meta.w;
+        const bool single = nseg == 1;
+        const int slot = cta + b;
+        if (ks > 1) {
+            if (active) {
+#pragma unroll
+                for (int g = 0; g < QG; ++g) {
+                    float* dst = sScratch + (static_cast<size_t>(ts) * H + hk * QG + g) * DH + dg * E;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) dst[e] = acc[g][e];
+                }
+            }
+            named_sync(1, ncons);
+            for (int idx = tid; idx < H * GL; idx += ncons) {
+                const int h = idx / GL;
+                const int dc = idx - h * GL;
+                float a[E];
+#pragma unroll
+                for (int e = 0; e < E; ++e) a[e] = 0.0f;
+                for (int s2 = 0; s2 < ks; ++s2) {
+                    const float* src = sScratch + (static_cast<size_t>(s2) * H + h) * DH + dc * E;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) a[e] += src[e];
+                }
+                if (single) {
+                    const float l = sL[h];
+                    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) a[e] *= inv;
+                    store_row<OutT, E>(out + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
+                } else {
+                    float* dst = p.part_acc + (static_cast<size_t>(slot) * H + h) * DH + dc * E;
+#pragma unroll
+                    for (int e = 0; e < E; e += 4)
+                        __stcg(reinterpret_cast<float4*>(dst + e), make_float4(a[e], a[e + 1], a[e + 2], a[e + 3]));
+                }
+            }
+        } else if (active) {
+#pragma unroll
+            for (int g = 0; g < QG; ++g) {
+                const int h = hk * QG + g;
+                if (single) {
+                    const float l = sL[h];
+                    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+                    float a[E];
+#pragma unroll
+                    for (int e = 0; e < E; ++e) a[e] = acc[g][e] * inv;
+                    store_row<OutT, E>(out + (static_cast<size_t>(b) * H + h) * DH + dg * E, a);
+                } else {
+                    float* dst = p.part_acc + (static_cast<size_t>(slot) * H + h) * DH + dg * E;
+#pragma unroll
+                    for (int e = 0; e < E; e += 4)
+                        __stcg(reinterpret_cast<float4*>(dst + e),
+                               make_float4(acc[g][e], acc[g][e + 1], acc[g][e + 2], acc[g][e + 3]));
+                }
+            }
+        }
+        if (single) continue;
+
+        for (int h = tid; h < H; h += ncons) __stcg(p.part_ml + static_cast<size_t>(slot) * H + h, make_float2(sM[h], sL[h]));
+        __threadfence();
+        named_sync(1, ncons);
+        if (tid == 0) {
+            const unsigned int prev = atomicAdd(p.counters + b, 1u);
+            misc[40] = (prev == static_cast<unsigned int>(nseg - 1)) ? 1 : 0;
+        }
+        named_sync(1, ncons);
+        if (misc[40]) {
+            __threadfence();
+            for (int idx = tid; idx < H * GL; idx += ncons) {
+                const int h = idx / GL;
+                const int dc = idx - h * GL;
+                float mmax = -INFINITY;
+                for (int s2 = 0; s2 < nseg; ++s2)
+                    mmax = fmaxf(mmax, __ldcg(p.part_ml + static_cast<size_t>(i0 + s2 + b) * H + h).x);
+                float l = 0.0f;
+                float a[E];
+#pragma unroll
+                for (int e = 0; e < E; ++e) a[e] = 0.0f;
+                for (int s2 = 0; s2 < nseg; ++s2) {
+                    const size_t sl = static_cast<size_t>(i0 + s2 + b);
+                    const float2 ml = __ldcg(p.part_ml + sl * H + h);
+                    const float w = exp2f(ml.x - mmax);
+                    l = fmaf(ml.y, w, l);
+                    const float* src = p.part_acc + (sl * H + h) * DH + dc * E;
+#pragma unroll
+                    for (int e = 0; e < E; e += 4) {
+                        const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + e));
+                        a[e] = fmaf(v4.x, w, a[e]);
+                        a[e + 1] = fmaf(v4.y, w, a[e + 1]);
+                        a[e + 2] = fmaf(v4.z, w, a[e + 2]);
+                        a[e + 3] = fmaf(v4.w, w, a[e + 3]);
+                    }
+                }
+                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+                for (int e = 0; e < E; ++e) a[e] *= inv;
+                store_row<OutT, E>(out + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
+            }
+            if (tid == 0) p.counters[b] = 0u;
+        }
+    }
+}
+
+}  // namespace b2

@@ -1,0 +1,210 @@
+// b2_common.cuh -- dtype traits, 16-byte vector conversion and the sm_100a
+// PTX primitives (mbarrier, bulk async copy, named barriers, bounded waits)
+// shared by the decode kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b2_decode.h"
+
+namespace b2 {
+
+constexpr int kBlockTokens = B2_BLOCK_TOKENS;
+
+// Per-device error word (see B2_DEVERR_*).  Kernels OR bits into it; the host
+// reads and clears it with b2_device_errors().  Defined here: the library is
+// one translation unit (b2_decode.cu), so this header is included once.
+__device__ unsigned int g_device_errors = 0;
+
+__device__ __forceinline__ void flag_error(unsigned int bits) { atomicOr(&g_device_errors, bits); }
+
+// ------------------------------------------------------------- dtype traits
+
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+    static constexpr int kPer16B = 4;
+    __device__ __forceinline__ static float to_f(float x) { return x; }
+    __device__ __forceinline__ static float from_f(float x) { return x; }
+};
+template <>
+struct Elem<__half> {
+    static constexpr int kPer16B = 8;
+    __device__ __forceinline__ static float to_f(__half x) { return __half2float(x); }
+    __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
+};
+template <>
+struct Elem<__nv_bfloat16> {
+    static constexpr int kPer16B = 8;
+    __device__ __forceinline__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+    __device__ __forceinline__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+
+// Widen one 16-byte vector of T into kPer16B floats.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& raw, float* f);
+
+template <>
+__device__ __forceinline__ void unpack16<float>(const uint4& raw, float* f) {
+    f[0] = __uint_as_float(raw.x);
+    f[1] = __uint_as_float(raw.y);
+    f[2] = __uint_as_float(raw.z);
+    f[3] = __uint_as_float(raw.w);
+}
+template <>
+__device__ __forceinline__ void unpack16<__half>(const uint4& raw, float* f) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __half2 h2 = *reinterpret_cast<const __half2*>(&w[i]);
+        float2 v = __half22float2(h2);
+        f[2 * i] = v.x;
+        f[2 * i + 1] = v.y;
+    }
+}
+template <>
+__device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& raw, float* f) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        // bf16 -> f32 is a 16-bit shift.
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+
+// Round kPer16B floats to T and pack them into one 16-byte vector.
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const float* f);
+
+template <>
+__device__ __forceinline__ uint4 pack16<float>(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+}
+template <>
+__device__ __forceinline__ uint4 pack16<__half>(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __half2 h2 = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <>
+__device__ __forceinline__ uint4 pack16<__nv_bfloat16>(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Store n (= kPer16B of the source type, 4 or 8) floats as OutT at dst,
+// which is 16-byte aligned.
+template <typename OutT, int N>
+__device__ __forceinline__ void store_row(OutT* dst, const float* f) {
+    constexpr int P = Elem<OutT>::kPer16B;
+    static_assert(N % P == 0, "store width");
+#pragma unroll
+    for (int i = 0; i < N / P; ++i) *reinterpret_cast<uint4*>(dst + i * P) = pack16<OutT>(f + i * P);
+}
+
+// ------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wall-clock bound on every pipeline wait: past it the wait reports failure
+// and the caller flags B2_DEVERR_TIMEOUT and winds down instead of spinning.
+constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+
+// Waits for the phase with the given parity to complete.  Returns false if
+// the wall-clock limit passed first.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+// One-dimensional bulk async copy global -> shared, completing on an mbarrier
+// (the TMA engine's untiled form; no tensor map, no multicast).  dst, src and
+// bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Named barrier over the first nthreads threads of the CTA (multiple of 32).
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also ORs a predicate over the participants.
+__device__ __forceinline__ bool named_sync_or(int id, int nthreads, bool pred) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred pin, pout;\n\t"
+        "setp.ne.u32 pin, %1, 0;\n\t"
+        "bar.red.or.pred pout, %2, %3, pin;\n\t"
+        "selp.u32 %0, 1, 0, pout;\n\t}"
+        : "=r"(out)
+        : "r"(pred ? 1u : 0u), "r"(id), "r"(nthreads)
+        : "memory");
+    return out != 0;
+}
+
+__device__ __forceinline__ uint4 ld_shared16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+}  // namespace b2

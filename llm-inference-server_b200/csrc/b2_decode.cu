@@ -1,0 +1,526 @@
+// b2_decode.cu -- extern "C" entry points of libb2decode.so (include/b2_decode.h).
+//
+// Host side of the kernel-launch layer: argument checks (returned as status
+// codes before anything is launched), the attention launch plan (stages,
+// token subgroups, grid = one CTA per SM), and dtype / head_dim dispatch.
+// Nothing here allocates device memory or synchronises, except
+// b2_device_errors, which reads the device error word.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "append.cuh"
+#include "attention.cuh"
+#include "b2_common.cuh"
+#include "rows.cuh"
+
+namespace b2 {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* what) {
+    g_last_error = what;
+    return code;
+}
+
+int launch_status() {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        g_last_error = cudaGetErrorString(e);
+        return static_cast<int>(e);
+    }
+    return B2_OK;
+}
+
+int dtype_size(int dt) { return dt == B2_F32 ? 4 : 2; }
+bool dtype_ok(int dt) { return dt == B2_F32 || dt == B2_F16 || dt == B2_BF16; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct DeviceInfo {
+    int sms = 0;
+    int max_smem_optin = 0;
+};
+
+DeviceInfo device_info(int* dev_out) {
+    static DeviceInfo cache[64];
+    static std::once_flag once[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        *dev_out = -1;
+        return DeviceInfo{};
+    }
+    *dev_out = dev;
+    std::call_once(once[dev], [dev]() {
+        DeviceInfo d;
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cache[dev] = d;
+    });
+    return cache[dev];
+}
+
+// cudaFuncSetAttribute once per (kernel, device).
+template <typename K>
+void ensure_max_smem(K kernel, int dev, int bytes) {
+    static std::atomic<uint64_t> done{0};
+    const uint64_t bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done.fetch_or(bit, std::memory_order_acq_rel);
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Threads per attention CTA at most (consumers + the producer warp); keeps
+// the register cap at 128 per thread.
+constexpr int kAttnMaxThreads = 512;
+
+// ---------------------------------------------------------- attention plan
+
+struct AttnPlan {
+    int grid = 0, threads = 0, smem = 0;
+    AttnParams prm{};
+    size_t ws_counters = 0, ws_ml = 0, ws_acc = 0, ws_total = 0;
+};
+
+int check_attn_args(const B2PagedAttnArgs* a) {
+    if (a == nullptr) return fail(B2_ERR_NULL, "args is NULL");
+    if (!dtype_ok(a->dtype)) return fail(B2_ERR_DTYPE, "unknown dtype");
+    if (a->out_dtype != B2_F32 && a->out_dtype != a->dtype)
+        return fail(B2_ERR_DTYPE, "out_dtype must be F32 or equal to dtype");
+    if (a->batch < 0) return fail(B2_ERR_SHAPE, "batch < 0");
+    if (a->batch == 0) return B2_OK;
+    if (!a->q || !a->kv_pool || !a->block_tables || !a->seq_lens || !a->out)
+        return fail(B2_ERR_NULL, "q, kv_pool, block_tables, seq_lens and out are required");
+    if (a->head_dim != 64 && a->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+    if (a->n_kv_head <= 0 || a->n_head <= 0 || a->n_head % a->n_kv_head != 0)
+        return fail(B2_ERR_SHAPE, "n_head must be a positive multiple of n_kv_head");
+    const int qg = a->n_head / a->n_kv_head;
+    const int es = dtype_size(a->dtype);
+    if (!(qg == 1 || qg == 2 || qg == 4 || (qg == 8 && es == 4)))
+        return fail(B2_ERR_UNSUPPORTED, "query-group size must be 1, 2 or 4 (8 for f32)");
+    if (a->max_blocks_per_seq <= 0 || a->n_layer <= 0 || a->layer_idx < 0 || a->layer_idx >= a->n_layer ||
+        a->num_blocks <= 0)
+        return fail(B2_ERR_SHAPE, "max_blocks_per_seq, n_layer, layer_idx or num_blocks out of range");
+    if (a->max_blocks_per_seq > (1 << 26) / B2_BLOCK_TOKENS) return fail(B2_ERR_SHAPE, "max_blocks_per_seq too large");
+    if (a->q_row_stride < a->n_head * a->head_dim) return fail(B2_ERR_SHAPE, "q_row_stride < n_head*head_dim");
+    if (!aligned16(a->q) || !aligned16(a->kv_pool) || !aligned16(a->out) || (a->q_bias && !aligned16(a->q_bias)) ||
+        (static_cast<long long>(a->q_row_stride) * es) % 16 != 0)
+        return fail(B2_ERR_ALIGN, "q, q_bias, kv_pool and out must be 16-byte aligned, q_row_stride*elem 16-byte multiple");
+    return B2_OK;
+}
+
+int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
+    int dev = -1;
+    const DeviceInfo di = device_info(&dev);
+    if (dev < 0 || di.sms <= 0) return fail(B2_ERR_DEVICE, "no current CUDA device");
+    const int es = dtype_size(a->dtype);
+    const int E = 16 / es;
+    const int GL = a->head_dim / E;
+    const int C = a->n_kv_head * GL;
+    const int H = a->n_head;
+    const int maxt = kAttnMaxThreads;
+    const int slab = B2_BLOCK_TOKENS * a->n_kv_head * a->head_dim * es;
+    const int qbytes = H * a->head_dim * es;
+    const int off_meta = 2 * slab + qbytes;
+    const int stage = static_cast<int>(align_up(off_meta + 16, 128));
+    const int smem_cap = di.max_smem_optin;
+
+    int best_k = 0, best_s = 0, best_fixed = 0;
+    for (int k : {4, 2, 1}) {
+        const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * C, 32));
+        if (ncons + 32 > maxt) continue;
+        if (k > 1 && k * C > 512) continue;  // enough warps; keep smem for stages
+        const int scratch = k > 1 ? k * H * a->head_dim * 4 : 0;
+        const int fixed = 2 * H * B2_BLOCK_TOKENS * 4 + 3 * H * 4 + 256 + scratch;
+        int s = (smem_cap - fixed - 512) / stage;  // 512: barriers + alignment padding
+        if (s > 8) s = 8;
+        if (s < 2) continue;
+        best_k = k;
+        best_s = s;
+        best_fixed = fixed;
+        break;
+    }
+    if (best_k == 0) return fail(B2_ERR_UNSUPPORTED, "head shape does not fit the decode kernel's shared memory");
+    if (a->batch > 16 * (static_cast<int>(align_up(static_cast<size_t>(best_k) * C, 32)) + 32))
+        return fail(B2_ERR_UNSUPPORTED, "batch too large for one launch");
+
+    AttnParams& p = pl->prm;
+    p.ksplit = best_k;
+    p.ncons = static_cast<int>(align_up(static_cast<size_t>(best_k) * C, 32));
+    p.stages = best_s;
+    p.stage_bytes = stage;
+    p.slab_bytes = slab;
+    p.q_bytes = qbytes;
+    p.off_meta = off_meta;
+    int off = best_s * stage;
+    p.off_scores = off;
+    off += H * B2_BLOCK_TOKENS * 4;
+    p.off_probs = off;
+    off += H * B2_BLOCK_TOKENS * 4;
+    p.off_m = off;
+    off += H * 4;
+    p.off_l = off;
+    off += H * 4;
+    p.off_corr = off;
+    off += H * 4;
+    off = static_cast<int>(align_up(off, 16));
+    p.off_scratch = off;
+    off += best_fixed - (2 * H * B2_BLOCK_TOKENS * 4 + 3 * H * 4 + 256);
+    off = static_cast<int>(align_up(off, 16));
+    p.off_misc = off;
+    off += 256;
+    p.off_bars = off;
+    off += 2 * best_s * 8;
+    pl->smem = off;
+    pl->threads = p.ncons + 32;
+    pl->grid = di.sms;
+
+    const size_t slots = static_cast<size_t>(pl->grid) + a->batch;
+    pl->ws_counters = align_up(static_cast<size_t>(a->batch) * 4, 256);
+    pl->ws_ml = align_up(slots * H * sizeof(float2), 256);
+    pl->ws_acc = align_up(slots * H * a->head_dim * sizeof(float), 256);
+    pl->ws_total = pl->ws_counters + pl->ws_ml + pl->ws_acc;
+    return B2_OK;
+}
+
+template <typename T, int DH, int QG, typename OutT>
+int launch_attn_t(const AttnPlan& pl, cudaStream_t stream) {
+    constexpr int MAXT = kAttnMaxThreads;
+    auto kern = paged_decode_kernel<T, DH, QG, OutT, MAXT>;
+    int dev = -1;
+    const DeviceInfo di = device_info(&dev);
+    ensure_max_smem(kern, dev, di.max_smem_optin);
+    kern<<<pl.grid, pl.threads, pl.smem, stream>>>(pl.prm);
+    return launch_status();
+}
+
+template <typename T, typename OutT>
+int launch_attn_dh(const AttnPlan& pl, int dh, int qg, cudaStream_t s) {
+    if (dh == 64) {
+        switch (qg) {
+            case 1: return launch_attn_t<T, 64, 1, OutT>(pl, s);
+            case 2: return launch_attn_t<T, 64, 2, OutT>(pl, s);
+            case 4: return launch_attn_t<T, 64, 4, OutT>(pl, s);
+            case 8:
+                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 64, 8, OutT>(pl, s);
+                break;
+        }
+    } else {
+        switch (qg) {
+            case 1: return launch_attn_t<T, 128, 1, OutT>(pl, s);
+            case 2: return launch_attn_t<T, 128, 2, OutT>(pl, s);
+            case 4: return launch_attn_t<T, 128, 4, OutT>(pl, s);
+            case 8:
+                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 128, 8, OutT>(pl, s);
+                break;
+        }
+    }
+    return fail(B2_ERR_UNSUPPORTED, "no kernel for this head shape");
+}
+
+template <typename T>
+int launch_attn_out(const AttnPlan& pl, int out_f32, int dh, int qg, cudaStream_t s) {
+    if (out_f32) return launch_attn_dh<T, float>(pl, dh, qg, s);
+    return launch_attn_dh<T, T>(pl, dh, qg, s);
+}
+
+// Row-kernel grid: grid-stride loops over 16-byte chunks, a few waves of CTAs.
+int row_grid(long long nchunks) {
+    long long g = (nchunks + 255) / 256;
+    if (g > 148LL * 16) g = 148LL * 16;
+    return static_cast<int>(g < 1 ? 1 : g);
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+const char* b2_version(void) { return "b2decode 0.1 (sm_100a)"; }
+
+const char* b2_last_error_string(void) { return g_last_error.c_str(); }
+
+int b2_device_errors(uint32_t* bits_out) {
+    if (bits_out == nullptr) return fail(B2_ERR_NULL, "bits_out is NULL");
+    unsigned int v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_errors, sizeof(v));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_errors, &zero, sizeof(zero));
+    if (e != cudaSuccess) {
+        g_last_error = cudaGetErrorString(e);
+        return static_cast<int>(e);
+    }
+    *bits_out = v;
+    return B2_OK;
+}
+
+// ------------------------------------------------------------- kv append
+
+int b2_kv_append(const B2KvAppendArgs* a, b2_stream_t stream) {
+    if (a == nullptr) return fail(B2_ERR_NULL, "args is NULL");
+    if (!dtype_ok(a->dtype)) return fail(B2_ERR_DTYPE, "unknown dtype");
+    if (a->batch < 0) return fail(B2_ERR_SHAPE, "batch < 0");
+    if (a->batch == 0) return B2_OK;
+    if (!a->kv_pool || !a->k || !a->v || !a->block_tables || !a->seq_lens)
+        return fail(B2_ERR_NULL, "kv_pool, k, v, block_tables and seq_lens are required");
+    if (a->head_dim != 64 && a->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+    if (a->n_kv_head <= 0 || a->max_blocks_per_seq <= 0 || a->n_layer <= 0 || a->layer_idx < 0 ||
+        a->layer_idx >= a->n_layer || a->num_blocks <= 0)
+        return fail(B2_ERR_SHAPE, "n_kv_head, max_blocks_per_seq, n_layer, layer_idx or num_blocks out of range");
+    if (a->kv_row_stride < a->n_kv_head * a->head_dim) return fail(B2_ERR_SHAPE, "kv_row_stride < n_kv_head*head_dim");
+    if (a->seq_lens_post != nullptr && a->seq_lens_post == a->seq_lens)
+        return fail(B2_ERR_SHAPE, "seq_lens_post must not alias seq_lens");
+    const int es = dtype_size(a->dtype);
+    if (!aligned16(a->kv_pool) || !aligned16(a->k) || !aligned16(a->v) || (a->k_bias && !aligned16(a->k_bias)) ||
+        (a->v_bias && !aligned16(a->v_bias)) || (static_cast<long long>(a->kv_row_stride) * es) % 16 != 0)
+        return fail(B2_ERR_ALIGN, "pointers must be 16-byte aligned, kv_row_stride*elem a 16-byte multiple");
+    AppendParams p;
+    p.pool = a->kv_pool;
+    p.k = a->k;
+    p.v = a->v;
+    p.kv_row_stride = a->kv_row_stride;
+    p.k_bias = a->k_bias;
+    p.v_bias = a->v_bias;
+    p.block_tables = a->block_tables;
+    p.seq_lens = a->seq_lens;
+    p.seq_lens_post = a->seq_lens_post;
+    p.batch = a->batch;
+    p.n_kv_head = a->n_kv_head;
+    p.mbps = a->max_blocks_per_seq;
+    p.layer_idx = a->layer_idx;
+    p.n_layer = a->n_layer;
+    p.num_blocks = a->num_blocks;
+    const int E = 16 / es;
+    const long long total = static_cast<long long>(a->batch) * 2 * a->n_kv_head * (a->head_dim / E);
+    const int grid = static_cast<int>((total + 255) / 256);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (a->dtype == B2_F32) {
+        if (a->head_dim == 64) kv_append_kernel<float, 64><<<grid, 256, 0, s>>>(p);
+        else kv_append_kernel<float, 128><<<grid, 256, 0, s>>>(p);
+    } else if (a->dtype == B2_F16) {
+        if (a->head_dim == 64) kv_append_kernel<__half, 64><<<grid, 256, 0, s>>>(p);
+        else kv_append_kernel<__half, 128><<<grid, 256, 0, s>>>(p);
+    } else {
+        if (a->head_dim == 64) kv_append_kernel<__nv_bfloat16, 64><<<grid, 256, 0, s>>>(p);
+        else kv_append_kernel<__nv_bfloat16, 128><<<grid, 256, 0, s>>>(p);
+    }
+    return launch_status();
+}
+
+// ------------------------------------------------------- paged attention
+
+size_t b2_paged_attention_workspace_bytes(const B2PagedAttnArgs* a) {
+    if (check_attn_args(a) != B2_OK || a->batch == 0) return 0;
+    AttnPlan pl;
+    if (plan_attention(a, &pl) != B2_OK) return 0;
+    return pl.ws_total;
+}
+
+int b2_paged_attention_workspace_init(void* ws, size_t ws_bytes, const B2PagedAttnArgs* a, b2_stream_t stream) {
+    int rc = check_attn_args(a);
+    if (rc != B2_OK) return rc;
+    if (a->batch == 0) return B2_OK;
+    AttnPlan pl;
+    rc = plan_attention(a, &pl);
+    if (rc != B2_OK) return rc;
+    if (ws == nullptr || ws_bytes < pl.ws_total) return fail(B2_ERR_WORKSPACE, "workspace missing or too small");
+    const cudaError_t e = cudaMemsetAsync(ws, 0, pl.ws_counters, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        g_last_error = cudaGetErrorString(e);
+        return static_cast<int>(e);
+    }
+    return B2_OK;
+}
+
+int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_stream_t stream) {
+    int rc = check_attn_args(a);
+    if (rc != B2_OK) return rc;
+    if (a->batch == 0) return B2_OK;
+    AttnPlan pl;
+    rc = plan_attention(a, &pl);
+    if (rc != B2_OK) return rc;
+    if (ws == nullptr || ws_bytes < pl.ws_total || !aligned16(ws))
+        return fail(B2_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+    AttnParams& p = pl.prm;
+    p.q = a->q;
+    p.q_row_stride = a->q_row_stride;
+    p.q_bias = a->q_bias;
+    p.pool = a->kv_pool;
+    p.block_tables = a->block_tables;
+    p.seq_lens = a->seq_lens;
+    p.out = a->out;
+    p.batch = a->batch;
+    p.n_head = a->n_head;
+    p.n_kv_head = a->n_kv_head;
+    p.mbps = a->max_blocks_per_seq;
+    p.layer_idx = a->layer_idx;
+    p.n_layer = a->n_layer;
+    p.num_blocks = a->num_blocks;
+    const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
+    p.scale_log2 = scale * 1.4426950408889634f;
+    char* base = static_cast<char*>(ws);
+    p.counters = reinterpret_cast<unsigned int*>(base);
+    p.part_ml = reinterpret_cast<float2*>(base + pl.ws_counters);
+    p.part_acc = reinterpret_cast<float*>(base + pl.ws_counters + pl.ws_ml);
+    const int qg = a->n_head / a->n_kv_head;
+    const int out_f32 = a->out_dtype == B2_F32 && a->dtype != B2_F32;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (a->dtype == B2_F32) return launch_attn_dh<float, float>(pl, a->head_dim, qg, s);
+    if (a->dtype == B2_F16) return launch_attn_out<__half>(pl, out_f32, a->head_dim, qg, s);
+    return launch_attn_out<__nv_bfloat16>(pl, out_f32, a->head_dim, qg, s);
+}
+
+// ------------------------------------------------------------ row kernels
+
+int b2_add_layernorm(int32_t dtype, void* out, void* residual_out, const void* x, const void* bias,
+                     const void* residual_in, const void* gamma, const void* beta, int32_t batch, int32_t d_model,
+                     float eps, b2_stream_t stream) {
+    if (!dtype_ok(dtype)) return fail(B2_ERR_DTYPE, "unknown dtype");
+    if (batch < 0 || d_model <= 0) return fail(B2_ERR_SHAPE, "batch < 0 or d_model <= 0");
+    if (batch == 0) return B2_OK;
+    if (!out || !residual_in || !gamma || !beta) return fail(B2_ERR_NULL, "out, residual_in, gamma, beta required");
+    const int E = 16 / dtype_size(dtype);
+    if (d_model % E != 0) return fail(B2_ERR_SHAPE, "d_model*elem must be a multiple of 16 bytes");
+    if (!aligned16(out) || !aligned16(residual_in) || !aligned16(gamma) || !aligned16(beta) ||
+        (x && !aligned16(x)) || (bias && !aligned16(bias)) || (residual_out && !aligned16(residual_out)))
+        return fail(B2_ERR_ALIGN, "pointers must be 16-byte aligned");
+    const int per_lane = (d_model / E + 31) / 32;
+    if (per_lane > 16) return fail(B2_ERR_UNSUPPORTED, "d_model too large for the one-warp-per-row kernel");
+    const int grid = (batch + 3) / 4;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define B2_LN_LAUNCH(T, N)                                                                                     \
+    add_layernorm_kernel<T, N><<<grid, 128, 0, s>>>(static_cast<T*>(out), static_cast<T*>(residual_out),      \
+                                                    static_cast<const T*>(x), static_cast<const T*>(bias),       \
+                                                    static_cast<const T*>(residual_in), static_cast<const T*>(gamma), \
+                                                    static_cast<const T*>(beta), batch, d_model, eps)
+#define B2_LN_DISPATCH(T)              \
+    if (per_lane <= 2) B2_LN_LAUNCH(T, 2);      \
+    else if (per_lane <= 4) B2_LN_LAUNCH(T, 4); \
+    else if (per_lane <= 8) B2_LN_LAUNCH(T, 8); \
+    else B2_LN_LAUNCH(T, 16);
+    if (dtype == B2_F32) {
+        B2_LN_DISPATCH(float)
+    } else if (dtype == B2_F16) {
+        B2_LN_DISPATCH(__half)
+    } else {
+        B2_LN_DISPATCH(__nv_bfloat16)
+    }
+#undef B2_LN_DISPATCH
+#undef B2_LN_LAUNCH
+    return launch_status();
+}
+
+static int check_rowwise(int32_t dtype, const void* out, const void* x, const void* bias, int32_t batch, int32_t dim) {
+    if (!dtype_ok(dtype)) return fail(B2_ERR_DTYPE, "unknown dtype");
+    if (batch < 0 || dim <= 0) return fail(B2_ERR_SHAPE, "batch < 0 or dim <= 0");
+    if (batch > 0 && (!out || !x || !bias)) return fail(B2_ERR_NULL, "out, x and bias are required");
+    if (dim % (16 / dtype_size(dtype)) != 0) return fail(B2_ERR_SHAPE, "dim*elem must be a multiple of 16 bytes");
+    if (!aligned16(out) || !aligned16(x) || !aligned16(bias)) return fail(B2_ERR_ALIGN, "pointers must be 16-byte aligned");
+    return B2_OK;
+}
+
+int b2_bias_gelu(int32_t dtype, void* out, const void* x, const void* bias, int32_t batch, int32_t d_ff,
+                 b2_stream_t stream) {
+    int rc = check_rowwise(dtype, out, x, bias, batch, d_ff);
+    if (rc != B2_OK || batch == 0) return rc;
+    const int rc_chunks = d_ff / (16 / dtype_size(dtype));
+    const long long n = static_cast<long long>(batch) * rc_chunks;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int g = row_grid(n);
+    if (dtype == B2_F32)
+        bias_gelu_kernel<float><<<g, 256, 0, s>>>(static_cast<float*>(out), static_cast<const float*>(x),
+                                                  static_cast<const float*>(bias), n, rc_chunks);
+    else if (dtype == B2_F16)
+        bias_gelu_kernel<__half><<<g, 256, 0, s>>>(static_cast<__half*>(out), static_cast<const __half*>(x),
+                                                   static_cast<const __half*>(bias), n, rc_chunks);
+    else
+        bias_gelu_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out),
+                                                          static_cast<const __nv_bfloat16*>(x),
+                                                          static_cast<const __nv_bfloat16*>(bias), n, rc_chunks);
+    return launch_status();
+}
+
+int b2_add_bias(int32_t dtype, void* out, const void* x, const void* bias, int32_t batch, int32_t dim,
+                b2_stream_t stream) {
+    int rc = check_rowwise(dtype, out, x, bias, batch, dim);
+    if (rc != B2_OK || batch == 0) return rc;
+    const int rc_chunks = dim / (16 / dtype_size(dtype));
+    const long long n = static_cast<long long>(batch) * rc_chunks;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int g = row_grid(n);
+    if (dtype == B2_F32)
+        add_bias_kernel<float><<<g, 256, 0, s>>>(static_cast<float*>(out), static_cast<const float*>(x),
+                                                 static_cast<const float*>(bias), n, rc_chunks);
+    else if (dtype == B2_F16)
+        add_bias_kernel<__half><<<g, 256, 0, s>>>(static_cast<__half*>(out), static_cast<const __half*>(x),
+                                                  static_cast<const __half*>(bias), n, rc_chunks);
+    else
+        add_bias_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out),
+                                                         static_cast<const __nv_bfloat16*>(x),
+                                                         static_cast<const __nv_bfloat16*>(bias), n, rc_chunks);
+    return launch_status();
+}
+
+int b2_add_one(int32_t* out, const int32_t* in, int32_t batch, b2_stream_t stream) {
+    if (batch < 0) return fail(B2_ERR_SHAPE, "batch < 0");
+    if (batch == 0) return B2_OK;
+    if (!out || !in) return fail(B2_ERR_NULL, "out and in are required");
+    add_one_kernel<<<(batch + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(out, in, batch);
+    return launch_status();
+}
+
+int b2_embedding(int32_t dtype, void* out, const void* wte, const void* wpe, const int32_t* token_ids,
+                 const int32_t* positions, int32_t batch, int32_t d_model, int32_t vocab, int32_t n_pos,
+                 b2_stream_t stream) {
+    if (!dtype_ok(dtype)) return fail(B2_ERR_DTYPE, "unknown dtype");
+    if (batch < 0 || d_model <= 0 || vocab <= 0 || n_pos <= 0) return fail(B2_ERR_SHAPE, "bad sizes");
+    if (batch == 0) return B2_OK;
+    if (!out || !wte || !wpe || !token_ids || !positions) return fail(B2_ERR_NULL, "all pointers are required");
+    const int E = 16 / dtype_size(dtype);
+    if (d_model % E != 0) return fail(B2_ERR_SHAPE, "d_model*elem must be a multiple of 16 bytes");
+    if (!aligned16(out) || !aligned16(wte) || !aligned16(wpe)) return fail(B2_ERR_ALIGN, "pointers must be 16-byte aligned");
+    const int rcn = d_model / E;
+    const int g = row_grid(static_cast<long long>(batch) * rcn);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == B2_F32)
+        embedding_kernel<float><<<g, 256, 0, s>>>(static_cast<float*>(out), static_cast<const float*>(wte),
+                                                  static_cast<const float*>(wpe), token_ids, positions, batch, rcn,
+                                                  vocab, n_pos);
+    else if (dtype == B2_F16)
+        embedding_kernel<__half><<<g, 256, 0, s>>>(static_cast<__half*>(out), static_cast<const __half*>(wte),
+                                                   static_cast<const __half*>(wpe), token_ids, positions, batch, rcn,
+                                                   vocab, n_pos);
+    else
+        embedding_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out),
+                                                          static_cast<const __nv_bfloat16*>(wte),
+                                                          static_cast<const __nv_bfloat16*>(wpe), token_ids,
+                                                          positions, batch, rcn, vocab, n_pos);
+    return launch_status();
+}
+
+int b2_argmax(int32_t dtype, int32_t* out_tokens, const void* logits, int32_t batch, int32_t vocab,
+              b2_stream_t stream) {
+    if (!dtype_ok(dtype)) return fail(B2_ERR_DTYPE, "unknown dtype");
+    if (batch < 0 || vocab <= 0) return fail(B2_ERR_SHAPE, "bad sizes");
+    if (batch == 0) return B2_OK;
+    if (!out_tokens || !logits) return fail(B2_ERR_NULL, "out_tokens and logits are required");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == B2_F32)
+        argmax_kernel<float><<<batch, 256, 0, s>>>(out_tokens, static_cast<const float*>(logits), vocab);
+    else if (dtype == B2_F16)
+        argmax_kernel<__half><<<batch, 256, 0, s>>>(out_tokens, static_cast<const __half*>(logits), vocab);
+    else
+        argmax_kernel<__nv_bfloat16><<<batch, 256, 0, s>>>(out_tokens, static_cast<const __nv_bfloat16*>(logits),
+                                                           vocab);
+    return launch_status();
+}
+
+}  // extern "C"
