@@ -238,11 +238,11 @@ def host_workload(seed: int):
     return pool, bt, ctx, q
 
 
-def b2_workload(b2, device, seed: int, n_sets: int):
+def b2_workload(b2, device, seed: int, n_sets: int, pool_blocks: int = 65536):
     import torch
     from lis_b200.workloads import make_attention_workload
     return make_attention_workload(device, seed=seed, n_sets=n_sets, batch=BATCH, n_head=N_HEAD, n_kv_head=N_HEAD,
-                                   head_dim=HEAD_DIM, dtype=torch.float16)
+                                   head_dim=HEAD_DIM, dtype=torch.float16, pool_blocks=pool_blocks)
 
 
 def run_ours(args, rank: int, world: int, dist) -> None:
@@ -251,7 +251,7 @@ def run_ours(args, rank: int, world: int, dist) -> None:
     b2.load()
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
-    wl = b2_workload(b2, dev, seed=1000 + rank, n_sets=N_SETS)
+    wl = b2_workload(b2, dev, seed=1000 + rank, n_sets=args.sets, pool_blocks=args.pool_blocks)
     stream = torch.cuda.current_stream(dev)
     wl.workspace = b2.attention_workspace(wl.sets[0].args)
     ws = wl.workspace
@@ -388,6 +388,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--sets", type=int, default=N_SETS, help="rotating input sets (profiling uses fewer)")
+    ap.add_argument("--pool-blocks", type=int, default=65536, help="KV pool size in blocks (profiling uses fewer)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

@@ -6,10 +6,10 @@
 //
 //  * Work split.  Every sequence b owns nb_b = ceil(seq_len_b / 16) paged
 //    blocks.  All blocks of all sequences form one list of N units, and CTA i
-//    of the G resident CTAs (one per SM) takes units [i*N/G, (i+1)*N/G).  The
-//    split is therefore even whatever the length skew, and a sequence may be
-//    cut into segments handled by several CTAs (flash-decoding split-K with
-//    the split points chosen by load, not by a fixed chunk size).
+//    of the G = min(grid, N) working CTAs (one per SM) takes units
+//    [i*N/G, (i+1)*N/G).  The split is even whatever the length skew, and a
+//    sequence may be cut into segments handled by several CTAs
+//    (flash-decoding split-K with split points chosen by load).
 //  * Data movement.  For one layer, a block's K rows of ALL kv heads are one
 //    contiguous slab of 16*n_kv_head*head_dim elements (layout
 //    [block][layer][K|V][16][n_kv_head][head_dim], kv_cache.h:6-7), with the V
@@ -17,13 +17,15 @@
 //    (only the valid token rows) with 1-D bulk async copies (cp.async.bulk,
 //    the TMA engine's untiled path) into a ring of shared-memory stages
 //    guarded by mbarriers; q rows travel the same way at a segment's first
-//    block.  Consumer warps never touch global memory for K/V.
+//    block.  Consumer warps never read K/V from global memory.
 //  * Math.  Consumer thread (ts, c) owns 16-byte chunk c of the token row
 //    (kv head c / GL, dims (c % GL) * E ...) and the tokens t = ts (mod k) of
-//    each block.  QK^T: 16-byte shared loads, fp32 FMAs, a GL-lane xor-shuffle
-//    reduction.  Softmax: one (head, token) pair per lane, 16-lane max/sum
-//    shuffles, online rescaling in the log2 domain.  PV: the same chunk
-//    ownership, so the accumulator stays in registers.
+//    every block.  The GL lanes that share a head row form a group that
+//    reduces q.k with xor shuffles and keeps that head's online-softmax state
+//    (m, l) and its slice of the accumulator in registers, rescaling once per
+//    batch of up to four tokens.  No CTA-wide barrier is needed per block:
+//    warps only meet at the stage mbarriers, and at a segment's end, where the
+//    k token subgroups are merged through shared memory.
 //  * Merge.  A sequence finished inside one CTA is normalised and written
 //    directly.  Otherwise each CTA writes (m, l, acc) to the workspace, bumps
 //    the sequence's counter, and the CTA that arrives last merges all
@@ -54,13 +56,14 @@ struct AttnParams {
     int slab_bytes;  // 16 * n_kv_head * head_dim * sizeof(T)
     int q_bytes;     // n_head * head_dim * sizeof(T)
     int off_meta;    // within a stage
-    int off_scores, off_probs, off_m, off_l, off_corr, off_scratch, off_misc, off_bars;
+    int off_scratch, off_misc, off_bars;
     unsigned int* counters;  // [batch] merge counters, zero between launches
     float2* part_ml;         // [grid + batch][n_head] (m, l)
     float* part_acc;         // [grid + batch][n_head][head_dim]
 };
 
-// Largest CTA index whose range start floor(i*N/G) is <= u.
+// Largest working-CTA index whose range start floor(i*N/G) is <= u.  With
+// G <= N every working CTA owns at least one unit.
 __device__ __forceinline__ int cta_of_unit(long long u, long long N, int G) {
     return static_cast<int>(((u + 1) * G - 1) / N);
 }
@@ -70,7 +73,7 @@ __device__ __forceinline__ int clamp_seq_len(int c, int mbps) {
 }
 
 // Exclusive scan of v over all threads of the CTA; *total gets the sum.
-// warp_sums needs 32 ints of shared memory.  Contains __syncthreads.
+// warp_sums needs 33 ints of shared memory.  Contains __syncthreads.
 __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nwarps = (blockDim.x + 31) >> 5;
@@ -104,13 +107,13 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     constexpr int GL = DH / E;  // lanes sharing one head row
     static_assert(GL >= 2 && GL <= 32 && (32 % GL) == 0, "head_dim / dtype combination");
     constexpr int ES = static_cast<int>(sizeof(T));
+    constexpr int TB = 4;  // tokens per online-softmax rescale
 
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int H = p.n_head;
     const int Hkv = p.n_kv_head;
     const int C = Hkv * GL;  // 16-byte chunks per token row (all kv heads)
-    const int G = gridDim.x;
     const int cta = blockIdx.x;
     const int B = p.batch;
     const int S = p.stages;
@@ -118,18 +121,15 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
     uint64_t* empty = full + S;
     int* misc = reinterpret_cast<int*>(smem + p.off_misc);  // [0..1] start, [2..34] scan, [40] last flag
-    float* sS = reinterpret_cast<float*>(smem + p.off_scores);
-    float* sP = reinterpret_cast<float*>(smem + p.off_probs);
-    float* sM = reinterpret_cast<float*>(smem + p.off_m);
-    float* sL = reinterpret_cast<float*>(smem + p.off_l);
-    float* sCorr = reinterpret_cast<float*>(smem + p.off_corr);
     float* sScratch = reinterpret_cast<float*>(smem + p.off_scratch);
 
+    uint64_t* segbar = empty + S;  // consumer-wide sync at segment ends
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], static_cast<uint32_t>(p.ncons / 32));
         }
+        mbar_init(segbar, static_cast<uint32_t>(p.ncons));
         fence_mbar_init();
     }
 
@@ -140,8 +140,9 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     for (int b = b_lo; b < b_hi; ++b) local += (clamp_seq_len(__ldg(p.seq_lens + b), p.mbps) + 15) >> 4;
     int N = 0;
     const int excl = block_exclusive_scan(local, misc + 2, &N);
-    const long long s_unit = static_cast<long long>(cta) * N / G;
-    const long long e_unit = static_cast<long long>(cta + 1) * N / G;
+    const int G = min(static_cast<int>(gridDim.x), max(N, 1));
+    const long long s_unit = cta < G ? static_cast<long long>(cta) * N / G : 0;
+    const long long e_unit = cta < G ? static_cast<long long>(cta + 1) * N / G : 0;
     {
         int run = excl;
         for (int b = b_lo; b < b_hi; ++b) {
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 misc[1] = run;
             }
             run += nb;
-            if (b % G == cta) {
+            if (b % static_cast<int>(gridDim.x) == cta) {
                 if (raw != cl) flag_error(B2_DEVERR_SEQ_LEN);
                 if (nb == 0) {  // no keys: the reference writes 0 (l == 0)
                     OutT* o = reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(b) * H * DH;
@@ -270,6 +271,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     // ===================================================== consumer threads
     const int ncons = p.ncons;
     const int ks = p.ksplit;
+    (void)ncons;
     const int ts = tid / C;
     const int c = tid - ts * C;
     const bool active = ts < ks;
@@ -277,126 +279,126 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     const int dg = c - hk * GL;
     const int lane = tid & 31;
     const unsigned gmask = (GL == 32) ? 0xffffffffu : (((1u << GL) - 1u) << (lane & ~(GL - 1)));
-    const unsigned hmask = 0xffffu << (lane & 16);
+    // All consumer threads meet on segbar (bounded): returns false on timeout.
+    uint32_t seg_parity = 0;
+    auto consumers_sync = [&]() -> bool {
+        mbar_arrive(segbar);
+        const bool ok = mbar_wait_bounded(segbar, seg_parity);
+        seg_parity ^= 1u;
+        return !__any_sync(0xffffffffu, !ok);
+    };
 
     float qf[QG][E];
     float acc[QG][E];
+    float m_run[QG];
+    float l_run[QG];
 #pragma unroll
-    for (int g = 0; g < QG; ++g)
+    for (int g = 0; g < QG; ++g) {
+        m_run[g] = -INFINITY;
+        l_run[g] = 0.0f;
 #pragma unroll
         for (int e = 0; e < E; ++e) {
             qf[g][e] = 0.0f;
             acc[g][e] = 0.0f;
         }
+    }
 
     OutT* out = static_cast<OutT*>(p.out);
     for (int n = 0; n < nunits; ++n) {
         const int st = n % S;
         const uint32_t ph = static_cast<uint32_t>(n / S) & 1u;
         unsigned char* stage = smem + static_cast<size_t>(st) * p.stage_bytes;
-        const bool timed_out = !mbar_wait_bounded(&full[st], ph);
-        int4 meta = make_int4(0, 0, 1, 0);
-        if (!timed_out) meta = *reinterpret_cast<const int4*>(stage + p.off_meta);
+        // A warp that gives up leaves the kernel as a whole (warp-uniform
+        // decision); the others then time out on their own bounded waits.
+        if (__any_sync(0xffffffffu, !mbar_wait_bounded(&full[st], ph))) {
+            if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+            return;
+        }
+        const int4 meta = *reinterpret_cast<const int4*>(stage + p.off_meta);
         const int b = meta.x;
-        const int ntok = timed_out ? 0 : min(meta.y & 0xff, kBlockTokens);
+        const int ntok = min(meta.y & 0xff, kBlockTokens);
         const bool first = (meta.y >> 8) & 1;
         const bool last = (meta.y >> 9) & 1;
 
-        if (first && active) {
-            const unsigned char* qs = stage + 2 * p.slab_bytes;
-#pragma unroll
-            for (int g = 0; g < QG; ++g) {
-                float f[E], bf[E];
-                unpack16<T>(ld_shared16(qs + ((hk * QG + g) * DH + dg * E) * ES), f);
-                if (p.q_bias != nullptr) {
-                    // q + bias rounded to T, as the reference's separate
-                    // add_bias launch stores it (engine.cu:158).
-                    unpack16<T>(__ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.q_bias) +
-                                                                     (hk * QG + g) * DH + dg * E)),
-                                bf);
-#pragma unroll
-                    for (int e = 0; e < E; ++e) f[e] = Elem<T>::to_f(Elem<T>::from_f(__fadd_rn(f[e], bf[e])));
-                }
-#pragma unroll
-                for (int e = 0; e < E; ++e) {
-                    qf[g][e] = f[e] * p.scale_log2;
-                    acc[g][e] = 0.0f;
-                }
-            }
-        }
-
-        // ---- phase A: scores s[h][t] = q_h . k_t (log2 domain)
         if (active) {
-            const unsigned char* K = stage;
-            for (int t = ts; t < ntok; t += ks) {
-                float kf[E];
-                unpack16<T>(ld_shared16(K + (t * C + c) * 16), kf);
-                float d[QG];
+            if (first) {
+                const unsigned char* qs = stage + 2 * p.slab_bytes;
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
-                    float a = 0.0f;
+                    float f[E];
+                    unpack16<T>(ld_shared16(qs + ((hk * QG + g) * DH + dg * E) * ES), f);
+                    if (p.q_bias != nullptr) {
+                        // q + bias rounded to T, as the reference's separate
+                        // add_bias launch stores it (engine.cu:158).
+                        float bf[E];
+                        unpack16<T>(__ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.q_bias) +
+                                                                         (hk * QG + g) * DH + dg * E)),
+                                    bf);
 #pragma unroll
-                    for (int e = 0; e < E; ++e) a = fmaf(qf[g][e], kf[e], a);
-                    d[g] = a;
+                        for (int e = 0; e < E; ++e) f[e] = Elem<T>::to_f(Elem<T>::from_f(__fadd_rn(f[e], bf[e])));
+                    }
+#pragma unroll
+                    for (int e = 0; e < E; ++e) {
+                        qf[g][e] = f[e] * p.scale_log2;
+                        acc[g][e] = 0.0f;
+                    }
+                    m_run[g] = -INFINITY;
+                    l_run[g] = 0.0f;
+                }
+            }
+            const unsigned char* K = stage;
+            const unsigned char* V = stage + p.slab_bytes;
+            for (int t0 = ts; t0 < ntok; t0 += TB * ks) {
+                const int cnt = min(TB, (ntok - t0 + ks - 1) / ks);  // same for the whole lane group
+                float s[TB][QG];
+#pragma unroll
+                for (int j = 0; j < TB; ++j) {
+                    if (j < cnt) {
+                        float kf[E];
+                        unpack16<T>(ld_shared16(K + ((t0 + j * ks) * C + c) * 16), kf);
+#pragma unroll
+                        for (int g = 0; g < QG; ++g) {
+                            float a = 0.0f;
+#pragma unroll
+                            for (int e = 0; e < E; ++e) a = fmaf(qf[g][e], kf[e], a);
+                            s[j][g] = a;
+                        }
+                    } else {
+#pragma unroll
+                        for (int g = 0; g < QG; ++g) s[j][g] = 0.0f;
+                    }
                 }
 #pragma unroll
                 for (int off = GL / 2; off > 0; off >>= 1)
 #pragma unroll
-                    for (int g = 0; g < QG; ++g) d[g] += __shfl_xor_sync(gmask, d[g], off);
-                if (dg == 0) {
+                    for (int j = 0; j < TB; ++j)
 #pragma unroll
-                    for (int g = 0; g < QG; ++g) sS[(hk * QG + g) * kBlockTokens + t] = d[g];
-                }
-            }
-        }
-        if (named_sync_or(1, ncons, timed_out)) {
-            if (tid == 0) flag_error(B2_DEVERR_TIMEOUT);
-            break;
-        }
-
-        // ---- phase B: online softmax statistics per head over this block
-        for (int idx = tid; idx < H * kBlockTokens; idx += ncons) {
-            const int h = idx >> 4;
-            const int t = idx & 15;
-            const float sv = t < ntok ? sS[idx] : -INFINITY;
-            float bm = sv;
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) bm = fmaxf(bm, __shfl_xor_sync(hmask, bm, off));
-            const float mo = first ? -INFINITY : sM[h];
-            const float mn = fmaxf(mo, bm);
-            const float pv = t < ntok ? exp2f(sv - mn) : 0.0f;
-            float ps = pv;
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) ps += __shfl_xor_sync(hmask, ps, off);
-            if (t == 0) {
-                const float corr = first ? 0.0f : exp2f(mo - mn);
-                sL[h] = (first ? 0.0f : sL[h] * corr) + ps;
-                sM[h] = mn;
-                sCorr[h] = corr;
-            }
-            sP[idx] = pv;
-        }
-        named_sync(1, ncons);
-
-        // ---- phase C: acc = acc * corr + sum_t p_t v_t
-        if (active) {
-            if (!first) {
+                        for (int g = 0; g < QG; ++g) s[j][g] += __shfl_xor_sync(gmask, s[j][g], off);
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
-                    const float cr = sCorr[hk * QG + g];
+                    float mx = m_run[g];
 #pragma unroll
-                    for (int e = 0; e < E; ++e) acc[g][e] *= cr;
+                    for (int j = 0; j < TB; ++j)
+                        if (j < cnt) mx = fmaxf(mx, s[j][g]);
+                    const float corr = exp2f(m_run[g] - mx);  // 0 on the first batch (m_run = -inf)
+                    m_run[g] = mx;
+                    l_run[g] *= corr;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) acc[g][e] *= corr;
                 }
-            }
-            const unsigned char* V = stage + p.slab_bytes;
-            for (int t = ts; t < ntok; t += ks) {
-                float vf[E];
-                unpack16<T>(ld_shared16(V + (t * C + c) * 16), vf);
 #pragma unroll
-                for (int g = 0; g < QG; ++g) {
-                    const float pw = sP[(hk * QG + g) * kBlockTokens + t];
+                for (int j = 0; j < TB; ++j) {
+                    if (j < cnt) {
+                        float vf[E];
+                        unpack16<T>(ld_shared16(V + ((t0 + j * ks) * C + c) * 16), vf);
 #pragma unroll
-                    for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pw, vf[e], acc[g][e]);
+                        for (int g = 0; g < QG; ++g) {
+                            const float pw = exp2f(s[j][g] - m_run[g]);
+                            l_run[g] += pw;
+#pragma unroll
+                            for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pw, vf[e], acc[g][e]);
+                        }
+                    }
                 }
             }
         }
@@ -405,34 +407,47 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
 
         if (!last) continue;
 
-        // ---- segment end: combine token subgroups, then write or merge
+        // ---- segment end: merge the k token subgroups, then write or hand off
         const int nseg = meta.z;
         const int i0 = meta.w;
         const bool single = nseg == 1;
         const int slot = cta + b;
         if (ks > 1) {
+            float* sacc = sScratch;                                          // [ks][H][DH]
+            float* sml = sScratch + static_cast<size_t>(ks) * H * DH;        // [ks][H][2]
             if (active) {
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
-                    float* dst = sScratch + (static_cast<size_t>(ts) * H + hk * QG + g) * DH + dg * E;
+                    float* dst = sacc + (static_cast<size_t>(ts) * H + hk * QG + g) * DH + dg * E;
 #pragma unroll
                     for (int e = 0; e < E; ++e) dst[e] = acc[g][e];
+                    if (dg == 0) {
+                        sml[(ts * H + hk * QG + g) * 2] = m_run[g];
+                        sml[(ts * H + hk * QG + g) * 2 + 1] = l_run[g];
+                    }
                 }
             }
-            named_sync(1, ncons);
+            if (!consumers_sync()) {
+                if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+                return;
+            }
             for (int idx = tid; idx < H * GL; idx += ncons) {
                 const int h = idx / GL;
                 const int dc = idx - h * GL;
-                float a[E];
+                float mmax = -INFINITY;
+                for (int s2 = 0; s2 < ks; ++s2) mmax = fmaxf(mmax, sml[(s2 * H + h) * 2]);
+                float a[E], l = 0.0f;
 #pragma unroll
                 for (int e = 0; e < E; ++e) a[e] = 0.0f;
                 for (int s2 = 0; s2 < ks; ++s2) {
-                    const float* src = sScratch + (static_cast<size_t>(s2) * H + h) * DH + dc * E;
+                    const float ms = sml[(s2 * H + h) * 2];
+                    const float w = ms == -INFINITY ? 0.0f : exp2f(ms - mmax);  // a subgroup may have had no tokens
+                    l = fmaf(sml[(s2 * H + h) * 2 + 1], w, l);
+                    const float* src = sacc + (static_cast<size_t>(s2) * H + h) * DH + dc * E;
 #pragma unroll
-                    for (int e = 0; e < E; ++e) a[e] += src[e];
+                    for (int e = 0; e < E; ++e) a[e] = fmaf(src[e], w, a[e]);
                 }
                 if (single) {
-                    const float l = sL[h];
                     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll
                     for (int e = 0; e < E; ++e) a[e] *= inv;
@@ -442,6 +457,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
 #pragma unroll
                     for (int e = 0; e < E; e += 4)
                         __stcg(reinterpret_cast<float4*>(dst + e), make_float4(a[e], a[e + 1], a[e + 2], a[e + 3]));
+                    if (dc == 0) __stcg(p.part_ml + static_cast<size_t>(slot) * H + h, make_float2(mmax, l));
                 }
             }
         } else if (active) {
@@ -449,8 +465,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             for (int g = 0; g < QG; ++g) {
                 const int h = hk * QG + g;
                 if (single) {
-                    const float l = sL[h];
-                    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+                    const float inv = l_run[g] > 0.0f ? 1.0f / l_run[g] : 0.0f;
                     float a[E];
 #pragma unroll
                     for (int e = 0; e < E; ++e) a[e] = acc[g][e] * inv;
@@ -461,52 +476,63 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                     for (int e = 0; e < E; e += 4)
                         __stcg(reinterpret_cast<float4*>(dst + e),
                                make_float4(acc[g][e], acc[g][e + 1], acc[g][e + 2], acc[g][e + 3]));
+                    if (dg == 0) __stcg(p.part_ml + static_cast<size_t>(slot) * H + h, make_float2(m_run[g], l_run[g]));
                 }
             }
         }
-        if (single) continue;
-
-        for (int h = tid; h < H; h += ncons) __stcg(p.part_ml + static_cast<size_t>(slot) * H + h, make_float2(sM[h], sL[h]));
-        __threadfence();
-        named_sync(1, ncons);
-        if (tid == 0) {
-            const unsigned int prev = atomicAdd(p.counters + b, 1u);
-            misc[40] = (prev == static_cast<unsigned int>(nseg - 1)) ? 1 : 0;
-        }
-        named_sync(1, ncons);
-        if (misc[40]) {
+        if (!single) {
             __threadfence();
-            for (int idx = tid; idx < H * GL; idx += ncons) {
-                const int h = idx / GL;
-                const int dc = idx - h * GL;
-                float mmax = -INFINITY;
-                for (int s2 = 0; s2 < nseg; ++s2)
-                    mmax = fmaxf(mmax, __ldcg(p.part_ml + static_cast<size_t>(i0 + s2 + b) * H + h).x);
-                float l = 0.0f;
-                float a[E];
-#pragma unroll
-                for (int e = 0; e < E; ++e) a[e] = 0.0f;
-                for (int s2 = 0; s2 < nseg; ++s2) {
-                    const size_t sl = static_cast<size_t>(i0 + s2 + b);
-                    const float2 ml = __ldcg(p.part_ml + sl * H + h);
-                    const float w = exp2f(ml.x - mmax);
-                    l = fmaf(ml.y, w, l);
-                    const float* src = p.part_acc + (sl * H + h) * DH + dc * E;
-#pragma unroll
-                    for (int e = 0; e < E; e += 4) {
-                        const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + e));
-                        a[e] = fmaf(v4.x, w, a[e]);
-                        a[e + 1] = fmaf(v4.y, w, a[e + 1]);
-                        a[e + 2] = fmaf(v4.z, w, a[e + 2]);
-                        a[e + 3] = fmaf(v4.w, w, a[e + 3]);
-                    }
-                }
-                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-#pragma unroll
-                for (int e = 0; e < E; ++e) a[e] *= inv;
-                store_row<OutT, E>(out + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
+            if (!consumers_sync()) {
+                if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+                return;
             }
-            if (tid == 0) p.counters[b] = 0u;
+            if (tid == 0) {
+                const unsigned int prev = atomicAdd(p.counters + b, 1u);
+                misc[40] = (prev == static_cast<unsigned int>(nseg - 1)) ? 1 : 0;
+            }
+            if (!consumers_sync()) {
+                if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+                return;
+            }
+            if (misc[40]) {
+                __threadfence();
+                for (int idx = tid; idx < H * GL; idx += ncons) {
+                    const int h = idx / GL;
+                    const int dc = idx - h * GL;
+                    float mmax = -INFINITY;
+                    for (int s2 = 0; s2 < nseg; ++s2)
+                        mmax = fmaxf(mmax, __ldcg(p.part_ml + static_cast<size_t>(i0 + s2 + b) * H + h).x);
+                    float l = 0.0f;
+                    float a[E];
+#pragma unroll
+                    for (int e = 0; e < E; ++e) a[e] = 0.0f;
+                    for (int s2 = 0; s2 < nseg; ++s2) {
+                        const size_t sl = static_cast<size_t>(i0 + s2 + b);
+                        const float2 ml = __ldcg(p.part_ml + sl * H + h);
+                        const float w = exp2f(ml.x - mmax);
+                        l = fmaf(ml.y, w, l);
+                        const float* src = p.part_acc + (sl * H + h) * DH + dc * E;
+#pragma unroll
+                        for (int e = 0; e < E; e += 4) {
+                            const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + e));
+                            a[e] = fmaf(v4.x, w, a[e]);
+                            a[e + 1] = fmaf(v4.y, w, a[e + 1]);
+                            a[e + 2] = fmaf(v4.z, w, a[e + 2]);
+                            a[e + 3] = fmaf(v4.w, w, a[e + 3]);
+                        }
+                    }
+                    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) a[e] *= inv;
+                    store_row<OutT, E>(out + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
+                }
+                if (tid == 0) p.counters[b] = 0u;
+            }
+        }
+        // The scratch and the last-CTA flag are reused at the next segment end.
+        if ((ks > 1 || !single) && !consumers_sync()) {
+            if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+            return;
         }
     }
 }

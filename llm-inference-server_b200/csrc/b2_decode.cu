@@ -65,14 +65,19 @@ DeviceInfo device_info(int* dev_out) {
     return cache[dev];
 }
 
-// cudaFuncSetAttribute once per (kernel, device).
+// cudaFuncSetAttribute once per (kernel, device); `done` must be a flag word
+// owned by that one kernel instantiation.
 template <typename K>
-void ensure_max_smem(K kernel, int dev, int bytes) {
-    static std::atomic<uint64_t> done{0};
+int ensure_max_smem(K kernel, std::atomic<uint64_t>& done, int dev, int bytes) {
     const uint64_t bit = 1ull << dev;
-    if (done.load(std::memory_order_acquire) & bit) return;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (done.load(std::memory_order_acquire) & bit) return B2_OK;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) {
+        g_last_error = cudaGetErrorString(e);
+        return static_cast<int>(e);
+    }
     done.fetch_or(bit, std::memory_order_acq_rel);
+    return B2_OK;
 }
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -137,8 +142,8 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
         const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * C, 32));
         if (ncons + 32 > maxt) continue;
         if (k > 1 && k * C > 512) continue;  // enough warps; keep smem for stages
-        const int scratch = k > 1 ? k * H * a->head_dim * 4 : 0;
-        const int fixed = 2 * H * B2_BLOCK_TOKENS * 4 + 3 * H * 4 + 256 + scratch;
+        const int scratch = k > 1 ? k * H * (a->head_dim + 2) * 4 : 0;  // acc + (m, l) per subgroup
+        const int fixed = 256 + scratch;
         int s = (smem_cap - fixed - 512) / stage;  // 512: barriers + alignment padding
         if (s > 8) s = 8;
         if (s < 2) continue;
@@ -160,24 +165,13 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     p.q_bytes = qbytes;
     p.off_meta = off_meta;
     int off = best_s * stage;
-    p.off_scores = off;
-    off += H * B2_BLOCK_TOKENS * 4;
-    p.off_probs = off;
-    off += H * B2_BLOCK_TOKENS * 4;
-    p.off_m = off;
-    off += H * 4;
-    p.off_l = off;
-    off += H * 4;
-    p.off_corr = off;
-    off += H * 4;
-    off = static_cast<int>(align_up(off, 16));
     p.off_scratch = off;
-    off += best_fixed - (2 * H * B2_BLOCK_TOKENS * 4 + 3 * H * 4 + 256);
+    off += best_fixed - 256;
     off = static_cast<int>(align_up(off, 16));
     p.off_misc = off;
     off += 256;
     p.off_bars = off;
-    off += 2 * best_s * 8;
+    off += (2 * best_s + 1) * 8;
     pl->smem = off;
     pl->threads = p.ncons + 32;
     pl->grid = di.sms;
@@ -194,9 +188,11 @@ template <typename T, int DH, int QG, typename OutT>
 int launch_attn_t(const AttnPlan& pl, cudaStream_t stream) {
     constexpr int MAXT = kAttnMaxThreads;
     auto kern = paged_decode_kernel<T, DH, QG, OutT, MAXT>;
+    static std::atomic<uint64_t> smem_set{0};  // one flag word per instantiation
     int dev = -1;
     const DeviceInfo di = device_info(&dev);
-    ensure_max_smem(kern, dev, di.max_smem_optin);
+    const int rc = ensure_max_smem(kern, smem_set, dev, di.max_smem_optin);
+    if (rc != B2_OK) return rc;
     kern<<<pl.grid, pl.threads, pl.smem, stream>>>(pl.prm);
     return launch_status();
 }
