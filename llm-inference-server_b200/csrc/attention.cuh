@@ -107,7 +107,8 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     constexpr int GL = DH / E;  // lanes sharing one head row
     static_assert(GL >= 2 && GL <= 32 && (32 % GL) == 0, "head_dim / dtype combination");
     constexpr int ES = static_cast<int>(sizeof(T));
-    constexpr int TB = 4;  // tokens per online-softmax rescale
+    constexpr int TB = 4;           // tokens per online-softmax rescale
+    constexpr int kMaxPending = 16;  // deferred hand-offs per CTA before a flush
 
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
@@ -120,7 +121,8 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
     uint64_t* empty = full + S;
-    int* misc = reinterpret_cast<int*>(smem + p.off_misc);  // [0..1] start, [2..34] scan, [40] last flag
+    // misc (512 B): [0..1] first sequence and its prefix, [2..34] scan, [40] pending count, [48..111] pending list
+    int* misc = reinterpret_cast<int*>(smem + p.off_misc);
     float* sScratch = reinterpret_cast<float*>(smem + p.off_scratch);
 
     uint64_t* segbar = empty + S;  // consumer-wide sync at segment ends
@@ -130,11 +132,18 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             mbar_init(&empty[s], static_cast<uint32_t>(p.ncons / 32));
         }
         mbar_init(segbar, static_cast<uint32_t>(p.ncons));
+        misc[40] = 0;
         fence_mbar_init();
     }
 
+    // Programmatic dependent launch: let the next kernel in the stream start
+    // its own prologue as our CTAs retire, and wait here until the kernels
+    // before us (which produce q, the pool and seq_lens) have completed.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
     // ---- prologue: per-sequence block counts, global prefix, this CTA's range
-    const int per = (B + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
+    const int per =(B + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
     const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
     int local = 0;
     for (int b = b_lo; b < b_hi; ++b) local += (clamp_seq_len(__ldg(p.seq_lens + b), p.mbps) + 15) >> 4;
@@ -288,20 +297,94 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         return !__any_sync(0xffffffffu, !ok);
     };
 
-    float qf[QG][E];
+    OutT* const out_ptr = static_cast<OutT*>(p.out);
+    // Sequences whose partial this CTA wrote but has not yet reported
+    // (b, nseg, i0, last-flag).  Reporting is batched: one fence and atomic
+    // per entry at the end of the range instead of a stall per segment.
+    int* npend_s = misc + 40;
+    int4* pend = reinterpret_cast<int4*>(misc + 48);
+
+    // Combines the nseg partials of sequence b (workspace slots i0 + s + b)
+    // and writes its output; all consumer threads take part.
+    auto merge_sequence = [&](int b, int nseg, int i0) {
+        for (int idx = tid; idx < H * GL; idx += ncons) {
+            const int h = idx / GL;
+            const int dc = idx - h * GL;
+            float mmax = -INFINITY;
+            for (int s2 = 0; s2 < nseg; ++s2)
+                mmax = fmaxf(mmax, __ldcg(p.part_ml + static_cast<size_t>(i0 + s2 + b) * H + h).x);
+            float l = 0.0f;
+            float a[E];
+#pragma unroll
+            for (int e = 0; e < E; ++e) a[e] = 0.0f;
+            for (int s2 = 0; s2 < nseg; ++s2) {
+                const size_t sl = static_cast<size_t>(i0 + s2 + b);
+                const float2 ml = __ldcg(p.part_ml + sl * H + h);
+                const float w = exp2f(ml.x - mmax);
+                l = fmaf(ml.y, w, l);
+                const float* src = p.part_acc + (sl * H + h) * DH + dc * E;
+#pragma unroll
+                for (int e = 0; e < E; e += 4) {
+                    const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + e));
+                    a[e] = fmaf(v4.x, w, a[e]);
+                    a[e + 1] = fmaf(v4.y, w, a[e + 1]);
+                    a[e + 2] = fmaf(v4.z, w, a[e + 2]);
+                    a[e + 3] = fmaf(v4.w, w, a[e + 3]);
+                }
+            }
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+            for (int e = 0; e < E; ++e) a[e] *= inv;
+            store_row<OutT, E>(out_ptr + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
+        }
+    };
+
+    // Reports every pending partial: after the CTA-wide sync that ordered all
+    // partial writes, one thread per entry fences at gpu scope (cumulative over
+    // the CTA's writes) and bumps the sequence's counter; the CTA that brings a
+    // counter to nseg merges that sequence and resets the counter to zero.
+    auto flush_pending = [&]() -> bool {
+        const int np = npend_s[0];
+        if (np == 0) return true;
+        for (int j = tid; j < np; j += ncons) {
+            const int4 e = pend[j];
+            __threadfence();
+            const unsigned int prev = atomicAdd(p.counters + e.x, 1u);
+            const bool is_last = prev == static_cast<unsigned int>(e.y - 1);
+            if (is_last) __threadfence();
+            pend[j].w = is_last ? 1 : 0;
+        }
+        if (!consumers_sync()) {
+            if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+            return false;
+        }
+        for (int j = 0; j < np; ++j) {
+            const int4 e = pend[j];
+            if (!e.w) continue;
+            merge_sequence(e.x, e.y, e.z);
+            if (tid == 0) p.counters[e.x] = 0u;
+        }
+        if (tid == 0) npend_s[0] = 0;
+        if (!consumers_sync()) {
+            if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+            return false;
+        }
+        return true;
+    };
+
+    uint4 qraw[QG];  // this thread's q chunks, in the storage dtype (bias added)
     float acc[QG][E];
     float m_run[QG];
     float l_run[QG];
 #pragma unroll
     for (int g = 0; g < QG; ++g) {
+        qraw[g] = make_uint4(0u, 0u, 0u, 0u);
         m_run[g] = -INFINITY;
         l_run[g] = 0.0f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-            qf[g][e] = 0.0f;
-            acc[g][e] = 0.0f;
-        }
+        for (int e = 0; e < E; ++e) acc[g][e] = 0.0f;
     }
+    const float scale_log2 = p.scale_log2;
 
     OutT* out = static_cast<OutT*>(p.out);
     for (int n = 0; n < nunits; ++n) {
@@ -325,23 +408,21 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 const unsigned char* qs = stage + 2 * p.slab_bytes;
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
-                    float f[E];
-                    unpack16<T>(ld_shared16(qs + ((hk * QG + g) * DH + dg * E) * ES), f);
+                    qraw[g] = ld_shared16(qs + ((hk * QG + g) * DH + dg * E) * ES);
                     if (p.q_bias != nullptr) {
                         // q + bias rounded to T, as the reference's separate
                         // add_bias launch stores it (engine.cu:158).
-                        float bf[E];
+                        float f[E], bf[E];
+                        unpack16<T>(qraw[g], f);
                         unpack16<T>(__ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.q_bias) +
                                                                          (hk * QG + g) * DH + dg * E)),
                                     bf);
 #pragma unroll
-                        for (int e = 0; e < E; ++e) f[e] = Elem<T>::to_f(Elem<T>::from_f(__fadd_rn(f[e], bf[e])));
+                        for (int e = 0; e < E; ++e) f[e] = __fadd_rn(f[e], bf[e]);
+                        qraw[g] = pack16<T>(f);
                     }
 #pragma unroll
-                    for (int e = 0; e < E; ++e) {
-                        qf[g][e] = f[e] * p.scale_log2;
-                        acc[g][e] = 0.0f;
-                    }
+                    for (int e = 0; e < E; ++e) acc[g][e] = 0.0f;
                     m_run[g] = -INFINITY;
                     l_run[g] = 0.0f;
                 }
@@ -354,15 +435,9 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
 #pragma unroll
                 for (int j = 0; j < TB; ++j) {
                     if (j < cnt) {
-                        float kf[E];
-                        unpack16<T>(ld_shared16(K + ((t0 + j * ks) * C + c) * 16), kf);
+                        const uint4 kraw = ld_shared16(K + ((t0 + j * ks) * C + c) * 16);
 #pragma unroll
-                        for (int g = 0; g < QG; ++g) {
-                            float a = 0.0f;
-#pragma unroll
-                            for (int e = 0; e < E; ++e) a = fmaf(qf[g][e], kf[e], a);
-                            s[j][g] = a;
-                        }
+                        for (int g = 0; g < QG; ++g) s[j][g] = dot16<T>(qraw[g], kraw, 0.0f);
                     } else {
 #pragma unroll
                         for (int g = 0; g < QG; ++g) s[j][g] = 0.0f;
@@ -374,6 +449,10 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                     for (int j = 0; j < TB; ++j)
 #pragma unroll
                         for (int g = 0; g < QG; ++g) s[j][g] += __shfl_xor_sync(gmask, s[j][g], off);
+#pragma unroll
+                for (int j = 0; j < TB; ++j)
+#pragma unroll
+                    for (int g = 0; g < QG; ++g) s[j][g] *= scale_log2;  // (q.k) * scale, in log2 units
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
                     float mx = m_run[g];
@@ -389,14 +468,12 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
 #pragma unroll
                 for (int j = 0; j < TB; ++j) {
                     if (j < cnt) {
-                        float vf[E];
-                        unpack16<T>(ld_shared16(V + ((t0 + j * ks) * C + c) * 16), vf);
+                        const uint4 vraw = ld_shared16(V + ((t0 + j * ks) * C + c) * 16);
 #pragma unroll
                         for (int g = 0; g < QG; ++g) {
                             const float pw = exp2f(s[j][g] - m_run[g]);
                             l_run[g] += pw;
-#pragma unroll
-                            for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pw, vf[e], acc[g][e]);
+                            axpy16<T>(pw, vraw, acc[g]);
                         }
                     }
                 }
@@ -480,61 +557,20 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 }
             }
         }
-        if (!single) {
-            __threadfence();
-            if (!consumers_sync()) {
-                if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
-                return;
-            }
-            if (tid == 0) {
-                const unsigned int prev = atomicAdd(p.counters + b, 1u);
-                misc[40] = (prev == static_cast<unsigned int>(nseg - 1)) ? 1 : 0;
-            }
-            if (!consumers_sync()) {
-                if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
-                return;
-            }
-            if (misc[40]) {
-                __threadfence();
-                for (int idx = tid; idx < H * GL; idx += ncons) {
-                    const int h = idx / GL;
-                    const int dc = idx - h * GL;
-                    float mmax = -INFINITY;
-                    for (int s2 = 0; s2 < nseg; ++s2)
-                        mmax = fmaxf(mmax, __ldcg(p.part_ml + static_cast<size_t>(i0 + s2 + b) * H + h).x);
-                    float l = 0.0f;
-                    float a[E];
-#pragma unroll
-                    for (int e = 0; e < E; ++e) a[e] = 0.0f;
-                    for (int s2 = 0; s2 < nseg; ++s2) {
-                        const size_t sl = static_cast<size_t>(i0 + s2 + b);
-                        const float2 ml = __ldcg(p.part_ml + sl * H + h);
-                        const float w = exp2f(ml.x - mmax);
-                        l = fmaf(ml.y, w, l);
-                        const float* src = p.part_acc + (sl * H + h) * DH + dc * E;
-#pragma unroll
-                        for (int e = 0; e < E; e += 4) {
-                            const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + e));
-                            a[e] = fmaf(v4.x, w, a[e]);
-                            a[e + 1] = fmaf(v4.y, w, a[e + 1]);
-                            a[e + 2] = fmaf(v4.z, w, a[e + 2]);
-                            a[e + 3] = fmaf(v4.w, w, a[e + 3]);
-                        }
-                    }
-                    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-#pragma unroll
-                    for (int e = 0; e < E; ++e) a[e] *= inv;
-                    store_row<OutT, E>(out + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
-                }
-                if (tid == 0) p.counters[b] = 0u;
-            }
+        if (!single && tid == 0) {
+            // Hand-off deferred to the end of this CTA's range (or to a flush
+            // when the list is full): the partial is written, the arrival is not.
+            pend[npend_s[0]] = make_int4(b, nseg, i0, 0);
+            npend_s[0] += 1;
         }
-        // The scratch and the last-CTA flag are reused at the next segment end.
+        // The scratch (and the pending list's count) are reused at the next segment end.
         if ((ks > 1 || !single) && !consumers_sync()) {
             if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
             return;
         }
+        if (npend_s[0] == kMaxPending && !flush_pending()) return;
     }
+    flush_pending();
 }
 
 }  // namespace b2

@@ -118,6 +118,102 @@ __device__ __forceinline__ void store_row(OutT* dst, const float* f) {
     for (int i = 0; i < N / P; ++i) *reinterpret_cast<uint4*>(dst + i * P) = pack16<OutT>(f + i * P);
 }
 
+// ------------------------------------------------- mixed-precision chunk math
+// sm_100 has FMA-pipe instructions that take 16-bit operands with an fp32
+// accumulator (fma.rn.f32.{f16,bf16}, add.rn.f32.{f16,bf16}).  A product of
+// two 16-bit floats is exact in fp32, so dot16 gives the same value as
+// widening both operands first -- without a separate conversion instruction
+// per element (the widening cvt runs on the quarter-rate XU pipe).
+
+// acc + sum_e q[e] * k[e] over one 16-byte chunk; q and k hold the same dtype.
+template <typename T>
+__device__ __forceinline__ float dot16(const uint4& q, const uint4& k, float acc);
+
+template <>
+__device__ __forceinline__ float dot16<float>(const uint4& q, const uint4& k, float acc) {
+    acc = fmaf(__uint_as_float(q.x), __uint_as_float(k.x), acc);
+    acc = fmaf(__uint_as_float(q.y), __uint_as_float(k.y), acc);
+    acc = fmaf(__uint_as_float(q.z), __uint_as_float(k.z), acc);
+    return fmaf(__uint_as_float(q.w), __uint_as_float(k.w), acc);
+}
+
+#define B2_DOT2_ASM(TY, REG)                                                                   \
+    "{\n\t.reg ." REG " ql, qh, kl, kh;\n\t"                                                   \
+    "mov.b32 {ql, qh}, %1;\n\t"                                                                \
+    "mov.b32 {kl, kh}, %2;\n\t"                                                                \
+    "fma.rn.f32." TY " %0, ql, kl, %0;\n\t"                                                    \
+    "fma.rn.f32." TY " %0, qh, kh, %0;\n\t}"
+
+__device__ __forceinline__ float dot2_f16(uint32_t q2, uint32_t k2, float acc) {
+    asm(B2_DOT2_ASM("f16", "f16") : "+f"(acc) : "r"(q2), "r"(k2));
+    return acc;
+}
+__device__ __forceinline__ float dot2_bf16(uint32_t q2, uint32_t k2, float acc) {
+    asm(B2_DOT2_ASM("bf16", "b16") : "+f"(acc) : "r"(q2), "r"(k2));
+    return acc;
+}
+#undef B2_DOT2_ASM
+
+template <>
+__device__ __forceinline__ float dot16<__half>(const uint4& q, const uint4& k, float acc) {
+    // two independent chains, summed at the end, halve the dependency depth
+    float a = dot2_f16(q.x, k.x, acc);
+    float b = dot2_f16(q.y, k.y, 0.0f);
+    a = dot2_f16(q.z, k.z, a);
+    b = dot2_f16(q.w, k.w, b);
+    return a + b;
+}
+template <>
+__device__ __forceinline__ float dot16<__nv_bfloat16>(const uint4& q, const uint4& k, float acc) {
+    float a = dot2_bf16(q.x, k.x, acc);
+    float b = dot2_bf16(q.y, k.y, 0.0f);
+    a = dot2_bf16(q.z, k.z, a);
+    b = dot2_bf16(q.w, k.w, b);
+    return a + b;
+}
+
+// Both halves of a packed pair widened exactly to fp32 on the FMA pipe
+// (x + 0 with x a 16-bit float and the sum in fp32).
+__device__ __forceinline__ float2 widen2_f16(uint32_t w) {
+    float lo, hi;
+    asm("{\n\t.reg .f16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+        "add.rn.f32.f16 %0, a, %3;\n\tadd.rn.f32.f16 %1, b, %3;\n\t}"
+        : "=f"(lo), "=f"(hi)
+        : "r"(w), "f"(0.0f));
+    return make_float2(lo, hi);
+}
+
+// acc[e] += p * v[e] over one 16-byte chunk of v.
+template <typename T>
+__device__ __forceinline__ void axpy16(float p, const uint4& v, float* acc);
+
+template <>
+__device__ __forceinline__ void axpy16<float>(float p, const uint4& v, float* acc) {
+    acc[0] = fmaf(p, __uint_as_float(v.x), acc[0]);
+    acc[1] = fmaf(p, __uint_as_float(v.y), acc[1]);
+    acc[2] = fmaf(p, __uint_as_float(v.z), acc[2]);
+    acc[3] = fmaf(p, __uint_as_float(v.w), acc[3]);
+}
+template <>
+__device__ __forceinline__ void axpy16<__half>(float p, const uint4& v, float* acc) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = widen2_f16(w[i]);
+        acc[2 * i] = fmaf(p, f.x, acc[2 * i]);
+        acc[2 * i + 1] = fmaf(p, f.y, acc[2 * i + 1]);
+    }
+}
+template <>
+__device__ __forceinline__ void axpy16<__nv_bfloat16>(float p, const uint4& v, float* acc) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        acc[2 * i] = fmaf(p, __uint_as_float(w[i] << 16), acc[2 * i]);
+        acc[2 * i + 1] = fmaf(p, __uint_as_float(w[i] & 0xffff0000u), acc[2 * i + 1]);
+    }
+}
+
 // ------------------------------------------------------------ PTX wrappers
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

@@ -45,6 +45,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 struct DeviceInfo {
     int sms = 0;
     int max_smem_optin = 0;
+    int smem_per_sm = 0;
 };
 
 DeviceInfo device_info(int* dev_out) {
@@ -60,6 +61,7 @@ DeviceInfo device_info(int* dev_out) {
         DeviceInfo d;
         cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
         cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
         cache[dev] = d;
     });
     return cache[dev];
@@ -85,6 +87,8 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // Threads per attention CTA at most (consumers + the producer warp); keeps
 // the register cap at 128 per thread.
 constexpr int kAttnMaxThreads = 512;
+// Shared bytes of the attention kernel's misc area (scan, pending hand-offs).
+constexpr int kMiscBytes = 512;
 
 // ---------------------------------------------------------- attention plan
 
@@ -135,22 +139,29 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     const int qbytes = H * a->head_dim * es;
     const int off_meta = 2 * slab + qbytes;
     const int stage = static_cast<int>(align_up(off_meta + 16, 128));
-    const int smem_cap = di.max_smem_optin;
-
-    int best_k = 0, best_s = 0, best_fixed = 0;
-    for (int k : {4, 2, 1}) {
-        const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * C, 32));
-        if (ncons + 32 > maxt) continue;
-        if (k > 1 && k * C > 512) continue;  // enough warps; keep smem for stages
-        const int scratch = k > 1 ? k * H * (a->head_dim + 2) * 4 : 0;  // acc + (m, l) per subgroup
-        const int fixed = 256 + scratch;
-        int s = (smem_cap - fixed - 512) / stage;  // 512: barriers + alignment padding
-        if (s > 8) s = 8;
-        if (s < 2) continue;
-        best_k = k;
-        best_s = s;
-        best_fixed = fixed;
-        break;
+    // Two CTAs per SM when each still gets a double-buffered ring: one CTA's
+    // prologue, merges and tail then overlap the other's streaming.  The
+    // 128-register cap limits a co-resident pair to 256 threads each.
+    int best_k = 0, best_s = 0, best_fixed = 0, best_cps = 0;
+    for (int cps : {2, 1}) {
+        const int smem_cap = cps == 1 ? di.max_smem_optin : di.smem_per_sm / cps - 1024;
+        const int thread_cap = cps == 1 ? maxt : 256;
+        for (int k : {4, 2, 1}) {
+            const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * C, 32));
+            if (ncons + 32 > thread_cap) continue;
+            if (k > 1 && k * C > 512) continue;  // enough warps; keep smem for stages
+            const int scratch = k > 1 ? k * H * (a->head_dim + 2) * 4 : 0;  // acc + (m, l) per subgroup
+            const int fixed = kMiscBytes + scratch;
+            int s = (smem_cap - fixed - 512) / stage;  // 512: barriers + alignment padding
+            if (s > 8) s = 8;
+            if (s < 2) continue;
+            best_k = k;
+            best_s = s;
+            best_fixed = fixed;
+            best_cps = cps;
+            break;
+        }
+        if (best_k != 0) break;
     }
     if (best_k == 0) return fail(B2_ERR_UNSUPPORTED, "head shape does not fit the decode kernel's shared memory");
     if (a->batch > 16 * (static_cast<int>(align_up(static_cast<size_t>(best_k) * C, 32)) + 32))
@@ -166,15 +177,15 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     p.off_meta = off_meta;
     int off = best_s * stage;
     p.off_scratch = off;
-    off += best_fixed - 256;
+    off += best_fixed - kMiscBytes;
     off = static_cast<int>(align_up(off, 16));
     p.off_misc = off;
-    off += 256;
+    off += kMiscBytes;
     p.off_bars = off;
     off += (2 * best_s + 1) * 8;
     pl->smem = off;
     pl->threads = p.ncons + 32;
-    pl->grid = di.sms;
+    pl->grid = di.sms * best_cps;
 
     const size_t slots = static_cast<size_t>(pl->grid) + a->batch;
     pl->ws_counters = align_up(static_cast<size_t>(a->batch) * 4, 256);
@@ -193,7 +204,24 @@ int launch_attn_t(const AttnPlan& pl, cudaStream_t stream) {
     const DeviceInfo di = device_info(&dev);
     const int rc = ensure_max_smem(kern, smem_set, dev, di.max_smem_optin);
     if (rc != B2_OK) return rc;
-    kern<<<pl.grid, pl.threads, pl.smem, stream>>>(pl.prm);
+    // Programmatic dependent launch (the kernel waits on griddepcontrol.wait
+    // before reading its inputs), so its launch overlaps the previous kernel's tail.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
+    cfg.blockDim = dim3(static_cast<unsigned>(pl.threads));
+    cfg.dynamicSmemBytes = static_cast<size_t>(pl.smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, pl.prm);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        g_last_error = cudaGetErrorString(e);
+        return static_cast<int>(e);
+    }
     return launch_status();
 }
 
