@@ -120,13 +120,15 @@ B2_API int b2_kv_append(const B2KvAppendArgs* args, b2_stream_t stream);
  * keys of sequence b (post-append count), keys of kv head h / (n_head/n_kv_head).
  * A sequence with seq_lens[b] == 0 gets a zero output, like the reference.
  *
- * The work is split over the whole GPU by KV blocks (every CTA gets the same
- * number of 16-token blocks, whatever the per-sequence lengths); sequences
- * that span CTAs are merged in-kernel by the last CTA to finish.  That needs
- * a workspace: size it with b2_paged_attention_workspace_bytes and zero it
- * once with b2_paged_attention_workspace_init before its first use (the
- * kernel leaves it zeroed again).  One workspace serves any number of
- * launches on one stream; launches that may run concurrently need their own.
+ * The work is split over the whole GPU by key rows (every CTA streams the
+ * same number of K/V rows, whatever the per-sequence lengths), so one
+ * sequence may be cut into pieces handled by several CTAs.  Each piece's
+ * partial softmax state goes to a caller-provided workspace, and a second,
+ * small kernel merges the pieces and writes `out`.  Size the workspace with
+ * b2_paged_attention_workspace_bytes; it needs no initialisation.  One
+ * workspace serves any number of launches on one stream; launches that may
+ * run concurrently need their own.  Both kernels use programmatic dependent
+ * launch, so each may start while the kernel before it finishes.
  * ---------------------------------------------------------------------- */
 typedef struct B2PagedAttnArgs {
     int32_t dtype;     /* b2_dtype of q and the pool */
@@ -153,12 +155,9 @@ typedef struct B2PagedAttnArgs {
  * current device (depends on the SM count). */
 B2_API size_t b2_paged_attention_workspace_bytes(const B2PagedAttnArgs* args);
 
-/* Zeroes the workspace's merge counters (stream-ordered, no allocation). */
-B2_API int b2_paged_attention_workspace_init(void* workspace, size_t workspace_bytes,
-                                      const B2PagedAttnArgs* args, b2_stream_t stream);
-
+/* Two launches on `stream`: the split attention kernel, then the merge. */
 B2_API int b2_paged_attention(const B2PagedAttnArgs* args, void* workspace, size_t workspace_bytes,
-                       b2_stream_t stream);
+                              b2_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Row kernels around attention.  All take dtype (f32 / f16 / bf16),

@@ -28,7 +28,7 @@ DEVERR_BLOCK_ID, DEVERR_SEQ_LEN, DEVERR_TIMEOUT, DEVERR_TOKEN = 1, 2, 4, 8
 # Every symbol include/b2_decode.h declares.
 DECODE_SYMBOLS = (
     "b2_version", "b2_last_error_string", "b2_device_errors", "b2_kv_append",
-    "b2_paged_attention_workspace_bytes", "b2_paged_attention_workspace_init", "b2_paged_attention",
+    "b2_paged_attention_workspace_bytes", "b2_paged_attention",
     "b2_add_layernorm", "b2_bias_gelu", "b2_add_bias", "b2_add_one", "b2_embedding", "b2_argmax",
 )
 
@@ -78,7 +78,6 @@ def load() -> ctypes.CDLL:
     lib.b2_kv_append.argtypes = [ctypes.POINTER(KvAppendArgs), _vp]
     lib.b2_paged_attention_workspace_bytes.argtypes = [ctypes.POINTER(PagedAttnArgs)]
     lib.b2_paged_attention_workspace_bytes.restype = ctypes.c_size_t
-    lib.b2_paged_attention_workspace_init.argtypes = [_vp, ctypes.c_size_t, ctypes.POINTER(PagedAttnArgs), _vp]
     lib.b2_paged_attention.argtypes = [ctypes.POINTER(PagedAttnArgs), _vp, ctypes.c_size_t, _vp]
     lib.b2_add_layernorm.argtypes = [_c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp]
     lib.b2_bias_gelu.argtypes = [_c_int, _vp, _vp, _vp, _c_int, _c_int, _vp]
@@ -139,15 +138,13 @@ def attn_args(q, q_row_stride, kv_pool, block_tables, seq_lens, out, *, n_head, 
                          n_kv_head, head_dim, max_blocks_per_seq, layer_idx, n_layer, num_blocks, scale)
 
 
-def attention_workspace(args: PagedAttnArgs, stream=None):
-    """Allocates (torch) and zero-initialises a workspace for launches shaped like args."""
+def attention_workspace(args: PagedAttnArgs):
+    """Allocates (torch) a workspace for launches shaped like args; it needs no initialisation."""
     import torch
     n = load().b2_paged_attention_workspace_bytes(ctypes.byref(args))
     if n == 0:
         raise B2Error(-3, load().b2_last_error_string().decode() or "workspace size query failed")
-    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
-    _check(load().b2_paged_attention_workspace_init(ws.data_ptr(), n, ctypes.byref(args), _stream(stream)))
-    return ws
+    return torch.empty(n, dtype=torch.uint8, device="cuda")
 
 
 def paged_attention(args: PagedAttnArgs, workspace, stream=None) -> None:

@@ -303,4 +303,8 @@ __device__ __forceinline__ bool named_sync_or(int id, int nthreads, bool pred) {
 
 __device__ __forceinline__ uint4 ld_shared16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
+// Acquire-release fence at GPU scope (lighter than the sequentially
+// consistent fence __threadfence() issues).
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 }  // namespace b2

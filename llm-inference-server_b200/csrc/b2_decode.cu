@@ -87,15 +87,16 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // Threads per attention CTA at most (consumers + the producer warp); keeps
 // the register cap at 128 per thread.
 constexpr int kAttnMaxThreads = 512;
-// Shared bytes of the attention kernel's misc area (scan, pending hand-offs).
-constexpr int kMiscBytes = 512;
+// Shared bytes of the attention kernel's misc area (first sequence, scan).
+constexpr int kMiscBytes = 256;
 
 // ---------------------------------------------------------- attention plan
 
 struct AttnPlan {
     int grid = 0, threads = 0, smem = 0;
+    int combine_threads = 0;
     AttnParams prm{};
-    size_t ws_counters = 0, ws_ml = 0, ws_acc = 0, ws_total = 0;
+    size_t ws_info = 0, ws_ml = 0, ws_acc = 0, ws_total = 0;
 };
 
 int check_attn_args(const B2PagedAttnArgs* a) {
@@ -118,6 +119,8 @@ int check_attn_args(const B2PagedAttnArgs* a) {
         a->num_blocks <= 0)
         return fail(B2_ERR_SHAPE, "max_blocks_per_seq, n_layer, layer_idx or num_blocks out of range");
     if (a->max_blocks_per_seq > (1 << 26) / B2_BLOCK_TOKENS) return fail(B2_ERR_SHAPE, "max_blocks_per_seq too large");
+    if (static_cast<long long>(a->batch) * a->max_blocks_per_seq * B2_BLOCK_TOKENS >= (1LL << 31))
+        return fail(B2_ERR_SHAPE, "batch * max_blocks_per_seq * 16 must stay below 2^31 token rows");
     if (a->q_row_stride < a->n_head * a->head_dim) return fail(B2_ERR_SHAPE, "q_row_stride < n_head*head_dim");
     if (!aligned16(a->q) || !aligned16(a->kv_pool) || !aligned16(a->out) || (a->q_bias && !aligned16(a->q_bias)) ||
         (static_cast<long long>(a->q_row_stride) * es) % 16 != 0)
@@ -140,24 +143,21 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     const int off_meta = 2 * slab + qbytes;
     const int stage = static_cast<int>(align_up(off_meta + 16, 128));
     // Two CTAs per SM when each still gets a double-buffered ring: one CTA's
-    // prologue, merges and tail then overlap the other's streaming.  The
-    // 128-register cap limits a co-resident pair to 256 threads each.
-    int best_k = 0, best_s = 0, best_fixed = 0, best_cps = 0;
+    // prologue and tail then overlap the other's streaming.  The 128-register
+    // cap limits a co-resident pair to 256 threads each.
+    int best_k = 0, best_s = 0, best_cps = 0;
     for (int cps : {2, 1}) {
         const int smem_cap = cps == 1 ? di.max_smem_optin : di.smem_per_sm / cps - 1024;
         const int thread_cap = cps == 1 ? maxt : 256;
         for (int k : {4, 2, 1}) {
             const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * C, 32));
             if (ncons + 32 > thread_cap) continue;
-            if (k > 1 && k * C > 512) continue;  // enough warps; keep smem for stages
-            const int scratch = k > 1 ? k * H * (a->head_dim + 2) * 4 : 0;  // acc + (m, l) per subgroup
-            const int fixed = kMiscBytes + scratch;
-            int s = (smem_cap - fixed - 512) / stage;  // 512: barriers + alignment padding
+            if (k > 1 && k * C > 512) continue;  // enough warps
+            int s = (smem_cap - kMiscBytes - 512) / stage;  // 512: barriers + alignment padding
             if (s > 8) s = 8;
             if (s < 2) continue;
             best_k = k;
             best_s = s;
-            best_fixed = fixed;
             best_cps = cps;
             break;
         }
@@ -176,47 +176,40 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     p.q_bytes = qbytes;
     p.off_meta = off_meta;
     int off = best_s * stage;
-    p.off_scratch = off;
-    off += best_fixed - kMiscBytes;
-    off = static_cast<int>(align_up(off, 16));
     p.off_misc = off;
     off += kMiscBytes;
     p.off_bars = off;
-    off += (2 * best_s + 1) * 8;
+    off += 2 * best_s * 8;
     pl->smem = off;
     pl->threads = p.ncons + 32;
     pl->grid = di.sms * best_cps;
+    pl->combine_threads = static_cast<int>(align_up(static_cast<size_t>(H) * GL, 32));
 
-    const size_t slots = static_cast<size_t>(pl->grid) + a->batch;
-    pl->ws_counters = align_up(static_cast<size_t>(a->batch) * 4, 256);
+    // One partial per (CTA, sequence) pair and token subgroup; cta + b < grid + batch.
+    const size_t slots = (static_cast<size_t>(pl->grid) + a->batch) * best_k;
+    pl->ws_info = align_up(static_cast<size_t>(a->batch) * sizeof(int2), 256);
     pl->ws_ml = align_up(slots * H * sizeof(float2), 256);
     pl->ws_acc = align_up(slots * H * a->head_dim * sizeof(float), 256);
-    pl->ws_total = pl->ws_counters + pl->ws_ml + pl->ws_acc;
+    pl->ws_total = pl->ws_info + pl->ws_ml + pl->ws_acc;
     return B2_OK;
 }
 
-template <typename T, int DH, int QG, typename OutT>
-int launch_attn_t(const AttnPlan& pl, cudaStream_t stream) {
-    constexpr int MAXT = kAttnMaxThreads;
-    auto kern = paged_decode_kernel<T, DH, QG, OutT, MAXT>;
-    static std::atomic<uint64_t> smem_set{0};  // one flag word per instantiation
-    int dev = -1;
-    const DeviceInfo di = device_info(&dev);
-    const int rc = ensure_max_smem(kern, smem_set, dev, di.max_smem_optin);
-    if (rc != B2_OK) return rc;
-    // Programmatic dependent launch (the kernel waits on griddepcontrol.wait
-    // before reading its inputs), so its launch overlaps the previous kernel's tail.
+// Launch with programmatic dependent launch: the kernel waits on
+// griddepcontrol.wait before reading what the kernel before it wrote, so its
+// launch and set-up overlap that kernel's tail.
+template <typename K, typename P>
+int launch_pdl(K kern, dim3 grid, dim3 block, int smem, cudaStream_t stream, const P& prm) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
-    cfg.blockDim = dim3(static_cast<unsigned>(pl.threads));
-    cfg.dynamicSmemBytes = static_cast<size_t>(pl.smem);
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, pl.prm);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
     if (e != cudaSuccess) {
         cudaGetLastError();
         g_last_error = cudaGetErrorString(e);
@@ -225,34 +218,61 @@ int launch_attn_t(const AttnPlan& pl, cudaStream_t stream) {
     return launch_status();
 }
 
-template <typename T, typename OutT>
+template <typename T, int DH, int QG>
+int launch_attn_t(const AttnPlan& pl, cudaStream_t stream) {
+    constexpr int MAXT = kAttnMaxThreads;
+    auto kern = paged_decode_kernel<T, DH, QG, MAXT>;
+    static std::atomic<uint64_t> smem_set{0};  // one flag word per instantiation
+    int dev = -1;
+    const DeviceInfo di = device_info(&dev);
+    const int rc = ensure_max_smem(kern, smem_set, dev, di.max_smem_optin);
+    if (rc != B2_OK) return rc;
+    return launch_pdl(kern, dim3(static_cast<unsigned>(pl.grid)), dim3(static_cast<unsigned>(pl.threads)), pl.smem,
+                      stream, pl.prm);
+}
+
+template <typename T>
 int launch_attn_dh(const AttnPlan& pl, int dh, int qg, cudaStream_t s) {
     if (dh == 64) {
         switch (qg) {
-            case 1: return launch_attn_t<T, 64, 1, OutT>(pl, s);
-            case 2: return launch_attn_t<T, 64, 2, OutT>(pl, s);
-            case 4: return launch_attn_t<T, 64, 4, OutT>(pl, s);
+            case 1: return launch_attn_t<T, 64, 1>(pl, s);
+            case 2: return launch_attn_t<T, 64, 2>(pl, s);
+            case 4: return launch_attn_t<T, 64, 4>(pl, s);
             case 8:
-                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 64, 8, OutT>(pl, s);
+                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 64, 8>(pl, s);
                 break;
         }
     } else {
         switch (qg) {
-            case 1: return launch_attn_t<T, 128, 1, OutT>(pl, s);
-            case 2: return launch_attn_t<T, 128, 2, OutT>(pl, s);
-            case 4: return launch_attn_t<T, 128, 4, OutT>(pl, s);
+            case 1: return launch_attn_t<T, 128, 1>(pl, s);
+            case 2: return launch_attn_t<T, 128, 2>(pl, s);
+            case 4: return launch_attn_t<T, 128, 4>(pl, s);
             case 8:
-                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 128, 8, OutT>(pl, s);
+                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 128, 8>(pl, s);
                 break;
         }
     }
     return fail(B2_ERR_UNSUPPORTED, "no kernel for this head shape");
 }
 
-template <typename T>
-int launch_attn_out(const AttnPlan& pl, int out_f32, int dh, int qg, cudaStream_t s) {
-    if (out_f32) return launch_attn_dh<T, float>(pl, dh, qg, s);
-    return launch_attn_dh<T, T>(pl, dh, qg, s);
+template <int DH, int E>
+int launch_combine_out(const CombineParams& c, int out_dtype, int batch, int threads, cudaStream_t s) {
+    const dim3 grid(static_cast<unsigned>(batch)), block(static_cast<unsigned>(threads));
+    if (out_dtype == B2_F32) return launch_pdl(paged_decode_combine_kernel<DH, E, float>, grid, block, 0, s, c);
+    if constexpr (E == 8) {  // 16-bit outputs only come with 16-bit inputs (8 elements per chunk)
+        if (out_dtype == B2_F16) return launch_pdl(paged_decode_combine_kernel<DH, E, __half>, grid, block, 0, s, c);
+        return launch_pdl(paged_decode_combine_kernel<DH, E, __nv_bfloat16>, grid, block, 0, s, c);
+    }
+    return fail(B2_ERR_DTYPE, "16-bit output needs 16-bit inputs");
+}
+
+int launch_combine(const CombineParams& c, int dtype, int out_dtype, int dh, int batch, int threads,
+                   cudaStream_t s) {
+    const int E = 16 / dtype_size(dtype);
+    if (dh == 64) return E == 8 ? launch_combine_out<64, 8>(c, out_dtype, batch, threads, s)
+                                : launch_combine_out<64, 4>(c, out_dtype, batch, threads, s);
+    return E == 8 ? launch_combine_out<128, 8>(c, out_dtype, batch, threads, s)
+                  : launch_combine_out<128, 4>(c, out_dtype, batch, threads, s);
 }
 
 // Row-kernel grid: grid-stride loops over 16-byte chunks, a few waves of CTAs.
@@ -348,22 +368,6 @@ size_t b2_paged_attention_workspace_bytes(const B2PagedAttnArgs* a) {
     return pl.ws_total;
 }
 
-int b2_paged_attention_workspace_init(void* ws, size_t ws_bytes, const B2PagedAttnArgs* a, b2_stream_t stream) {
-    int rc = check_attn_args(a);
-    if (rc != B2_OK) return rc;
-    if (a->batch == 0) return B2_OK;
-    AttnPlan pl;
-    rc = plan_attention(a, &pl);
-    if (rc != B2_OK) return rc;
-    if (ws == nullptr || ws_bytes < pl.ws_total) return fail(B2_ERR_WORKSPACE, "workspace missing or too small");
-    const cudaError_t e = cudaMemsetAsync(ws, 0, pl.ws_counters, static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) {
-        g_last_error = cudaGetErrorString(e);
-        return static_cast<int>(e);
-    }
-    return B2_OK;
-}
-
 int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_stream_t stream) {
     int rc = check_attn_args(a);
     if (rc != B2_OK) return rc;
@@ -380,7 +384,6 @@ int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_s
     p.pool = a->kv_pool;
     p.block_tables = a->block_tables;
     p.seq_lens = a->seq_lens;
-    p.out = a->out;
     p.batch = a->batch;
     p.n_head = a->n_head;
     p.n_kv_head = a->n_kv_head;
@@ -391,15 +394,23 @@ int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_s
     const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     p.scale_log2 = scale * 1.4426950408889634f;
     char* base = static_cast<char*>(ws);
-    p.counters = reinterpret_cast<unsigned int*>(base);
-    p.part_ml = reinterpret_cast<float2*>(base + pl.ws_counters);
-    p.part_acc = reinterpret_cast<float*>(base + pl.ws_counters + pl.ws_ml);
+    p.seq_info = reinterpret_cast<int2*>(base);
+    p.part_ml = reinterpret_cast<float2*>(base + pl.ws_info);
+    p.part_acc = reinterpret_cast<float*>(base + pl.ws_info + pl.ws_ml);
     const int qg = a->n_head / a->n_kv_head;
-    const int out_f32 = a->out_dtype == B2_F32 && a->dtype != B2_F32;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (a->dtype == B2_F32) return launch_attn_dh<float, float>(pl, a->head_dim, qg, s);
-    if (a->dtype == B2_F16) return launch_attn_out<__half>(pl, out_f32, a->head_dim, qg, s);
-    return launch_attn_out<__nv_bfloat16>(pl, out_f32, a->head_dim, qg, s);
+    if (a->dtype == B2_F32) rc = launch_attn_dh<float>(pl, a->head_dim, qg, s);
+    else if (a->dtype == B2_F16) rc = launch_attn_dh<__half>(pl, a->head_dim, qg, s);
+    else rc = launch_attn_dh<__nv_bfloat16>(pl, a->head_dim, qg, s);
+    if (rc != B2_OK) return rc;
+    CombineParams cp;
+    cp.seq_info = p.seq_info;
+    cp.part_ml = p.part_ml;
+    cp.part_acc = p.part_acc;
+    cp.out = a->out;
+    cp.n_head = a->n_head;
+    cp.ksplit = p.ksplit;
+    return launch_combine(cp, a->dtype, a->out_dtype, a->head_dim, a->batch, pl.combine_threads, s);
 }
 
 // ------------------------------------------------------------ row kernels
