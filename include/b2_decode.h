@@ -160,6 +160,32 @@ B2_API int b2_paged_attention(const B2PagedAttnArgs* args, void* workspace, size
                               b2_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Paged decode attention without any device allocation.
+ * No counterpart in the reference: it exists for callers that cannot allocate
+ * device memory when they run attention -- for example a plugin whose host
+ * runtime owns all device memory through its own pool and forbids allocation
+ * outside it, or a hard real-time decode loop that cannot take cudaMalloc's
+ * implicit device synchronisation and unbounded latency.
+ *
+ * Same arguments and results as b2_paged_attention, but the workspace is a
+ * fixed array of B2_NOALLOC_SCRATCH_BYTES compiled into the library: every GPU
+ * that loads the library holds it until the process exits.  Shapes whose
+ * workspace (b2_paged_attention_workspace_bytes) exceeds it are rejected with
+ * B2_ERR_WORKSPACE before anything is launched.
+ *
+ * The first call on a device looks up the array's device address for that
+ * device (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls share the one array, and each call fully rewrites the
+ * part it reads before reading it, so nothing needs clearing -- but calls
+ * whose kernels overlap on the GPU (different streams, no ordering between
+ * them) race on it: order them on one stream, or use b2_paged_attention with
+ * a workspace per stream.
+ * ---------------------------------------------------------------------- */
+#define B2_NOALLOC_SCRATCH_BYTES (4u << 20) /* 4 MiB */
+
+B2_API int b2_paged_attention_noalloc(const B2PagedAttnArgs* args, b2_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Row kernels around attention.  All take dtype (f32 / f16 / bf16),
  * compute in fp32, and accept out == x (in place).
  * ---------------------------------------------------------------------- */

@@ -413,6 +413,57 @@ int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_s
     return launch_combine(cp, a->dtype, a->out_dtype, a->head_dim, a->batch, pl.combine_threads, s);
 }
 
+}  // extern "C"
+
+// --------------------------------------- attention with a built-in workspace
+// For callers that may not allocate device memory on their decode path (a
+// plugin whose host runtime owns all device memory through its own pool, a
+// hard real-time loop that cannot take cudaMalloc's implicit synchronisation),
+// the workspace can come from this fixed array instead.  It is part of the
+// module, so every device that loads the library holds it until exit.  Host
+// code must not pass `g_noalloc_scratch` itself to a kernel: on the host that
+// name is only a stand-in for the symbol; the device address comes from
+// cudaGetSymbolAddress, looked up once per device below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[B2_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+struct NoAllocScratch {
+    std::once_flag once;
+    void* ptr = nullptr;
+    cudaError_t err = cudaSuccess;
+};
+NoAllocScratch g_noalloc_devices[64];
+}  // namespace
+
+extern "C" int b2_paged_attention_noalloc(const B2PagedAttnArgs* a, b2_stream_t stream) {
+    int rc = check_attn_args(a);
+    if (rc != B2_OK) return rc;
+    if (a->batch == 0) return B2_OK;
+    AttnPlan pl;
+    rc = plan_attention(a, &pl);
+    if (rc != B2_OK) return rc;
+    if (pl.ws_total > B2_NOALLOC_SCRATCH_BYTES) {
+        char msg[200];
+        std::snprintf(msg, sizeof(msg),
+                      "this shape needs a %zu-byte workspace, more than the %u-byte built-in scratch of "
+                      "b2_paged_attention_noalloc; use b2_paged_attention with a caller-provided workspace",
+                      pl.ws_total, static_cast<unsigned>(B2_NOALLOC_SCRATCH_BYTES));
+        return fail(B2_ERR_WORKSPACE, msg);
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(B2_ERR_DEVICE, "no current CUDA device");
+    // First call on this device: its address of the array (the device is current here).
+    NoAllocScratch& s = g_noalloc_devices[dev];
+    std::call_once(s.once, [&s]() { s.err = cudaGetSymbolAddress(&s.ptr, g_noalloc_scratch); });
+    if (s.err != cudaSuccess || s.ptr == nullptr) {
+        g_last_error = std::string("cudaGetSymbolAddress for the built-in scratch failed: ") + cudaGetErrorString(s.err);
+        return s.err != cudaSuccess ? static_cast<int>(s.err) : B2_ERR_DEVICE;
+    }
+    return b2_paged_attention(a, s.ptr, B2_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+extern "C" {
+
 // ------------------------------------------------------------ row kernels
 
 int b2_add_layernorm(int32_t dtype, void* out, void* residual_out, const void* x, const void* bias,
