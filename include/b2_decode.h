@@ -192,7 +192,7 @@ B2_API int b2_paged_attention_noalloc(const B2PagedAttnArgs* args, b2_stream_t s
 
 /* Fused residual add + LayerNorm.  Replaces kernels::launch_add_layernorm
  * (kernels.h:39-44, layernorm.cu:56-63):
- *   r = x + residual_in (+ bias when bias != NULL);  residual_out = r;
+ *   r = residual_in + (x + bias)  (x, bias optional);  residual_out = r;
  *   out = (r - mean(r)) / sqrt(var(r) + eps) * gamma + beta.
  * Statistics are taken over the unrounded fp32 r.  x may be NULL (adds zero),
  * replacing the reference's persistent zero buffer (engine.cu:97). */

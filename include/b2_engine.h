@@ -1,0 +1,121 @@
+/*
+ * b2_engine.h -- C-ABI of the GPT-2 decode engine (libb2engine.so).
+ *
+ * The decode-step orchestration of kanish10/LLM-Inference-Server's gpu-engine
+ * (Engine / Engine::Impl, gpu-engine/include/engine/engine_api.h:9-48 and
+ * gpu-engine/src/engine.cu:71-388), rebuilt over the sm_100a kernels of
+ * libb2decode.so and cuBLAS.  The same life cycle and the same calls:
+ * create (init) -> add_sequence -> decode_step ... -> free_sequence, with
+ * free_blocks() for admission control and a CUDA-graph switch.  Differences:
+ * a dtype per engine (f32 / f16 / bf16; the reference is f16 only), status
+ * codes instead of exceptions, and two bench hooks (synthetic weights made on
+ * the device, sequences whose context is treated as already cached).
+ *
+ * include/b2_engine_api.hpp wraps this in a C++ class with the reference's
+ * Engine signatures.  Every call that takes an engine runs on that engine's
+ * device and stream; one engine must not be used from two threads at once.
+ */
+#ifndef B2_ENGINE_H
+#define B2_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "b2_decode.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct b2_engine b2_engine;
+
+/* gpu-engine/include/engine/engine_api.h:9-13 (EngineConfig) plus the dtype,
+ * the graph switch (Engine::set_use_cuda_graphs) and the device. */
+typedef struct B2EngineConfig {
+    int32_t max_batch;       /* largest batch decode_step accepts */
+    int32_t max_seq_len;     /* positions per sequence (<= n_ctx) */
+    int32_t kv_block_budget; /* KV pool size in 16-token blocks */
+    int32_t dtype;           /* b2_dtype of weights, activations and KV */
+    int32_t use_cuda_graphs; /* 1: capture and replay one graph per batch bucket */
+    int32_t device;          /* CUDA device ordinal; -1 = the current device */
+} B2EngineConfig;
+
+/* gpu-engine/include/engine/model.h:7-18 (GPT2Config). */
+typedef struct B2ModelShape {
+    int32_t n_layer;
+    int32_t n_head;
+    int32_t d_model;
+    int32_t vocab_size;
+    int32_t n_ctx;
+    float layer_norm_epsilon;
+    int32_t eos_token_id;
+} B2ModelShape;
+
+/* Engine::init (engine.cu:240-294): reads weights_dir/{config.json,
+ * manifest.json, weights.bin} in the reference exporter's format
+ * (gpu-engine/export/export_gpt2.py), checks total_bytes and checksum_sum
+ * like WeightsLoader, converts to cfg->dtype and uploads. */
+B2_API int b2_engine_create(const char* weights_dir, const B2EngineConfig* cfg, b2_engine** out);
+
+/* Bench hook: weights drawn on the device, every matrix, embedding and bias
+ * ~ N(0, std) from a counter-based generator keyed by seed, LayerNorm gamma 1
+ * and beta 0 -- for model sizes where writing weight files is pointless. */
+B2_API int b2_engine_create_synthetic(const B2ModelShape* shape, uint64_t seed, float std,
+                                      const B2EngineConfig* cfg, b2_engine** out);
+
+B2_API void b2_engine_destroy(b2_engine* eng);
+
+/* Engine::add_sequence (engine.cu:296-307): registers a prompt and takes its
+ * first KV block.  Returns a sequence id >= 0, -1 if the pool is exhausted,
+ * or another negative status. */
+B2_API int32_t b2_engine_add_sequence(b2_engine* eng, const int32_t* prompt, int32_t prompt_len);
+
+/* Bench hook: a sequence whose first ctx_len positions count as already
+ * cached (their KV is whatever the pool holds; the pool starts zeroed) and
+ * whose next input token is last_token.  Takes the blocks those positions
+ * need.  Returns an id, -1 when the pool is exhausted, or a status. */
+B2_API int32_t b2_engine_add_sequence_cached(b2_engine* eng, int32_t ctx_len, int32_t last_token);
+
+/* Engine::decode_step (engine.cu:309-377): one token for each listed sequence
+ * -- its next prompt token while it is still inside its prompt, otherwise its
+ * last generated token -- and one next-token id per entry, in order.  A new
+ * block is taken when a sequence crosses a 16-token boundary; running out of
+ * blocks returns B2_ERR_POOL (the reference throws) with nothing launched. */
+B2_API int b2_engine_decode_step(b2_engine* eng, const int32_t* seq_ids, int32_t batch, int32_t* out_next_tokens);
+
+/* Engine::free_sequence: returns the sequence's blocks; unknown ids are ignored. */
+B2_API int b2_engine_free_sequence(b2_engine* eng, int32_t seq_id);
+
+/* Engine::free_blocks: blocks left in the pool. */
+B2_API int64_t b2_engine_free_blocks(const b2_engine* eng);
+
+/* Engine::set_use_cuda_graphs. */
+B2_API int b2_engine_set_use_cuda_graphs(b2_engine* eng, int32_t enabled);
+
+/* The model shape, and the stream every launch of this engine goes to (a
+ * cudaStream_t), for callers that time steps with CUDA events. */
+B2_API int b2_engine_shape(const b2_engine* eng, B2ModelShape* out);
+B2_API int b2_engine_stream(const b2_engine* eng, b2_stream_t* out);
+
+/* Text of the last engine error on the calling thread. */
+B2_API const char* b2_engine_last_error(void);
+
+#define B2_ERR_POOL (-8) /* the KV block pool ran out during decode_step */
+#define B2_ERR_IO (-9)   /* a weight file is missing, short or inconsistent */
+
+/* The engine's paged-block allocator, exposed so its behaviour can be checked
+ * against the reference's BlockPool (gpu-engine/src/kv_cache_pool.cpp:6-28):
+ * LIFO free stack, allocate() -> -1 when empty, free() refuses an id out of
+ * range (returns 1) or not allocated (returns 2). */
+typedef struct b2_block_pool b2_block_pool;
+B2_API b2_block_pool* b2_block_pool_create(int32_t num_blocks);
+B2_API void b2_block_pool_destroy(b2_block_pool* pool);
+B2_API int32_t b2_block_pool_allocate(b2_block_pool* pool);
+B2_API int32_t b2_block_pool_free(b2_block_pool* pool, int32_t block_id);
+B2_API int32_t b2_block_pool_num_free(const b2_block_pool* pool);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2_ENGINE_H */

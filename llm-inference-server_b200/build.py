@@ -79,10 +79,29 @@ def build_engine(verbose: bool = False) -> Path:
                                                            LIB / "libb2decode.so"]
     if _stale(out, deps):
         LIB.mkdir(exist_ok=True)
-        cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-shared", "-o", str(out),
-               *map(str, srcs), "-L", str(LIB), "-lb2decode", "-lcublas", "-Xlinker", "-rpath,$ORIGIN"]
+        cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-I", str(_json_include()),
+               "-shared", "-o", str(out), *map(str, srcs), "-L", str(LIB), "-lb2decode", "-lcublas",
+               "-Xlinker", "-rpath,$ORIGIN"]
         _run(cmd, verbose)
     return out
+
+
+def _json_include() -> Path:
+    """Directory holding nlohmann/json.hpp (header-only; the reference's
+    config / manifest parser).  Looked up in the environment: B2_JSON_INCLUDE,
+    the system include dirs, then copies vendored by installed Python
+    packages."""
+    env = os.environ.get("B2_JSON_INCLUDE")
+    cands = [Path(env)] if env else []
+    cands += [Path("/usr/include"), Path("/usr/local/include")]
+    import site
+    for sp in site.getsitepackages():
+        cands += sorted(Path(sp).glob("include/*/thirdparty"))
+        cands += sorted(Path(sp).glob("*/include"))
+    for c in cands:
+        if (c / "nlohmann" / "json.hpp").exists():
+            return c
+    raise RuntimeError("nlohmann/json.hpp not found; set B2_JSON_INCLUDE to its include directory")
 
 
 def build_all(verbose: bool = False) -> list[Path]:

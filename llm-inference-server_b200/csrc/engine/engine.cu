@@ -1,0 +1,719 @@
+// engine.cu -- GPT-2 decode engine over libb2decode (the sm_100a hot-path
+// kernels) and cuBLAS (the GEMMs); the C-ABI is include/b2_engine.h.
+//
+// Rebuilds Engine / Engine::Impl of gpu-engine/src/engine.cu:71-388 with the
+// same life cycle and the same host flow per decode step (engine.cu:309-377):
+// take KV blocks at 16-token boundaries, build token ids / positions /
+// seq_lens / block tables for the batch bucket (pad lanes replay the last
+// real lane), upload, run the step (a captured CUDA graph per bucket, or
+// direct launches), download the next tokens, synchronise.  What differs:
+//   * one packed upload per step instead of four copies;
+//   * the per-layer sequence fuses the reference's bias / add_one launches
+//     into neighbours: LN1(+fc_proj bias of the previous layer) -> QKV GEMM ->
+//     kv_append(+k,v bias, seq_lens+1) -> paged attention(+q bias) -> proj
+//     GEMM -> LN2(+proj bias) -> fc GEMM -> bias+GELU -> fc_proj GEMM;
+//     final LN(+fc_proj bias) -> tied lm_head GEMM -> argmax
+//     (reference: engine.cu:150-204, eleven launches per layer vs eight here);
+//   * f32 / f16 / bf16 storage with fp32 accumulation everywhere (the f32
+//     engine uses CUBLAS_COMPUTE_32F under pedantic math: no TF32);
+//   * capacity is checked before anything changes, so an exhausted pool
+//     returns B2_ERR_POOL instead of throwing half-way (engine.cu:227-233).
+#include <cublas_v2.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <nlohmann/json.hpp>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "b2_decode.h"
+#include "b2_engine.h"
+#include "block_pool.h"
+
+namespace b2 {
+namespace eng {
+
+thread_local std::string g_err;
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+void cuda_ok(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw Error(static_cast<int>(e), std::string(what) + ": " + cudaGetErrorString(e));
+}
+void cublas_ok(cublasStatus_t s, const char* what) {
+    if (s != CUBLAS_STATUS_SUCCESS) throw Error(B2_ERR_DEVICE, std::string(what) + ": cuBLAS status " + std::to_string(s));
+}
+void b2_ok(int rc, const char* what) {
+    if (rc != B2_OK) throw Error(rc, std::string(what) + ": " + b2_last_error_string());
+}
+
+int dtype_bytes(int dt) { return dt == B2_F32 ? 4 : 2; }
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// ------------------------------------------------------ synthetic weights
+// splitmix64 of (seed, tensor, index) -> two uniforms -> Box-Muller normal.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+template <typename T>
+__global__ void synth_normal_kernel(T* dst, size_t n, uint64_t key, float stdev) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint64_t r = mix64(key ^ mix64(i));
+        const float u1 = (static_cast<float>(r >> 40) + 1.0f) * (1.0f / 16777217.0f);  // (0, 1]
+        const float u2 = static_cast<float>((r >> 16) & 0xffffffu) * (1.0f / 16777216.0f);
+        const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+        dst[i] = static_cast<T>(z * stdev);
+    }
+}
+
+template <typename T>
+__global__ void fill_kernel(T* dst, size_t n, float v) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        dst[i] = static_cast<T>(v);
+}
+
+// ------------------------------------------------------------- the engine
+
+struct LayerW {
+    const void *ln1_g, *ln1_b, *qkv_w, *qkv_b, *proj_w, *proj_b, *ln2_g, *ln2_b, *fc_w, *fc_b, *fc_proj_w, *fc_proj_b;
+};
+
+struct Seq {
+    BlockTable table;
+    int seq_len = 0;  // positions already in the KV cache
+    std::vector<int32_t> prompt;
+    int prompt_pos = 0;
+    int32_t last_token = 0;
+};
+
+// Tensor list in the exporter's file order (gpu-engine/src/loader.cpp:28-47).
+struct TensorSpec {
+    std::string name;
+    std::vector<int64_t> shape;
+    int init;  // 0 normal, 1 ones, 2 zeros
+};
+
+std::vector<TensorSpec> tensor_specs(const B2ModelShape& s) {
+    const int64_t D = s.d_model, V = s.vocab_size;
+    std::vector<TensorSpec> t = {{"wte", {V, D}, 0}, {"wpe", {s.n_ctx, D}, 0}};
+    for (int i = 0; i < s.n_layer; ++i) {
+        const std::string p = "layer" + std::to_string(i) + ".";
+        t.push_back({p + "ln1_g", {D}, 1});
+        t.push_back({p + "ln1_b", {D}, 2});
+        t.push_back({p + "qkv_w", {3 * D, D}, 0});
+        t.push_back({p + "qkv_b", {3 * D}, 0});
+        t.push_back({p + "proj_w", {D, D}, 0});
+        t.push_back({p + "proj_b", {D}, 0});
+        t.push_back({p + "ln2_g", {D}, 1});
+        t.push_back({p + "ln2_b", {D}, 2});
+        t.push_back({p + "fc_w", {4 * D, D}, 0});
+        t.push_back({p + "fc_b", {4 * D}, 0});
+        t.push_back({p + "fc_proj_w", {D, 4 * D}, 0});
+        t.push_back({p + "fc_proj_b", {D}, 0});
+    }
+    t.push_back({"lnf_g", {D}, 1});
+    t.push_back({"lnf_b", {D}, 2});
+    return t;
+}
+
+size_t numel(const std::vector<int64_t>& shape) {
+    size_t n = 1;
+    for (auto d : shape) n *= static_cast<size_t>(d);
+    return n;
+}
+
+struct Engine {
+    B2ModelShape shape{};
+    B2EngineConfig cfg{};
+    int dt = B2_F16, es = 2, device = 0, head_dim = 0, mbps = 0, bucket_cap = 0;
+    void* weights = nullptr;
+    std::vector<const void*> tensor_ptrs;
+    const void *wte = nullptr, *wpe = nullptr, *lnf_g = nullptr, *lnf_b = nullptr;
+    std::vector<LayerW> layers;
+    void* pool = nullptr;
+    int num_blocks = 0;
+    std::unique_ptr<BlockPool> blocks;
+    cudaStream_t stream = nullptr;
+    cublasHandle_t cublas = nullptr;
+    void* cublas_ws = nullptr;
+    // Per-step buffers at fixed addresses (CUDA graphs replay them).
+    int32_t *d_in = nullptr, *d_seq_post = nullptr, *d_next = nullptr;
+    int32_t *h_in = nullptr, *h_next = nullptr;  // pinned
+    void *d_resid = nullptr, *d_x = nullptr, *d_qkv = nullptr, *d_attn = nullptr, *d_attn_out = nullptr,
+         *d_ff = nullptr, *d_ff_out = nullptr, *d_logits = nullptr;
+    void* attn_ws = nullptr;
+    size_t attn_ws_bytes = 0;
+    std::unordered_map<int, Seq> seqs;
+    int next_id = 0;
+    bool use_graphs = true;
+    std::map<int, cudaGraphExec_t> graphs;
+
+    int32_t* in_tokens() const { return d_in; }
+    int32_t* in_positions() const { return d_in + cfg.max_batch; }
+    int32_t* in_seq_lens() const { return d_in + 2 * cfg.max_batch; }
+    int32_t* in_tables() const { return d_in + 3 * cfg.max_batch; }
+
+    ~Engine() {
+        if (device >= 0) cudaSetDevice(device);
+        for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+        if (cublas) cublasDestroy(cublas);
+        if (stream) cudaStreamDestroy(stream);
+        void* dev_ptrs[] = {weights, pool, cublas_ws, d_in, d_seq_post, d_next, d_resid, d_x, d_qkv,
+                            d_attn, d_attn_out, d_ff, d_ff_out, d_logits, attn_ws};
+        for (void* p : dev_ptrs)
+            if (p) cudaFree(p);
+        if (h_in) cudaFreeHost(h_in);
+        if (h_next) cudaFreeHost(h_next);
+    }
+
+    void check_shape() {
+        const B2ModelShape& s = shape;
+        if (s.n_layer <= 0 || s.n_head <= 0 || s.d_model <= 0 || s.d_model % s.n_head || s.vocab_size <= 0 ||
+            s.n_ctx <= 0)
+            throw Error(B2_ERR_SHAPE, "invalid model shape");
+        head_dim = s.d_model / s.n_head;
+        if (head_dim != 64 && head_dim != 128) throw Error(B2_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+        if (cfg.max_batch <= 0 || cfg.max_seq_len <= 0 || cfg.max_seq_len > s.n_ctx || cfg.kv_block_budget <= 0)
+            throw Error(B2_ERR_SHAPE, "invalid engine config (max_batch, max_seq_len <= n_ctx, kv_block_budget)");
+        if (cfg.dtype != B2_F32 && cfg.dtype != B2_F16 && cfg.dtype != B2_BF16) throw Error(B2_ERR_DTYPE, "unknown dtype");
+    }
+
+    // Weight arena: every tensor at a 256-byte aligned offset, in file order.
+    std::vector<size_t> layout(const std::vector<TensorSpec>& specs, size_t* total) const {
+        std::vector<size_t> off;
+        size_t o = 0;
+        for (const auto& t : specs) {
+            off.push_back(o);
+            o = align256(o + numel(t.shape) * es);
+        }
+        *total = o;
+        return off;
+    }
+
+    void bind_tensors(const std::vector<size_t>& off) {
+        auto at = [&](size_t i) { return static_cast<const void*>(static_cast<char*>(weights) + off[i]); };
+        size_t i = 0;
+        wte = at(i++);
+        wpe = at(i++);
+        layers.resize(static_cast<size_t>(shape.n_layer));
+        for (auto& l : layers) {
+            l.ln1_g = at(i++);
+            l.ln1_b = at(i++);
+            l.qkv_w = at(i++);
+            l.qkv_b = at(i++);
+            l.proj_w = at(i++);
+            l.proj_b = at(i++);
+            l.ln2_g = at(i++);
+            l.ln2_b = at(i++);
+            l.fc_w = at(i++);
+            l.fc_b = at(i++);
+            l.fc_proj_w = at(i++);
+            l.fc_proj_b = at(i++);
+        }
+        lnf_g = at(i++);
+        lnf_b = at(i++);
+    }
+
+    void setup_device() {
+        if (cfg.device >= 0) cuda_ok(cudaSetDevice(cfg.device), "cudaSetDevice");
+        cuda_ok(cudaGetDevice(&device), "cudaGetDevice");
+        dt = cfg.dtype;
+        es = dtype_bytes(dt);
+        use_graphs = cfg.use_cuda_graphs != 0;
+        cuda_ok(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        cublas_ok(cublasCreate(&cublas), "cublasCreate");
+        cublas_ok(cublasSetStream(cublas, stream), "cublasSetStream");
+        // A fixed cuBLAS workspace keeps GEMMs capturable in CUDA graphs.
+        const size_t ws = 32u << 20;
+        cuda_ok(cudaMalloc(&cublas_ws, ws), "malloc cublas workspace");
+        cublas_ok(cublasSetWorkspace(cublas, cublas_ws, ws), "cublasSetWorkspace");
+        cublas_ok(cublasSetMathMode(cublas, dt == B2_F32 ? CUBLAS_PEDANTIC_MATH : CUBLAS_DEFAULT_MATH),
+                  "cublasSetMathMode");
+    }
+
+    void setup_buffers() {
+        const int B = cfg.max_batch, D = shape.d_model, V = shape.vocab_size;
+        mbps = (cfg.max_seq_len + B2_BLOCK_TOKENS - 1) / B2_BLOCK_TOKENS;
+        num_blocks = cfg.kv_block_budget;
+        const size_t block_bytes =
+            static_cast<size_t>(shape.n_layer) * 2 * B2_BLOCK_TOKENS * shape.n_head * head_dim * es;
+        cuda_ok(cudaMalloc(&pool, block_bytes * num_blocks), "malloc KV pool");
+        cuda_ok(cudaMemsetAsync(pool, 0, block_bytes * num_blocks, stream), "memset KV pool");
+        blocks = std::make_unique<BlockPool>(num_blocks);
+        const size_t in_ints = 3 * static_cast<size_t>(B) + static_cast<size_t>(B) * mbps;
+        cuda_ok(cudaMalloc(&d_in, in_ints * 4), "malloc step inputs");
+        cuda_ok(cudaMemsetAsync(d_in, 0, in_ints * 4, stream), "memset step inputs");
+        cuda_ok(cudaMallocHost(&h_in, in_ints * 4), "pinned step inputs");
+        std::memset(h_in, 0, in_ints * 4);
+        cuda_ok(cudaMalloc(&d_seq_post, B * 4), "malloc seq_lens_post");
+        cuda_ok(cudaMalloc(&d_next, B * 4), "malloc next tokens");
+        cuda_ok(cudaMallocHost(&h_next, B * 4), "pinned next tokens");
+        auto act = [&](void** p, size_t cols, const char* what) { cuda_ok(cudaMalloc(p, static_cast<size_t>(B) * cols * es), what); };
+        act(&d_resid, D, "malloc residual");
+        act(&d_x, D, "malloc ln out");
+        act(&d_qkv, 3 * static_cast<size_t>(D), "malloc qkv");
+        act(&d_attn, D, "malloc attention out");
+        act(&d_attn_out, D, "malloc proj out");
+        act(&d_ff, 4 * static_cast<size_t>(D), "malloc ff");
+        act(&d_ff_out, D, "malloc ff out");
+        act(&d_logits, V, "malloc logits");
+        B2PagedAttnArgs a = attn_args(B, 0);
+        attn_ws_bytes = b2_paged_attention_workspace_bytes(&a);
+        if (attn_ws_bytes == 0) throw Error(B2_ERR_UNSUPPORTED, std::string("attention shape: ") + b2_last_error_string());
+        cuda_ok(cudaMalloc(&attn_ws, attn_ws_bytes), "malloc attention workspace");
+        bucket_cap = B;
+        cuda_ok(cudaStreamSynchronize(stream), "engine set-up");
+    }
+
+    B2PagedAttnArgs attn_args(int bucket, int layer) const {
+        B2PagedAttnArgs a{};
+        a.dtype = dt;
+        a.out_dtype = dt;
+        a.q = d_qkv;
+        a.q_row_stride = 3 * shape.d_model;
+        a.kv_pool = pool;
+        a.block_tables = in_tables();
+        a.seq_lens = d_seq_post;
+        a.out = d_attn;
+        a.batch = bucket;
+        a.n_head = shape.n_head;
+        a.n_kv_head = shape.n_head;
+        a.head_dim = head_dim;
+        a.max_blocks_per_seq = mbps;
+        a.layer_idx = layer;
+        a.n_layer = shape.n_layer;
+        a.num_blocks = num_blocks;
+        return a;
+    }
+
+    // Row-major Y[batch, O] = X[batch, I] . W^T with W row-major [O, I]: the
+    // convention of gpu-engine/include/engine/kernels.h:9-20.
+    void gemm(int batch, int I, int O, const void* X, const void* W, void* Y) {
+        const float alpha = 1.0f, beta = 0.0f;
+        const cudaDataType_t t = dt == B2_F32 ? CUDA_R_32F : (dt == B2_F16 ? CUDA_R_16F : CUDA_R_16BF);
+        cublas_ok(cublasGemmEx(cublas, CUBLAS_OP_T, CUBLAS_OP_N, O, batch, I, &alpha, W, t, I, X, t, I, &beta, Y, t, O,
+                               CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
+                  "cublasGemmEx");
+    }
+
+    void run_step_kernels(int bucket) {
+        const int D = shape.d_model, V = shape.vocab_size, L = shape.n_layer;
+        const float eps = shape.layer_norm_epsilon;
+        b2_stream_t s = stream;
+        const char* qkv = static_cast<const char*>(d_qkv);
+        b2_ok(b2_embedding(dt, d_resid, wte, wpe, in_tokens(), in_positions(), bucket, D, V, shape.n_ctx, s), "embedding");
+        const void* delta = nullptr;
+        const void* delta_bias = nullptr;
+        for (int l = 0; l < L; ++l) {
+            const LayerW& w = layers[static_cast<size_t>(l)];
+            b2_ok(b2_add_layernorm(dt, d_x, d_resid, delta, delta_bias, d_resid, w.ln1_g, w.ln1_b, bucket, D, eps, s), "ln1");
+            gemm(bucket, D, 3 * D, d_x, w.qkv_w, d_qkv);
+            B2KvAppendArgs ka{};
+            ka.dtype = dt;
+            ka.kv_pool = pool;
+            ka.k = qkv + static_cast<size_t>(D) * es;
+            ka.v = qkv + 2 * static_cast<size_t>(D) * es;
+            ka.kv_row_stride = 3 * D;
+            ka.k_bias = static_cast<const char*>(w.qkv_b) + static_cast<size_t>(D) * es;
+            ka.v_bias = static_cast<const char*>(w.qkv_b) + 2 * static_cast<size_t>(D) * es;
+            ka.block_tables = in_tables();
+            ka.seq_lens = in_seq_lens();
+            ka.seq_lens_post = l == 0 ? d_seq_post : nullptr;  // same for every layer
+            ka.batch = bucket;
+            ka.n_kv_head = shape.n_head;
+            ka.head_dim = head_dim;
+            ka.max_blocks_per_seq = mbps;
+            ka.layer_idx = l;
+            ka.n_layer = L;
+            ka.num_blocks = num_blocks;
+            b2_ok(b2_kv_append(&ka, s), "kv_append");
+            B2PagedAttnArgs aa = attn_args(bucket, l);
+            aa.q_bias = w.qkv_b;
+            b2_ok(b2_paged_attention(&aa, attn_ws, attn_ws_bytes, s), "paged_attention");
+            gemm(bucket, D, D, d_attn, w.proj_w, d_attn_out);
+            b2_ok(b2_add_layernorm(dt, d_x, d_resid, d_attn_out, w.proj_b, d_resid, w.ln2_g, w.ln2_b, bucket, D, eps, s), "ln2");
+            gemm(bucket, D, 4 * D, d_x, w.fc_w, d_ff);
+            b2_ok(b2_bias_gelu(dt, d_ff, d_ff, w.fc_b, bucket, 4 * D, s), "bias_gelu");
+            gemm(bucket, 4 * D, D, d_ff, w.fc_proj_w, d_ff_out);
+            delta = d_ff_out;
+            delta_bias = w.fc_proj_b;
+        }
+        b2_ok(b2_add_layernorm(dt, d_x, d_resid, delta, delta_bias, d_resid, lnf_g, lnf_b, bucket, D, eps, s), "ln_f");
+        gemm(bucket, D, V, d_x, wte, d_logits);  // lm_head tied to wte
+        b2_ok(b2_argmax(dt, d_next, d_logits, bucket, V, s), "argmax");
+    }
+
+    cudaGraphExec_t graph_for(int bucket) {
+        auto it = graphs.find(bucket);
+        if (it != graphs.end()) return it->second;
+        cudaGraph_t g = nullptr;
+        cuda_ok(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+        try {
+            run_step_kernels(bucket);
+        } catch (...) {
+            cudaStreamEndCapture(stream, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        cuda_ok(cudaStreamEndCapture(stream, &g), "cudaStreamEndCapture");
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        cuda_ok(e, "cudaGraphInstantiate");
+        graphs[bucket] = exec;
+        return exec;
+    }
+
+    // Batch buckets 1, 2, 4, ... up to max_batch (the reference stops at 8,
+    // engine.cu:52-59, and pads everything larger to max_batch).
+    int pick_bucket(int batch) const {
+        int b = 1;
+        while (b < batch) b <<= 1;
+        return b < cfg.max_batch ? b : cfg.max_batch;
+    }
+
+    void decode_step(const int32_t* ids, int batch, int32_t* out) {
+        if (batch <= 0 || batch > cfg.max_batch) throw Error(B2_ERR_SHAPE, "batch must be in [1, max_batch]");
+        std::vector<Seq*> sv(static_cast<size_t>(batch));
+        int need = 0;
+        for (int i = 0; i < batch; ++i) {
+            auto it = seqs.find(ids[i]);
+            if (it == seqs.end()) throw Error(B2_ERR_SHAPE, "unknown sequence id " + std::to_string(ids[i]));
+            Seq& q = it->second;
+            if (q.seq_len >= cfg.max_seq_len) throw Error(B2_ERR_SHAPE, "sequence " + std::to_string(ids[i]) + " reached max_seq_len");
+            for (int j = 0; j < i; ++j)
+                if (sv[static_cast<size_t>(j)] == &q) throw Error(B2_ERR_SHAPE, "sequence listed twice in one step");
+            sv[static_cast<size_t>(i)] = &q;
+            if (static_cast<int>(q.table.ids.size()) * B2_BLOCK_TOKENS <= q.seq_len) ++need;
+        }
+        if (need > blocks->num_free()) throw Error(B2_ERR_POOL, "KV cache block pool exhausted");
+        const int bucket = pick_bucket(batch);
+        const int B = cfg.max_batch;
+        int32_t* tok = h_in;
+        int32_t* pos = h_in + B;
+        int32_t* sl = h_in + 2 * B;
+        int32_t* bt = h_in + 3 * B;
+        for (int i = 0; i < batch; ++i) {
+            Seq& q = *sv[static_cast<size_t>(i)];
+            if (static_cast<int>(q.table.ids.size()) * B2_BLOCK_TOKENS <= q.seq_len) q.table.ids.push_back(blocks->allocate());
+            tok[i] = q.prompt_pos < static_cast<int>(q.prompt.size()) ? q.prompt[static_cast<size_t>(q.prompt_pos)] : q.last_token;
+            pos[i] = q.seq_len;
+            sl[i] = q.seq_len;
+            int32_t* row = bt + static_cast<size_t>(i) * mbps;
+            for (size_t j = 0; j < q.table.ids.size(); ++j) row[j] = q.table.ids[j];
+        }
+        for (int i = batch; i < bucket; ++i) {  // pad lanes replay the last real lane
+            tok[i] = tok[batch - 1];
+            pos[i] = pos[batch - 1];
+            sl[i] = sl[batch - 1];
+            std::memcpy(bt + static_cast<size_t>(i) * mbps, bt + static_cast<size_t>(batch - 1) * mbps, mbps * 4);
+        }
+        const size_t up = (3 * static_cast<size_t>(B) + static_cast<size_t>(bucket) * mbps) * 4;
+        cuda_ok(cudaMemcpyAsync(d_in, h_in, up, cudaMemcpyHostToDevice, stream), "upload step inputs");
+        if (use_graphs)
+            cuda_ok(cudaGraphLaunch(graph_for(bucket), stream), "cudaGraphLaunch");
+        else
+            run_step_kernels(bucket);
+        cuda_ok(cudaMemcpyAsync(h_next, d_next, static_cast<size_t>(batch) * 4, cudaMemcpyDeviceToHost, stream),
+                "download next tokens");
+        cuda_ok(cudaStreamSynchronize(stream), "decode step");
+        for (int i = 0; i < batch; ++i) {
+            Seq& q = *sv[static_cast<size_t>(i)];
+            if (q.prompt_pos < static_cast<int>(q.prompt.size())) ++q.prompt_pos;
+            ++q.seq_len;
+            q.last_token = h_next[i];
+            out[i] = h_next[i];
+        }
+    }
+};
+
+// ----------------------------------------------------------- weight files
+
+B2ModelShape read_config(const std::string& dir) {
+    std::ifstream f(dir + "/config.json");
+    if (!f) throw Error(B2_ERR_IO, "cannot open " + dir + "/config.json");
+    nlohmann::json j;
+    f >> j;
+    B2ModelShape s{};
+    s.n_layer = j.at("n_layer").get<int>();
+    s.n_head = j.at("n_head").get<int>();
+    s.d_model = j.at("d_model").get<int>();
+    s.vocab_size = j.at("vocab_size").get<int>();
+    s.n_ctx = j.at("n_ctx").get<int>();
+    s.layer_norm_epsilon = j.at("layer_norm_epsilon").get<float>();
+    s.eos_token_id = j.at("eos_token_id").get<int>();
+    if (j.at("head_dim").get<int>() * s.n_head != s.d_model) throw Error(B2_ERR_IO, "config.json: head_dim * n_head != d_model");
+    return s;
+}
+
+// Reads weights.bin / manifest.json, checks them the way the reference's
+// WeightsLoader does (total_bytes, byte ranges, shapes, the double
+// checksum_sum to 1e-6 relative; weights_loader.cpp:28-71), converts to the
+// engine dtype and uploads into the arena.
+void load_weights(Engine& e, const std::string& dir) {
+    std::ifstream mf(dir + "/manifest.json");
+    if (!mf) throw Error(B2_ERR_IO, "cannot open " + dir + "/manifest.json");
+    nlohmann::json man;
+    mf >> man;
+    std::ifstream wf(dir + "/weights.bin", std::ios::binary | std::ios::ate);
+    if (!wf) throw Error(B2_ERR_IO, "cannot open " + dir + "/weights.bin");
+    const size_t file_bytes = static_cast<size_t>(wf.tellg());
+    wf.seekg(0);
+    if (file_bytes != man.at("total_bytes").get<size_t>()) throw Error(B2_ERR_IO, "weights.bin size differs from manifest total_bytes");
+    std::vector<char> blob(file_bytes);
+    wf.read(blob.data(), static_cast<std::streamsize>(file_bytes));
+    if (!wf) throw Error(B2_ERR_IO, "short read of weights.bin");
+    std::unordered_map<std::string, const nlohmann::json*> by_name;
+    for (const auto& t : man.at("tensors")) by_name[t.at("name").get<std::string>()] = &t;
+
+    const auto specs = tensor_specs(e.shape);
+    size_t total = 0;
+    const auto off = e.layout(specs, &total);
+    cuda_ok(cudaMalloc(&e.weights, total), "malloc weights");
+    char* staging = nullptr;
+    cuda_ok(cudaMallocHost(&staging, total), "pinned weight staging");
+    std::unique_ptr<char, void (*)(char*)> guard(staging, [](char* p) { cudaFreeHost(p); });
+    double checksum = 0.0;
+    for (size_t i = 0; i < specs.size(); ++i) {
+        auto it = by_name.find(specs[i].name);
+        if (it == by_name.end()) throw Error(B2_ERR_IO, "manifest lacks tensor " + specs[i].name);
+        const nlohmann::json& t = *it->second;
+        std::vector<int64_t> shp;
+        for (auto& d : t.at("shape")) shp.push_back(d.get<int64_t>());
+        if (shp != specs[i].shape) throw Error(B2_ERR_IO, "tensor " + specs[i].name + " has an unexpected shape");
+        const size_t o = t.at("byte_offset").get<size_t>(), len = t.at("byte_length").get<size_t>();
+        const size_t n = numel(shp);
+        if (o + len > file_bytes || len != n * 4) throw Error(B2_ERR_IO, "tensor " + specs[i].name + " byte range is inconsistent");
+        const float* src = reinterpret_cast<const float*>(blob.data() + o);
+        char* dst = staging + off[i];
+        for (size_t k = 0; k < n; ++k) checksum += static_cast<double>(src[k]);
+        if (e.dt == B2_F32) {
+            std::memcpy(dst, src, n * 4);
+        } else if (e.dt == B2_F16) {
+            __half* h = reinterpret_cast<__half*>(dst);
+            for (size_t k = 0; k < n; ++k) h[k] = __float2half_rn(src[k]);
+        } else {
+            __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(dst);
+            for (size_t k = 0; k < n; ++k) h[k] = __float2bfloat16_rn(src[k]);
+        }
+    }
+    const double want = man.value("checksum_sum", 0.0);
+    if (std::fabs(checksum - want) / std::max(1.0, std::fabs(want)) > 1e-6)
+        throw Error(B2_ERR_IO, "weight checksum_sum differs from the manifest (corrupt export?)");
+    cuda_ok(cudaMemcpy(e.weights, staging, total, cudaMemcpyHostToDevice), "upload weights");
+    e.bind_tensors(off);
+}
+
+void synth_weights(Engine& e, uint64_t seed, float stdev) {
+    const auto specs = tensor_specs(e.shape);
+    size_t total = 0;
+    const auto off = e.layout(specs, &total);
+    cuda_ok(cudaMalloc(&e.weights, total), "malloc weights");
+    for (size_t i = 0; i < specs.size(); ++i) {
+        void* dst = static_cast<char*>(e.weights) + off[i];
+        const size_t n = numel(specs[i].shape);
+        const uint64_t key = seed * 0x100000001b3ull + i;
+        const int grid = static_cast<int>(std::min<size_t>((n + 255) / 256, 148 * 32));
+        if (e.dt == B2_F32) {
+            if (specs[i].init == 0) synth_normal_kernel<float><<<grid, 256, 0, e.stream>>>(static_cast<float*>(dst), n, key, stdev);
+            else fill_kernel<float><<<grid, 256, 0, e.stream>>>(static_cast<float*>(dst), n, specs[i].init == 1 ? 1.0f : 0.0f);
+        } else if (e.dt == B2_F16) {
+            if (specs[i].init == 0) synth_normal_kernel<__half><<<grid, 256, 0, e.stream>>>(static_cast<__half*>(dst), n, key, stdev);
+            else fill_kernel<__half><<<grid, 256, 0, e.stream>>>(static_cast<__half*>(dst), n, specs[i].init == 1 ? 1.0f : 0.0f);
+        } else {
+            if (specs[i].init == 0)
+                synth_normal_kernel<__nv_bfloat16><<<grid, 256, 0, e.stream>>>(static_cast<__nv_bfloat16*>(dst), n, key, stdev);
+            else
+                fill_kernel<__nv_bfloat16><<<grid, 256, 0, e.stream>>>(static_cast<__nv_bfloat16*>(dst), n,
+                                                                        specs[i].init == 1 ? 1.0f : 0.0f);
+        }
+        cuda_ok(cudaGetLastError(), "synthetic weights");
+    }
+    cuda_ok(cudaStreamSynchronize(e.stream), "synthetic weights");
+    e.bind_tensors(off);
+}
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        return B2_OK;
+    } catch (const Error& err) {
+        g_err = err.what();
+        return err.code;
+    } catch (const std::exception& ex) {
+        g_err = ex.what();
+        return B2_ERR_IO;
+    }
+}
+
+}  // namespace eng
+}  // namespace b2
+
+struct b2_engine : b2::eng::Engine {};
+struct b2_block_pool : b2::BlockPool {
+    explicit b2_block_pool(int n) : b2::BlockPool(n) {}
+};
+
+using b2::eng::Error;
+using b2::eng::guarded;
+
+extern "C" {
+
+const char* b2_engine_last_error(void) { return b2::eng::g_err.c_str(); }
+
+int b2_engine_create(const char* weights_dir, const B2EngineConfig* cfg, b2_engine** out) {
+    if (!weights_dir || !cfg || !out) {
+        b2::eng::g_err = "weights_dir, cfg and out are required";
+        return B2_ERR_NULL;
+    }
+    *out = nullptr;
+    auto e = std::make_unique<b2_engine>();
+    const int rc = guarded([&] {
+        e->cfg = *cfg;
+        e->shape = b2::eng::read_config(weights_dir);
+        e->check_shape();
+        e->setup_device();
+        b2::eng::load_weights(*e, weights_dir);
+        e->setup_buffers();
+    });
+    if (rc == B2_OK) *out = e.release();
+    return rc;
+}
+
+int b2_engine_create_synthetic(const B2ModelShape* shape, uint64_t seed, float stdev, const B2EngineConfig* cfg,
+                               b2_engine** out) {
+    if (!shape || !cfg || !out) {
+        b2::eng::g_err = "shape, cfg and out are required";
+        return B2_ERR_NULL;
+    }
+    *out = nullptr;
+    auto e = std::make_unique<b2_engine>();
+    const int rc = guarded([&] {
+        e->cfg = *cfg;
+        e->shape = *shape;
+        e->check_shape();
+        e->setup_device();
+        b2::eng::synth_weights(*e, seed, stdev);
+        e->setup_buffers();
+    });
+    if (rc == B2_OK) *out = e.release();
+    return rc;
+}
+
+void b2_engine_destroy(b2_engine* eng) { delete eng; }
+
+int32_t b2_engine_add_sequence(b2_engine* eng, const int32_t* prompt, int32_t prompt_len) {
+    if (!eng || (prompt_len > 0 && !prompt) || prompt_len < 0) {
+        b2::eng::g_err = "bad arguments";
+        return B2_ERR_NULL;
+    }
+    int32_t id = -1;
+    const int rc = guarded([&] {
+        for (int i = 0; i < prompt_len; ++i)
+            if (prompt[i] < 0 || prompt[i] >= eng->shape.vocab_size) throw Error(B2_ERR_SHAPE, "prompt token outside the vocabulary");
+        const int blk = eng->blocks->allocate();
+        if (blk < 0) return;  // pool exhausted: -1, like the reference
+        b2::eng::Seq q;
+        q.table.ids.push_back(blk);
+        q.prompt.assign(prompt, prompt + prompt_len);
+        id = eng->next_id++;
+        eng->seqs.emplace(id, std::move(q));
+    });
+    return rc == B2_OK ? id : rc;
+}
+
+int32_t b2_engine_add_sequence_cached(b2_engine* eng, int32_t ctx_len, int32_t last_token) {
+    if (!eng) return B2_ERR_NULL;
+    int32_t id = -1;
+    const int rc = guarded([&] {
+        if (ctx_len < 0 || ctx_len >= eng->cfg.max_seq_len) throw Error(B2_ERR_SHAPE, "ctx_len must be in [0, max_seq_len)");
+        if (last_token < 0 || last_token >= eng->shape.vocab_size) throw Error(B2_ERR_SHAPE, "last_token outside the vocabulary");
+        const int nblk = ctx_len / B2_BLOCK_TOKENS + 1;  // covers positions [0, ctx_len]
+        if (nblk > eng->blocks->num_free()) return;
+        b2::eng::Seq q;
+        for (int i = 0; i < nblk; ++i) q.table.ids.push_back(eng->blocks->allocate());
+        q.seq_len = ctx_len;
+        q.last_token = last_token;
+        id = eng->next_id++;
+        eng->seqs.emplace(id, std::move(q));
+    });
+    return rc == B2_OK ? id : rc;
+}
+
+int b2_engine_decode_step(b2_engine* eng, const int32_t* seq_ids, int32_t batch, int32_t* out_next_tokens) {
+    if (!eng || !seq_ids || !out_next_tokens) {
+        b2::eng::g_err = "engine, seq_ids and out_next_tokens are required";
+        return B2_ERR_NULL;
+    }
+    return guarded([&] {
+        b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
+        eng->decode_step(seq_ids, batch, out_next_tokens);
+    });
+}
+
+int b2_engine_free_sequence(b2_engine* eng, int32_t seq_id) {
+    if (!eng) return B2_ERR_NULL;
+    return guarded([&] {
+        auto it = eng->seqs.find(seq_id);
+        if (it == eng->seqs.end()) return;
+        for (int blk : it->second.table.ids) eng->blocks->free(blk);
+        eng->seqs.erase(it);
+    });
+}
+
+int64_t b2_engine_free_blocks(const b2_engine* eng) { return eng ? eng->blocks->num_free() : 0; }
+
+int b2_engine_set_use_cuda_graphs(b2_engine* eng, int32_t enabled) {
+    if (!eng) return B2_ERR_NULL;
+    eng->use_graphs = enabled != 0;
+    return B2_OK;
+}
+
+int b2_engine_shape(const b2_engine* eng, B2ModelShape* out) {
+    if (!eng || !out) return B2_ERR_NULL;
+    *out = eng->shape;
+    return B2_OK;
+}
+
+int b2_engine_stream(const b2_engine* eng, b2_stream_t* out) {
+    if (!eng || !out) return B2_ERR_NULL;
+    *out = eng->stream;
+    return B2_OK;
+}
+
+b2_block_pool* b2_block_pool_create(int32_t num_blocks) { return num_blocks >= 0 ? new b2_block_pool(num_blocks) : nullptr; }
+void b2_block_pool_destroy(b2_block_pool* pool) { delete pool; }
+int32_t b2_block_pool_allocate(b2_block_pool* pool) { return pool ? pool->allocate() : -1; }
+int32_t b2_block_pool_free(b2_block_pool* pool, int32_t block_id) {
+    try {
+        pool->free(block_id);
+        return 0;
+    } catch (const std::out_of_range&) {
+        return 1;
+    } catch (const std::logic_error&) {
+        return 2;
+    }
+}
+int32_t b2_block_pool_num_free(const b2_block_pool* pool) { return pool ? pool->num_free() : 0; }
+
+}  // extern "C"

@@ -36,19 +36,26 @@ __global__ void __launch_bounds__(128) add_layernorm_kernel(T* out, T* residual_
     for (int i = 0; i < NCH; ++i) {
         const int c = lane + 32 * i;
         if (c < nch) {
-            float r[E];
+            // r = residual + (x + bias): the bias belongs to the GEMM output x,
+            // as in the reference (add_bias before the residual add,
+            // engine.cu:184-188; cpu_model.cpp:164-165 adds linear-with-bias).
+            float r[E], xf[E];
             unpack16<T>(__ldg(reinterpret_cast<const uint4*>(residual_in + base) + c), r);
             if (x != nullptr) {
-                float xf[E];
                 unpack16<T>(__ldg(reinterpret_cast<const uint4*>(x + base) + c), xf);
+            } else {
 #pragma unroll
-                for (int e = 0; e < E; ++e) r[e] = __fadd_rn(xf[e], r[e]);
+                for (int e = 0; e < E; ++e) xf[e] = 0.0f;
             }
             if (bias != nullptr) {
                 float bf[E];
                 unpack16<T>(__ldg(reinterpret_cast<const uint4*>(bias) + c), bf);
 #pragma unroll
-                for (int e = 0; e < E; ++e) r[e] = __fadd_rn(r[e], bf[e]);
+                for (int e = 0; e < E; ++e) xf[e] = __fadd_rn(xf[e], bf[e]);
+            }
+            if (x != nullptr || bias != nullptr) {
+#pragma unroll
+                for (int e = 0; e < E; ++e) r[e] = __fadd_rn(r[e], xf[e]);
             }
 #pragma unroll
             for (int e = 0; e < E; ++e) {

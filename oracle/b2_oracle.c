@@ -315,7 +315,7 @@ int oracle_paged_attention(int dt, const void* q, int q_row_stride, const void* 
 
 /* ------------------------------------------------------ layer-norm and MLP */
 
-/* residual_out = x + residual_in [+ bias] (stored in dt); out = LN of that sum
+/* residual_out = residual_in + (x + bias) (stored in dt); out = LN of that sum
  * with mean and variance accumulated in double (cpu_model.cpp:27-47) over the
  * float sum; the normalised value is computed in double, rounded to float,
  * then * gamma + beta in float -- the exact cpu_model.cpp:44 expression.
@@ -329,9 +329,12 @@ void oracle_add_layernorm(int dt, float* out, void* out_dt_copy, void* residual_
         const size_t base = (size_t)b * d_model;
         double mean = 0.0;
         for (int d = 0; d < d_model; ++d) {
+            /* residual + (x + bias): the bias belongs to the GEMM output x
+             * (engine.cu:184-188 adds it before the residual add) */
+            float xb = x ? ld(x, dt, base + d) : 0.0f;
+            if (bias) xb = xb + ld(bias, dt, d);
             row[d] = ld(residual_in, dt, base + d);
-            if (x) row[d] = ld(x, dt, base + d) + row[d];
-            if (bias) row[d] = row[d] + ld(bias, dt, d); /* the engine folds the GEMM bias in here */
+            if (x || bias) row[d] = row[d] + xb;
             mean += row[d];
         }
         mean /= d_model;

@@ -1,0 +1,129 @@
+"""The GPT-2 decode engine on the GPU, through its C-ABI (libb2engine.so).
+
+Parity: with fp32 weights the engine's greedy tokens must equal, token for
+token, what the reference's CPUModel::greedy_generate
+(gpu-engine/src/reference/cpu_model.cpp:198-216) produced on the same synthetic
+weights (fixtures in tests/golden/, made by tests/golden/make_golden.py from
+the reference compiled from its sources).  Sequences of different prompt
+lengths run together in one batch, the way the reference's scheduler feeds
+Engine::decode_step (prompt tokens one per step, then generated tokens).
+"""
+from __future__ import annotations
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def E(b2, cuda):
+    from lis_b200 import engine
+    engine.load()
+    return engine
+
+
+def engine_greedy(eng, prompts, n_new):
+    """Feeds every prompt through Engine::decode_step in one shared batch and
+    returns the n_new tokens generated after each prompt."""
+    ids = [eng.add_sequence(p) for p in prompts]
+    assert min(ids) >= 0
+    consumed = [0] * len(prompts)
+    gen: list[list[int]] = [[] for _ in prompts]
+    while True:
+        active = [i for i in range(len(prompts)) if len(gen[i]) < n_new]
+        if not active:
+            break
+        out = eng.decode_step([ids[i] for i in active])
+        for i, tok in zip(active, out):
+            consumed[i] += 1
+            if consumed[i] >= len(prompts[i]):
+                gen[i].append(tok)
+    for i in ids:
+        eng.free_sequence(i)
+    return gen
+
+
+def _model_dir(tmp_path_factory, shape, seed, std, name):
+    from lis_b200 import model_files as MF
+    return MF.write_model_dir(tmp_path_factory.mktemp(name), MF.GPT2Shape(**shape), seed=seed, std=std)
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_engine_fp32_matches_reference_tokens_tiny(E, golden, tmp_path_factory, graphs):
+    fx = golden("gpt2_tiny_greedy.json")
+    case = next(c for c in fx["cases"] if c["shape"]["d_model"] // c["shape"]["n_head"] in (64, 128))
+    d = _model_dir(tmp_path_factory, case["shape"], case["seed"], case["std"], case["name"])
+    eng = E.Engine()
+    assert eng.init(d, E.Config(max_batch=4, max_seq_len=case["shape"]["n_ctx"], kv_block_budget=64, dtype=0,
+                                use_cuda_graphs=graphs)), eng.last_error()
+    got = engine_greedy(eng, case["prompts"], case["n_new"])
+    assert got == case["generated"]
+    assert eng.free_blocks() == 64
+
+
+def test_engine_fp32_matches_reference_tokens_gpt2_small(E, golden, tmp_path_factory):
+    """GPT-2 small fp32, 8 prompts of 16-128 tokens, 64 greedy steps each."""
+    fx = golden("gpt2_small_greedy.json")
+    from lis_b200 import model_files as MF
+    d = MF.write_model_dir(tmp_path_factory.mktemp("small"), MF.GPT2_SMALL, seed=fx["seed"], std=fx["std"])
+    eng = E.Engine()
+    assert eng.init(d, E.Config(max_batch=8, max_seq_len=256, kv_block_budget=256, dtype=0)), eng.last_error()
+    got = engine_greedy(eng, fx["prompts"], fx["n_new"])
+    for i, (g, want) in enumerate(zip(got, fx["generated"])):
+        assert g == want, f"prompt {i} (len {len(fx['prompts'][i])}) diverged"
+
+
+@pytest.mark.parametrize("dtype", [1, 2])
+def test_engine_half_precision_runs_and_graphs_agree(E, golden, tmp_path_factory, dtype):
+    fx = golden("gpt2_tiny_greedy.json")
+    case = next(c for c in fx["cases"] if c["shape"]["d_model"] // c["shape"]["n_head"] in (64, 128))
+    d = _model_dir(tmp_path_factory, case["shape"], case["seed"], case["std"], f"half{dtype}")
+    outs = []
+    for graphs in (True, False):
+        eng = E.Engine()
+        assert eng.init(d, E.Config(max_batch=4, max_seq_len=case["shape"]["n_ctx"], kv_block_budget=64,
+                                    dtype=dtype, use_cuda_graphs=graphs)), eng.last_error()
+        outs.append(engine_greedy(eng, case["prompts"], case["n_new"]))
+        eng.close()
+    assert outs[0] == outs[1]
+    vocab = case["shape"]["vocab_size"]
+    assert all(0 <= t < vocab for seq in outs[0] for t in seq)
+
+
+def test_engine_block_accounting_and_pool_exhaustion(E):
+    shape = E.ModelShape(n_layer=2, n_head=2, d_model=128, vocab_size=500, n_ctx=128, layer_norm_epsilon=1e-5,
+                         eos_token_id=-1)
+    eng = E.Engine()
+    eng.init_synthetic(shape, E.Config(max_batch=4, max_seq_len=128, kv_block_budget=3, dtype=1), seed=5, std=0.1)
+    a = eng.add_sequence([1, 2, 3])
+    b = eng.add_sequence([4])
+    assert (a, b) == (0, 1) and eng.free_blocks() == 1
+    for _ in range(16):  # positions 0..15 fit in the first blocks
+        eng.decode_step([a, b])
+    assert eng.free_blocks() == 1
+    eng.decode_step([a])  # a crosses into its second block
+    assert eng.free_blocks() == 0
+    assert eng.add_sequence([7]) == -1  # like the reference: -1 when the pool is empty
+    with pytest.raises(Exception) as ei:
+        eng.decode_step([a, b])  # b needs a block, none left: nothing launched
+    assert getattr(ei.value, "code", None) == E.ERR_POOL
+    assert eng.free_blocks() == 0
+    eng.free_sequence(a)
+    eng.free_sequence(12345)  # unknown ids are ignored
+    assert eng.free_blocks() == 2
+    out = eng.decode_step([b])
+    assert eng.free_blocks() == 1 and 0 <= out[0] < 500
+
+
+def test_engine_synthetic_cached_contexts(E):
+    """The bench path: synthetic weights, sequences with cached contexts of
+    different lengths, every batch bucket size, graphs on."""
+    shape = E.ModelShape(n_layer=2, n_head=12, d_model=768, vocab_size=1000, n_ctx=1024, layer_norm_epsilon=1e-5,
+                         eos_token_id=-1)
+    eng = E.Engine()
+    eng.init_synthetic(shape, E.Config(max_batch=16, max_seq_len=1024, kv_block_budget=1200, dtype=2), seed=1)
+    ids = [eng.add_sequence_cached(100 + 57 * i, i) for i in range(16)]
+    assert min(ids) >= 0
+    for n in (1, 3, 8, 16):
+        out = eng.decode_step(ids[:n])
+        assert len(out) == n and all(0 <= t < 1000 for t in out)
