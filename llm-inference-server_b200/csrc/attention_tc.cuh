@@ -1,0 +1,647 @@
+// attention_tc.cuh -- grouped-query paged decode attention on the 5th-generation
+// tensor cores (tcgen05 + TMEM + TMA), for 8 KV heads of head_dim 128 and
+// 8 * QG query heads (QG = 1, 2, 4, 8).
+//
+// Same result and contract as paged_decode_kernel (attention.cuh), which
+// restates gpu-engine/src/kernels/attention.cu:49-127 (softmax over the
+// seq_lens[b] cached keys of kv head h / QG).  Why a second kernel: with
+// grouped queries every K/V element feeds QG dot products, and on the CUDA
+// cores the FMAs, conversions and shuffles of 8 * QG heads outrun the issue
+// slots before HBM is saturated.  Here the two contractions of a 16-token
+// block run on the tensor cores:
+//
+//   one block slab in shared memory, rows r = kv_head * 16 + token (128 rows):
+//       K[r][0..128)   V[r][0..128)         (TMA, SWIZZLE_128B, 2 boxes each)
+//   S^T[r][hq]  = sum_d K[r][d] * Q[hq][d]            M=128, N=NP, K=128
+//   O^T[d][hq] += sum_r V[r][d] * P^T[hq][r]          M=128, N=NP, K=128
+//
+// Q holds all NP (= max(16, H)) query heads, so S^T is computed for every
+// (row, head) pair and a row reads back only the QG columns of its own kv
+// head.  P^T is block-diagonal: entry (hq, r) is the softmax weight when hq
+// belongs to row r's kv head and 0 otherwise (the zeros are written once),
+// so the second product sums over the right keys only.  Tensor work is 8x
+// the useful FLOPs, far below the tensor-core roof; the kernel is HBM-bound.
+//
+// Softmax: scores are scaled into log2 units; each (kv head, query head)
+// keeps a reference maximum m_ref that only moves when a block maximum
+// exceeds it by more than 8, so weights stay <= 2^8 and O in TMEM is
+// rescaled only on those (rare) moves -- exact arithmetic, not an
+// approximation.  Weights p are split into hi = T(p) and lo = T(p - hi) and
+// both parts are multiplied in, so O carries ~16 significant bits of each
+// weight (a single 16-bit weight would carry 8 for bf16).
+//
+// Work split and partials are those of paged_decode_kernel, in units of
+// 16-token blocks: every CTA owns an equal share of the batch's blocks and
+// writes one partial (m, l, acc) per sequence piece, merged by
+// paged_decode_combine_kernel.
+//
+// Roles (160 threads, one CTA per SM):
+//   warps 0-3  softmax / epilogue, one TMEM lane (MMA row) per thread;
+//              thread 0 also issues the MMAs;
+//   warp 4     TMA producer: block-table reads, one stage per block.
+// Every wait is bounded (b2_common.cuh); a wait that gives up flags
+// B2_DEVERR_TIMEOUT and the CTA leaves through the common exit, which waits
+// for its own MMAs and copies and frees its TMEM.
+#pragma once
+
+#include <cuda.h>
+
+#include "attention.cuh"
+#include "b2_common.cuh"
+
+namespace b2 {
+
+constexpr int kTcKvHeads = 8;
+constexpr int kTcHeadDim = 128;
+constexpr int kTcHalfBytes = 16 * kTcKvHeads * 64 * 2;  // one TMA box: 128 rows x 64 elements = 16 KiB
+constexpr int kTcStageBytes = 4 * kTcHalfBytes;          // K lo/hi dims, V lo/hi dims
+constexpr int kTcThreads = 160;
+constexpr int kTcConsumers = 128;
+
+struct TcParams {
+    const void* q;
+    int q_row_stride;
+    const void* q_bias;
+    const int* block_tables;
+    const int* seq_lens;
+    int batch, mbps, layer_idx, n_layer, num_blocks;
+    float scale_log2;
+    int stages;
+    int2* seq_info;
+    float2* part_ml;
+    float* part_acc;
+};
+
+// ---------------------------------------------------------------- PTX glue
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem], both described by shared-memory descriptors.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+
+// Arrives on `bar` once every MMA this thread issued before it has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// 8 consecutive TMEM columns of this warp's 32 lanes (one lane per thread),
+// waited for inside the same statement so no use can precede the wait.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+    uint32_t r0, r1, r2, r3, r4, r5, r6, r7;
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3), "=r"(r4), "=r"(r5), "=r"(r6), "=r"(r7)
+        : "r"(taddr)
+        : "memory");
+    v[0] = __uint_as_float(r0);
+    v[1] = __uint_as_float(r1);
+    v[2] = __uint_as_float(r2);
+    v[3] = __uint_as_float(r3);
+    v[4] = __uint_as_float(r4);
+    v[5] = __uint_as_float(r5);
+    v[6] = __uint_as_float(r6);
+    v[7] = __uint_as_float(r7);
+}
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+    uint32_t r0, r1, r2, r3;
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+        : "r"(taddr)
+        : "memory");
+    v[0] = __uint_as_float(r0);
+    v[1] = __uint_as_float(r1);
+    v[2] = __uint_as_float(r2);
+    v[3] = __uint_as_float(r3);
+}
+__device__ __forceinline__ void tmem_ld2(uint32_t taddr, float* v) {
+    uint32_t r0, r1;
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r0), "=r"(r1)
+        : "r"(taddr)
+        : "memory");
+    v[0] = __uint_as_float(r0);
+    v[1] = __uint_as_float(r1);
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Barriers of the 128 softmax threads (ids 1..7; 0 is __syncthreads).  bar.red
+// is warp-aligned, so the warp is reconverged first (thread 0 runs extra
+// issuer code between barriers).
+__device__ __forceinline__ bool tc_sync_or(int id, bool pred) {
+    __syncwarp();
+    return named_sync_or(id, kTcConsumers, pred);
+}
+__device__ __forceinline__ void tc_sync(int id) {
+    __syncwarp();
+    named_sync(id, kTcConsumers);
+}
+
+// 4-D tiled TMA load (no multicast) completing on `bar`.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor, SWIZZLE_128B layout (sm_100 format:
+// start >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride byte
+// offset >> 4 in 32-45, version 1 in 46-47, layout type 2 in 61-63).
+//   K-major operand: rows of 128 B (64 elements), 8-row groups 1024 B apart
+//     (SBO); the leading offset is unused (1).  One MMA (K = 16) reads 32 B
+//     of every row: advance the start by 32 B per K step.
+//   MN-major operand: 128-B rows run along M; 8 K-rows form a 1024-B atom
+//     (SBO = next 8 K-rows), LBO = next 64 elements of M.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
+           (static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16 with fp32 accumulation: D format F32
+// (bits 4-5 = 1), A/B format F16 (0) or BF16 (1) in bits 7-9 / 10-12, A/B
+// major in bits 15 / 16 (1 = MN-major), N >> 3 in bits 17-22, M >> 4 in 24-28.
+template <typename T>
+__host__ __device__ constexpr uint32_t umma_idesc(int M, int N, bool a_mn, bool b_mn) {
+    return (1u << 4) | ((Elem<T>::kIsBf16 ? 1u : 0u) << 7) | ((Elem<T>::kIsBf16 ? 1u : 0u) << 10) |
+           ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Byte offset of element (row, col) (col < 64) in a 128-B-row SWIZZLE_128B
+// tile whose base is 1024-B aligned: 16-B chunk index XOR (row % 8).
+__device__ __forceinline__ uint32_t sw128_offset(int row, int col, int es) {
+    const int byte = col * es;
+    return static_cast<uint32_t>(row * 128 + ((((byte >> 4) ^ row) & 7) << 4) + (byte & 15));
+}
+
+// Shared-memory plan shared by host and device (bytes from the 1024-aligned base).
+template <int QG>
+struct TcLayout {
+    static constexpr int H = kTcKvHeads * QG;
+    static constexpr int NP = H < 16 ? 16 : H;     // MMA N (query heads, padded)
+    static constexpr int QHALF = NP * 128;         // one 64-dim half of Q, or of one P^T part
+    static constexpr int TMEM_COLS = 3 * NP <= 64 ? 64 : (3 * NP <= 128 ? 128 : 256);
+    __host__ __device__ static constexpr int off_q(int S) { return S * kTcStageBytes; }
+    __host__ __device__ static constexpr int off_p(int S) { return off_q(S) + 2 * QHALF; }  // [hi|lo][dims half]
+    __host__ __device__ static constexpr int off_meta(int S) { return off_p(S) + 4 * QHALF; }
+    __host__ __device__ static constexpr int off_corr(int S) { return off_meta(S) + 16 * S; }
+    __host__ __device__ static constexpr int off_bars(int S) { return off_corr(S) + 4 * NP; }
+    // full[S], empty[S], s_full[2], pv, done
+    __host__ __device__ static constexpr int off_tmem(int S) { return off_bars(S) + 8 * (2 * S + 4); }
+    __host__ __device__ static constexpr int off_misc(int S) { return off_tmem(S) + 16; }
+    __host__ __device__ static constexpr int bytes(int S) { return off_misc(S) + 4 * 36 + 1024; }
+};
+
+template <typename T, int QG>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    paged_decode_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap kv_map) {
+    using L = TcLayout<QG>;
+    constexpr int H = L::H;
+    constexpr int NP = L::NP;
+    constexpr int QHALF = L::QHALF;
+    constexpr uint32_t TMEM_COLS = L::TMEM_COLS;
+    constexpr uint32_t IDESC_QK = umma_idesc<T>(128, NP, false, false);
+    constexpr uint32_t IDESC_PV = umma_idesc<T>(128, NP, true, false);
+    constexpr int SCOLS = 2 * QG;  // S columns a warp reads: the QG heads of its two kv heads
+
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem =
+        smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // swizzled tiles need 1024-B alignment
+    const int S = p.stages;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int cta = blockIdx.x;
+    const int B = p.batch;
+
+    unsigned char* stages = smem;
+    unsigned char* qbuf = smem + L::off_q(S);
+    unsigned char* pbuf = smem + L::off_p(S);
+    int4* meta = reinterpret_cast<int4*>(smem + L::off_meta(S));
+    float* corr = reinterpret_cast<float*>(smem + L::off_corr(S));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::off_bars(S));
+    uint64_t* empty = full + S;
+    uint64_t* s_full = empty + S;
+    uint64_t* pv_bar = s_full + 2;
+    uint64_t* done_bar = pv_bar + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::off_tmem(S));
+    int* misc = reinterpret_cast<int*>(smem + L::off_misc(S));
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
+        mbar_init(pv_bar, 1);
+        mbar_init(done_bar, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    // Q rows >= H and the off-diagonal P^T entries stay zero for the whole kernel.
+    for (int i = tid; i < 6 * QHALF / 16; i += kTcThreads)
+        reinterpret_cast<uint4*>(qbuf)[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < NP; i += kTcThreads) corr[i] = 1.0f;  // padding heads are never rescaled
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // ---- prologue: per-sequence block counts, global prefix, this CTA's blocks
+    const int per = (B + kTcThreads - 1) / kTcThreads;
+    const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
+    int local = 0;
+    for (int b = b_lo; b < b_hi; ++b)
+        local += (clamp_seq_len(__ldg(p.seq_lens + b), p.mbps) + kBlockTokens - 1) / kBlockTokens;
+    int N = 0;
+    const int excl = block_exclusive_scan(local, misc + 2, &N);
+    const int G = min(static_cast<int>(gridDim.x), max(N, 1));
+    const long long s_unit = cta < G ? static_cast<long long>(cta) * N / G : 0;
+    const long long e_unit = cta < G ? static_cast<long long>(cta + 1) * N / G : 0;
+    {
+        int run = excl;
+        for (int b = b_lo; b < b_hi; ++b) {
+            const int raw = __ldg(p.seq_lens + b);
+            const int nbk = (clamp_seq_len(raw, p.mbps) + kBlockTokens - 1) / kBlockTokens;
+            if (nbk > 0 && run <= s_unit && s_unit < run + nbk) {
+                misc[0] = b;
+                misc[1] = run;
+            }
+            if (b % static_cast<int>(gridDim.x) == cta) {
+                if (raw != clamp_seq_len(raw, p.mbps)) flag_error(B2_DEVERR_SEQ_LEN);
+                int2 info = make_int2(0, 0);
+                if (nbk > 0) {
+                    const int i0 = cta_of_unit(run, N, G);
+                    info = make_int2(i0, cta_of_unit(run + nbk - 1, N, G) - i0 + 1);
+                }
+                p.seq_info[b] = info;
+            }
+            run += nbk;
+        }
+    }
+    __syncthreads();
+    const bool has_work = e_unit > s_unit;
+
+    if (warp == 4 && has_work) {
+        // ================================================= TMA producer
+        long long u = s_unit;
+        int bb = misc[0];
+        long long Pb = misc[1];
+        int n = 0;
+        bool failed = false;
+        while (u < e_unit && !failed && bb < B) {
+            const int b = bb + lane;
+            const int cl = b < B ? clamp_seq_len(__ldg(p.seq_lens + b), p.mbps) : 0;
+            const int nbk = (cl + kBlockTokens - 1) / kBlockTokens;
+            int incl = nbk;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += y;
+            }
+            const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
+            for (int sidx = 0; sidx < 32 && u < e_unit && !failed; ++sidx) {
+                const int cs = __shfl_sync(0xffffffffu, cl, sidx);
+                const int nbs = __shfl_sync(0xffffffffu, nbk, sidx);
+                const long long Ps = Pb + __shfl_sync(0xffffffffu, incl - nbk, sidx);
+                const int bs = bb + sidx;
+                if (nbs == 0 || Ps + nbs <= u) continue;
+                const int j0 = static_cast<int>(u - Ps);
+                const int j1 = static_cast<int>(min(e_unit, Ps + nbs) - Ps);
+                for (int jc = j0; jc < j1 && !failed; jc += 32) {
+                    const int jj = jc + lane;
+                    int blk_l = 0;
+                    if (jj < j1) {
+                        blk_l = __ldg(p.block_tables + static_cast<size_t>(bs) * p.mbps + jj);
+                        if (blk_l < 0 || blk_l >= p.num_blocks) {
+                            flag_error(B2_DEVERR_BLOCK_ID);
+                            blk_l = 0;
+                        }
+                    }
+                    const int cnt = min(32, j1 - jc);
+                    for (int x = 0; x < cnt; ++x) {
+                        const int blk = __shfl_sync(0xffffffffu, blk_l, x);
+                        int ok = 1;
+                        if (lane == 0) {
+                            const int st = n % S;
+                            if (!mbar_wait_bounded(&empty[st], (static_cast<uint32_t>(n / S) & 1u) ^ 1u)) {
+                                ok = 0;
+                            } else {
+                                const int j = jc + x;
+                                const int nvalid = j == nbs - 1 ? cs - j * kBlockTokens : kBlockTokens;
+                                const int flags = (j == j0 ? 1 : 0) | (j == j1 - 1 ? 2 : 0) |
+                                                  (Ps + j + 1 == e_unit ? 4 : 0);
+                                meta[st] = make_int4(bs, nvalid | (flags << 8), 0, 0);
+                                mbar_arrive_expect_tx(&full[st], kTcStageBytes);
+                                const int slab = (blk * p.n_layer + p.layer_idx) * 2;
+                                unsigned char* dst = stages + static_cast<size_t>(st) * kTcStageBytes;
+                                tma_load_4d(dst, &kv_map, 0, 0, 0, slab, &full[st]);
+                                tma_load_4d(dst + kTcHalfBytes, &kv_map, 64, 0, 0, slab, &full[st]);
+                                tma_load_4d(dst + 2 * kTcHalfBytes, &kv_map, 0, 0, 0, slab + 1, &full[st]);
+                                tma_load_4d(dst + 3 * kTcHalfBytes, &kv_map, 64, 0, 0, slab + 1, &full[st]);
+                            }
+                        }
+                        ok = __shfl_sync(0xffffffffu, ok, 0);
+                        if (!ok) {
+                            failed = true;
+                            break;
+                        }
+                        ++n;
+                    }
+                }
+                u = Ps + j1;
+            }
+            bb += 32;
+            Pb += wtotal;
+        }
+        if (lane == 0) {
+            if (failed) flag_error(B2_DEVERR_TIMEOUT);
+            for (int m = max(0, n - S); m < n; ++m)  // no copy may still be in flight at exit
+                if (!mbar_wait_bounded(&full[m % S], static_cast<uint32_t>(m / S) & 1u)) flag_error(B2_DEVERR_TIMEOUT);
+        }
+    } else if (warp < 4 && has_work) {
+        // ================================================ softmax warps
+        const int r = tid;           // MMA row = TMEM lane of S
+        const int hk = r >> 4;       // kv head of this row
+        const int t = r & 15;        // token within the block
+        const bool upper = (lane & 16) != 0;
+        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+        const uint32_t s_col0 = static_cast<uint32_t>(2 * warp * QG);
+        const uint32_t o_col = 2u * NP;
+        const float scale_log2 = p.scale_log2;
+        float m_ref[QG], l_part[QG];
+#pragma unroll
+        for (int g = 0; g < QG; ++g) {
+            m_ref[g] = -INFINITY;
+            l_part[g] = 0.0f;
+        }
+
+        auto issue_qk = [&](int m) {  // S^T[m % 2] = K(m) . Q^T
+            const uint32_t kb = smem_addr(stages + static_cast<size_t>(m % S) * kTcStageBytes);
+            const uint32_t qa = smem_addr(qbuf);
+            const uint32_t d = tmem + static_cast<uint32_t>((m & 1) * NP);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t h = static_cast<uint32_t>(kk >> 2), ko = static_cast<uint32_t>((kk & 3) * 32);
+                umma_f16(d, sw128_desc(kb + h * kTcHalfBytes + ko, 16, 1024), sw128_desc(qa + h * QHALF + ko, 16, 1024),
+                         IDESC_QK, kk > 0);
+            }
+        };
+        auto issue_pv = [&](int m, bool first_blk) {  // O^T (+)= V(m)^T . P^T, hi then lo part
+            const uint32_t vb = smem_addr(stages + static_cast<size_t>(m % S) * kTcStageBytes + 2 * kTcHalfBytes);
+            const uint32_t pb = smem_addr(pbuf);
+#pragma unroll
+            for (int part = 0; part < 2; ++part)
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t bo = static_cast<uint32_t>(part * 2 * QHALF + (kk >> 2) * QHALF + (kk & 3) * 32);
+                    umma_f16(tmem + o_col, sw128_desc(vb + static_cast<uint32_t>(kk) * 2048u, kTcHalfBytes, 1024),
+                             sw128_desc(pb + bo, 16, 1024), IDESC_PV, !(first_blk && part == 0 && kk == 0));
+                }
+        };
+
+        for (int n = 0;; ++n) {
+            const int st = n % S;
+            const bool got = mbar_wait_bounded(&full[st], static_cast<uint32_t>(n / S) & 1u);
+            if (tc_sync_or(1,!got)) {
+                if (tid == 0) flag_error(B2_DEVERR_TIMEOUT);
+                break;
+            }
+            const int4 m4 = meta[st];
+            const int b = m4.x;
+            const int nvalid = m4.y & 0xff;
+            const bool first = (m4.y >> 8) & 1;
+            const bool last = (m4.y >> 9) & 1;
+            const bool final_blk = (m4.y >> 10) & 1;
+
+            if (first) {
+                // ---- new sequence piece: its q (plus bias, rounded to T) into Q
+                const T* qsrc = static_cast<const T*>(p.q) + static_cast<size_t>(b) * p.q_row_stride;
+                for (int c = tid; c < H * 16; c += kTcConsumers) {
+                    const int hq = c >> 4, dc = c & 15;
+                    uint4 raw = __ldg(reinterpret_cast<const uint4*>(qsrc + hq * kTcHeadDim + dc * 8));
+                    if (p.q_bias != nullptr) {
+                        float f[8], bf[8];
+                        unpack16<T>(raw, f);
+                        unpack16<T>(__ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.q_bias) +
+                                                                         hq * kTcHeadDim + dc * 8)),
+                                    bf);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = __fadd_rn(f[e], bf[e]);
+                        raw = pack16<T>(f);
+                    }
+                    *reinterpret_cast<uint4*>(qbuf + (dc >> 3) * QHALF + sw128_offset(hq, (dc & 7) * 8, 2)) = raw;
+                }
+                fence_proxy_async_smem();
+                tc_sync(2);
+                if (tid == 0) {
+                    tc_fence_after();
+                    issue_qk(n);
+                    umma_commit(&s_full[n & 1]);
+                    if (!last) {
+                        if (mbar_wait_bounded(&full[(n + 1) % S], static_cast<uint32_t>((n + 1) / S) & 1u)) {
+                            issue_qk(n + 1);
+                            umma_commit(&s_full[(n + 1) & 1]);
+                        } else {
+                            flag_error(B2_DEVERR_TIMEOUT);  // the others give up on s_full
+                        }
+                    }
+                }
+#pragma unroll
+                for (int g = 0; g < QG; ++g) {
+                    m_ref[g] = -INFINITY;
+                    l_part[g] = 0.0f;
+                }
+            }
+
+            // ---- scores of block n: this row's QG query heads
+            const bool got_s = mbar_wait_bounded(&s_full[n & 1], static_cast<uint32_t>(n >> 1) & 1u);
+            if (tc_sync_or(3,!got_s)) {
+                if (tid == 0) flag_error(B2_DEVERR_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            float sv[SCOLS];
+            const uint32_t saddr = tmem + lane_base + static_cast<uint32_t>((n & 1) * NP) + s_col0;
+            if constexpr (SCOLS == 2) {
+                tmem_ld2(saddr, sv);
+            } else if constexpr (SCOLS == 4) {
+                tmem_ld4(saddr, sv);
+            } else {
+#pragma unroll
+                for (int c0 = 0; c0 < SCOLS; c0 += 8) tmem_ld8(saddr + c0, sv + c0);
+            }
+            const bool valid = t < nvalid;
+            float s[QG], cf[QG];
+            bool need = false;
+#pragma unroll
+            for (int g = 0; g < QG; ++g) {
+                s[g] = valid ? (upper ? sv[QG + g] : sv[g]) * scale_log2 : -INFINITY;
+                float bm = s[g];
+#pragma unroll
+                for (int off = 8; off > 0; off >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, off));
+                cf[g] = 1.0f;
+                if (bm > m_ref[g] + 8.0f) {  // the block has at least one valid row, so bm is finite
+                    cf[g] = exp2f(m_ref[g] - bm);  // 0 while m_ref is -inf
+                    m_ref[g] = bm;
+                    l_part[g] *= cf[g];
+                    need = true;
+                }
+            }
+            // P^T of block n-1 is still being read until PV(n-1) completes.
+            bool got_pv = true;
+            if (!first) got_pv = mbar_wait_bounded(pv_bar, static_cast<uint32_t>(n - 1) & 1u);
+            if (tc_sync_or(5,!got_pv)) {
+                if (tid == 0) flag_error(B2_DEVERR_TIMEOUT);
+                break;
+            }
+            const int kh = r >> 6, rr = r & 63;
+#pragma unroll
+            for (int g = 0; g < QG; ++g) {
+                const float pw = valid ? exp2f(s[g] - m_ref[g]) : 0.0f;
+                l_part[g] += pw;
+                const T hi = Elem<T>::from_f(pw);
+                const T lo = Elem<T>::from_f(pw - Elem<T>::to_f(hi));
+                const int hq = hk * QG + g;
+                const uint32_t off = static_cast<uint32_t>(kh * QHALF) + sw128_offset(hq, rr, 2);
+                *reinterpret_cast<T*>(pbuf + off) = hi;
+                *reinterpret_cast<T*>(pbuf + 2 * QHALF + off) = lo;
+                if ((lane & 15) == 0) corr[hq] = cf[g];
+            }
+            if (!valid) {
+                // rows past the sequence end: whatever the pool holds there (even
+                // NaN) must not reach O through 0 * V
+                unsigned char* vrow = stages + static_cast<size_t>(st) * kTcStageBytes + 2 * kTcHalfBytes + r * 128;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    reinterpret_cast<uint4*>(vrow)[i] = make_uint4(0u, 0u, 0u, 0u);
+                    reinterpret_cast<uint4*>(vrow + kTcHalfBytes)[i] = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            const bool rescale = tc_sync_or(4,need) && !first;
+            if (rescale) {
+                // O columns of heads whose reference max moved: O *= corr (lane = dim)
+                tc_fence_after();
+                const uint32_t oaddr = tmem + lane_base + o_col;
+#pragma unroll
+                for (int c0 = 0; c0 < NP; c0 += 8) {
+                    float o[8];
+                    tmem_ld8(oaddr + c0, o);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) o[i] *= corr[c0 + i];
+                    tmem_st8(oaddr + c0, o);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                tc_sync(6);
+            }
+            if (tid == 0) {
+                tc_fence_after();
+                issue_pv(n, first);
+                umma_commit(&empty[st]);
+                umma_commit(pv_bar);
+                if (!last) {
+                    const int4 m1 = meta[(n + 1) % S];  // block n+1 is of this piece; its stage is full
+                    if (!((m1.y >> 9) & 1)) {
+                        if (mbar_wait_bounded(&full[(n + 2) % S], static_cast<uint32_t>((n + 2) / S) & 1u)) {
+                            issue_qk(n + 2);
+                            umma_commit(&s_full[n & 1]);
+                        } else {
+                            flag_error(B2_DEVERR_TIMEOUT);
+                        }
+                    }
+                }
+            }
+            if (last) {
+                // ---- piece end: partial (m, l, acc) of sequence b, slot cta + b
+                const bool got_o = mbar_wait_bounded(pv_bar, static_cast<uint32_t>(n) & 1u);
+                if (tc_sync_or(7,!got_o)) {
+                    if (tid == 0) flag_error(B2_DEVERR_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const size_t slot = static_cast<size_t>(cta) + b;
+                const uint32_t oaddr = tmem + lane_base + o_col;
+                float* acc = p.part_acc + slot * H * kTcHeadDim + r;  // lane r holds dim r
+#pragma unroll
+                for (int c0 = 0; c0 < NP; c0 += 8) {
+                    float o[8];
+                    tmem_ld8(oaddr + c0, o);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        if (c0 + i < H) __stcg(acc + (c0 + i) * kTcHeadDim, o[i]);
+                }
+#pragma unroll
+                for (int g = 0; g < QG; ++g) {
+                    float lt = l_part[g];
+#pragma unroll
+                    for (int off = 8; off > 0; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
+                    if ((lane & 15) == 0) __stcg(p.part_ml + slot * H + hk * QG + g, make_float2(m_ref[g], lt));
+                }
+                tc_fence_before();
+            }
+            if (final_blk) break;
+        }
+    }
+
+    // ---- common exit: every MMA of this CTA done, every thread out of TMEM
+    if (tid == 0) {
+        umma_commit(done_bar);
+        if (!mbar_wait_bounded(done_bar, 0)) flag_error(B2_DEVERR_TIMEOUT);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+}  // namespace b2

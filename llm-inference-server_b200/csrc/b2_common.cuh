@@ -29,18 +29,21 @@ struct Elem;
 template <>
 struct Elem<float> {
     static constexpr int kPer16B = 4;
+    static constexpr bool kIsBf16 = false;
     __device__ __forceinline__ static float to_f(float x) { return x; }
     __device__ __forceinline__ static float from_f(float x) { return x; }
 };
 template <>
 struct Elem<__half> {
     static constexpr int kPer16B = 8;
+    static constexpr bool kIsBf16 = false;
     __device__ __forceinline__ static float to_f(__half x) { return __half2float(x); }
     __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
 };
 template <>
 struct Elem<__nv_bfloat16> {
     static constexpr int kPer16B = 8;
+    static constexpr bool kIsBf16 = true;
     __device__ __forceinline__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
     __device__ __forceinline__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
 };

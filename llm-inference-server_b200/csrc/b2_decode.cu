@@ -5,17 +5,21 @@
 // token subgroups, grid = one CTA per SM), and dtype / head_dim dispatch.
 // Nothing here allocates device memory or synchronises, except
 // b2_device_errors, which reads the device error word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "append.cuh"
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "b2_common.cuh"
 #include "rows.cuh"
 
@@ -95,9 +99,37 @@ constexpr int kMiscBytes = 256;
 struct AttnPlan {
     int grid = 0, threads = 0, smem = 0;
     int combine_threads = 0;
+    bool tensor_cores = false;  // paged_decode_tc_kernel instead of paged_decode_kernel
+    int tc_stages = 0;
     AttnParams prm{};
     size_t ws_info = 0, ws_ml = 0, ws_acc = 0, ws_total = 0;
 };
+
+// The tensor-core kernel serves 16-bit K/V with 8 kv heads of head_dim 128
+// and 8, 16 or 32 query heads.  B2_ATTENTION_TENSOR_CORES=0 in the
+// environment routes those shapes to the CUDA-core kernel instead (read once).
+bool tc_disabled_by_env() {
+    static const bool off = [] {
+        const char* v = std::getenv("B2_ATTENTION_TENSOR_CORES");
+        return v != nullptr && v[0] == '0';
+    }();
+    return off;
+}
+
+bool tc_eligible(const B2PagedAttnArgs* a) {
+    const int qg = a->n_head / a->n_kv_head;
+    return a->dtype != B2_F32 && a->head_dim == kTcHeadDim && a->n_kv_head == kTcKvHeads &&
+           (qg == 1 || qg == 2 || qg == 4) &&
+           static_cast<long long>(a->num_blocks) * a->n_layer * 2 < (1LL << 31) && !tc_disabled_by_env();
+}
+
+int tc_smem_bytes(int qg, int stages) {
+    switch (qg) {
+        case 1: return TcLayout<1>::bytes(stages);
+        case 2: return TcLayout<2>::bytes(stages);
+        default: return TcLayout<4>::bytes(stages);
+    }
+}
 
 int check_attn_args(const B2PagedAttnArgs* a) {
     if (a == nullptr) return fail(B2_ERR_NULL, "args is NULL");
@@ -138,6 +170,27 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     const int C = a->n_kv_head * GL;
     const int H = a->n_head;
     const int maxt = kAttnMaxThreads;
+    if (tc_eligible(a)) {
+        // One CTA per SM; as many 64-KiB stages as fit (3 for up to 32 heads).
+        const int qg = H / a->n_kv_head;
+        int stages = 4;
+        while (stages > 2 && tc_smem_bytes(qg, stages) > di.max_smem_optin) --stages;
+        if (tc_smem_bytes(qg, stages) <= di.max_smem_optin) {
+            pl->tensor_cores = true;
+            pl->tc_stages = stages;
+            pl->grid = di.sms;
+            pl->threads = kTcThreads;
+            pl->smem = tc_smem_bytes(qg, stages);
+            pl->combine_threads = static_cast<int>(align_up(static_cast<size_t>(H) * GL, 32));
+            pl->prm.ksplit = 1;
+            const size_t slots = static_cast<size_t>(pl->grid) + a->batch;
+            pl->ws_info = align_up(static_cast<size_t>(a->batch) * sizeof(int2), 256);
+            pl->ws_ml = align_up(slots * H * sizeof(float2), 256);
+            pl->ws_acc = align_up(slots * H * a->head_dim * sizeof(float), 256);
+            pl->ws_total = pl->ws_info + pl->ws_ml + pl->ws_acc;
+            return B2_OK;
+        }
+    }
     const int slab = B2_BLOCK_TOKENS * a->n_kv_head * a->head_dim * es;
     const int qbytes = H * a->head_dim * es;
     const int off_meta = 2 * slab + qbytes;
@@ -197,8 +250,8 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
 // Launch with programmatic dependent launch: the kernel waits on
 // griddepcontrol.wait before reading what the kernel before it wrote, so its
 // launch and set-up overlap that kernel's tail.
-template <typename K, typename P>
-int launch_pdl(K kern, dim3 grid, dim3 block, int smem, cudaStream_t stream, const P& prm) {
+template <typename K, typename... P>
+int launch_pdl(K kern, dim3 grid, dim3 block, int smem, cudaStream_t stream, const P&... prm) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -209,13 +262,73 @@ int launch_pdl(K kern, dim3 grid, dim3 block, int smem, cudaStream_t stream, con
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm...);
     if (e != cudaSuccess) {
         cudaGetLastError();
         g_last_error = cudaGetErrorString(e);
         return static_cast<int>(e);
     }
     return launch_status();
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// The pool as a 4-D tensor for the tensor-core kernel's TMA boxes:
+//   dim 0: head_dim elements (contiguous), box 64 (one 128-B swizzle row)
+//   dim 1: 16 token rows of a slab, stride n_kv_head*head_dim elements, box 16
+//   dim 2: kv head, stride head_dim elements, box 8
+//   dim 3: slab index ((block * n_layer + layer) * 2 + K|V), box 1
+// so one box lands as 128 rows (kv_head * 16 + token) of 128 B, swizzled.
+int encode_kv_map(const B2PagedAttnArgs* a, CUtensorMap* map) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr) return fail(B2_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t es = 2;
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kTcHeadDim), 16, static_cast<cuuint64_t>(kTcKvHeads),
+                                static_cast<cuuint64_t>(a->num_blocks) * a->n_layer * 2};
+    const cuuint64_t strides[3] = {kTcKvHeads * kTcHeadDim * es, kTcHeadDim * es,
+                                   16 * kTcKvHeads * kTcHeadDim * es};
+    const cuuint32_t box[4] = {64, 16, static_cast<cuuint32_t>(kTcKvHeads), 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(map, a->dtype == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           4, const_cast<void*>(a->kv_pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(B2_ERR_DEVICE, "cuTensorMapEncodeTiled rejected the KV pool layout");
+    return B2_OK;
+}
+
+template <typename T, int QG>
+int launch_tc_t(const AttnPlan& pl, const TcParams& tp, const CUtensorMap& map, cudaStream_t stream) {
+    auto kern = paged_decode_tc_kernel<T, QG>;
+    static std::atomic<uint64_t> smem_set{0};
+    int dev = -1;
+    const DeviceInfo di = device_info(&dev);
+    const int rc = ensure_max_smem(kern, smem_set, dev, di.max_smem_optin);
+    if (rc != B2_OK) return rc;
+    return launch_pdl(kern, dim3(static_cast<unsigned>(pl.grid)), dim3(static_cast<unsigned>(pl.threads)), pl.smem,
+                      stream, tp, map);
+}
+
+template <typename T>
+int launch_tc(const AttnPlan& pl, const TcParams& tp, const CUtensorMap& map, int qg, cudaStream_t s) {
+    switch (qg) {
+        case 1: return launch_tc_t<T, 1>(pl, tp, map, s);
+        case 2: return launch_tc_t<T, 2>(pl, tp, map, s);
+        case 4: return launch_tc_t<T, 4>(pl, tp, map, s);
+    }
+    return fail(B2_ERR_UNSUPPORTED, "no tensor-core kernel for this head shape");
 }
 
 template <typename T, int DH, int QG>
@@ -399,9 +512,34 @@ int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_s
     p.part_acc = reinterpret_cast<float*>(base + pl.ws_info + pl.ws_ml);
     const int qg = a->n_head / a->n_kv_head;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (a->dtype == B2_F32) rc = launch_attn_dh<float>(pl, a->head_dim, qg, s);
-    else if (a->dtype == B2_F16) rc = launch_attn_dh<__half>(pl, a->head_dim, qg, s);
-    else rc = launch_attn_dh<__nv_bfloat16>(pl, a->head_dim, qg, s);
+    if (pl.tensor_cores) {
+        CUtensorMap map;
+        rc = encode_kv_map(a, &map);
+        if (rc != B2_OK) return rc;
+        TcParams tp;
+        tp.q = a->q;
+        tp.q_row_stride = a->q_row_stride;
+        tp.q_bias = a->q_bias;
+        tp.block_tables = a->block_tables;
+        tp.seq_lens = a->seq_lens;
+        tp.batch = a->batch;
+        tp.mbps = a->max_blocks_per_seq;
+        tp.layer_idx = a->layer_idx;
+        tp.n_layer = a->n_layer;
+        tp.num_blocks = a->num_blocks;
+        tp.scale_log2 = p.scale_log2;
+        tp.stages = pl.tc_stages;
+        tp.seq_info = p.seq_info;
+        tp.part_ml = p.part_ml;
+        tp.part_acc = p.part_acc;
+        rc = a->dtype == B2_F16 ? launch_tc<__half>(pl, tp, map, qg, s) : launch_tc<__nv_bfloat16>(pl, tp, map, qg, s);
+    } else if (a->dtype == B2_F32) {
+        rc = launch_attn_dh<float>(pl, a->head_dim, qg, s);
+    } else if (a->dtype == B2_F16) {
+        rc = launch_attn_dh<__half>(pl, a->head_dim, qg, s);
+    } else {
+        rc = launch_attn_dh<__nv_bfloat16>(pl, a->head_dim, qg, s);
+    }
     if (rc != B2_OK) return rc;
     CombineParams cp;
     cp.seq_info = p.seq_info;
