@@ -1,22 +1,30 @@
 #!/usr/bin/env python3
 """Paged-attention decode benchmark (HBM GB/s) for the sm_100a hot path.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload mha|gqa]
 
-Workload (one step = one paged-attention launch over one batch): batch 64 per
-GPU, 12 heads, head_dim 64, fp16 K/V and q ~ N(0,1) from a seed, context
-U[128,1024], block size 16, block tables from a random permutation of a
-65536-block pool, scale 1/8, fp32 softmax.  Consecutive steps rotate through
-16 disjoint input sets (~1.8 GB of KV) so no launch is served from the
-126 MB L2.  Under torchrun every rank runs its own batch stream on its own
-GPU (weak scaling, no collective on the data path); the job's time is the
-max over ranks.
+One step = one paged-attention call (the split kernel and its merge kernel)
+over one batch.  Workloads:
+
+  mha (default, the headline): batch 64 per GPU, 12 heads, head_dim 64, fp16
+      K/V and q ~ N(0,1) from a seed, context U[128,1024], block size 16,
+      block tables from a random permutation of a 65536-block pool, scale 1/8,
+      fp32 softmax.  Consecutive steps rotate through 16 disjoint input sets
+      (~1.8 GB of KV) so no launch is served from the 126 MB L2.
+  gqa: batch 256 per GPU, 32 query heads over 8 kv heads, head_dim 128, bf16
+      K/V and q ~ N(0,1), context log-uniform in [512, 32768] (~7.2 GB of KV
+      per launch, far larger than L2), pool of 140000 blocks; runs on the
+      tensor-core kernel.
+
+Under torchrun every rank runs its own batch stream on its own GPU (weak
+scaling, no collective on the data path); the job's time is the max over
+ranks.
 
 The line also carries: the same metric end to end through the C-ABI with
-host buffers (e2e), the roofline of the kernel against the measured HBM copy
-bandwidth, the CPU baseline (the oracle's restatement of the reference CPU
-attention, multi-threaded, on a bounded sample), clocks sampled during the
-timed region, and the number of our kernel launches timed.
+host buffers (e2e), the roofline of the attention kernel against the measured
+HBM copy bandwidth, the CPU baseline (the oracle's restatement of the
+reference CPU attention, multi-threaded, on a bounded sample), clocks sampled
+during the timed region, and the number of our kernel launches timed.
 
 --impl reference times the reference's CPU implementation of the path (the
 oracle restatement of gpu-engine/src/reference/cpu_model.cpp:131-162 through
@@ -32,6 +40,7 @@ import re
 import sys
 import threading
 import time
+from dataclasses import dataclass
 from pathlib import Path
 
 import numpy as np
@@ -40,8 +49,35 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "paged-attn decode HBM GB/s"
-N_SETS = 16
-BATCH, N_HEAD, HEAD_DIM = 64, 12, 64
+
+
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    batch: int
+    n_head: int
+    n_kv_head: int
+    head_dim: int
+    dtype: str          # "f16" | "bf16"
+    ctx_lo: int
+    ctx_hi: int
+    log_uniform: bool
+    n_sets: int
+    pool_blocks: int
+    profile: str        # committed ncu summary holding traffic_bytes_per_launch
+    description: str
+
+
+WORKLOADS = {
+    "mha": Workload("mha", 64, 12, 12, 64, "f16", 128, 1024, False, 16, 65536, "paged_decode_microbench.md",
+                    "paged-attention decode microbench: batch 64 per GPU, 12 heads, head_dim 64, fp16 K/V and q "
+                    "N(0,1), context U[128,1024], block 16, random permutation of a 65536-block pool, scale 1/8"),
+    "gqa": Workload("gqa", 256, 32, 8, 128, "bf16", 512, 32768, True, 1, 140000, "paged_decode_tc_gqa.md",
+                    "grouped-query paged-attention decode: batch 256 per GPU, 32 query / 8 kv heads, head_dim 128, "
+                    "bf16 K/V and q N(0,1), context log-uniform [512,32768], block 16, random permutation of a "
+                    "140000-block pool, scale 1/sqrt(128)"),
+}
+WL = WORKLOADS["mha"]  # set by main()
 
 
 def import_package(name: str = "lis_b200"):
@@ -56,12 +92,22 @@ def import_package(name: str = "lis_b200"):
     return mod
 
 
-def workload_config(n_gpus: int) -> dict:
-    return {"workload": "paged-attention decode microbench: batch 64 per GPU, 12 heads, head_dim 64, fp16 K/V and q "
-                        "N(0,1), context U[128,1024], block 16, random permutation of a 65536-block pool, scale 1/8",
-            "global_batch": BATCH * n_gpus, "accumulate": "f32", "out_dtype": "f16",
-            "l2": f"inputs larger than L2: {N_SETS} disjoint input sets (~1.8 GB of KV) rotated between launches",
-            "parallelism": f"sequence-sharded x{n_gpus}, no collective"}
+def workload_config(n_gpus: int, n_sets: int | None = None) -> dict:
+    n_sets = WL.n_sets if n_sets is None else n_sets
+    l2 = (f"inputs larger than L2: {n_sets} disjoint input sets rotated between launches" if n_sets > 1 else
+          "inputs larger than L2: one input set of several GB per launch")
+    return {"workload": WL.description, "name": WL.name, "global_batch": WL.batch * n_gpus, "accumulate": "f32",
+            "out_dtype": WL.dtype, "l2": l2, "parallelism": f"sequence-sharded x{n_gpus}, no collective"}
+
+
+def torch_dtype():
+    import torch
+    return torch.float16 if WL.dtype == "f16" else torch.bfloat16
+
+
+def oracle_dtype():
+    from oracle import oracle as O
+    return O.F16 if WL.dtype == "f16" else O.BF16
 
 
 def measured_peak():
@@ -74,7 +120,7 @@ def measured_peak():
 
 def profiled_traffic():
     """dram bytes per launch of the attention kernel from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "paged_decode_microbench.md"
+    p = ROOT / "profiles" / WL.profile
     if not p.exists():
         return None, None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
@@ -143,18 +189,32 @@ class ClockSampler:
 
 # --------------------------------------------------------------- CPU legs
 
-def cpu_attention_rate(wl, budget_s: float, nthreads: int, n_seq=None):
-    """Times the oracle restatement of the reference CPU attention on a host
-    copy of input set 0 (optionally its first n_seq sequences)."""
-    from oracle import oracle as O
+def cpu_sample_seqs():
+    """Sequences of input set 0 the CPU legs start from: the whole mha batch;
+    16 sequences of the gqa batch (~0.5 GB of KV; the whole batch holds ~7 GB)."""
+    return None if WL.name == "mha" else 16
+
+
+def cpu_call(O, q, pool, bt, ctx, nthreads):
+    O.paged_attention(oracle_dtype(), q, WL.n_head * WL.head_dim, pool, bt, ctx, n_head=WL.n_head,
+                      n_kv_head=WL.n_kv_head, head_dim=WL.head_dim, max_blocks_per_seq=bt.shape[1], layer_idx=0,
+                      n_layer=1, nthreads=nthreads)
+
+
+def call_bytes(ctx) -> int:
     from lis_b200.workloads import attention_bytes
-    pool, bt, ctx, q = host_subset(wl, 0, n_seq)
-    nbytes = attention_bytes(ctx, N_HEAD, N_HEAD, HEAD_DIM, 2, 2, 2)
+    return attention_bytes(ctx, WL.n_head, WL.n_kv_head, WL.head_dim, 2, 2, 2)
+
+
+def cpu_attention_rate(wl, budget_s: float, nthreads: int):
+    """Times the oracle restatement of the reference CPU attention on a host
+    copy of (part of) input set 0."""
+    from oracle import oracle as O
+    pool, bt, ctx, q = host_subset(wl, 0, cpu_sample_seqs())
+    nbytes = call_bytes(ctx)
     reps, t0 = 0, time.perf_counter()
     while True:
-        O.paged_attention(O.F16, q, N_HEAD * HEAD_DIM, pool, bt, ctx, n_head=N_HEAD, n_kv_head=N_HEAD,
-                          head_dim=HEAD_DIM, max_blocks_per_seq=bt.shape[1], layer_idx=0, n_layer=1,
-                          nthreads=nthreads)
+        cpu_call(O, q, pool, bt, ctx, nthreads)
         reps += 1
         el = time.perf_counter() - t0
         if el >= budget_s:
@@ -175,46 +235,44 @@ def run_reference_arm(args, rank: int, world: int) -> None:
         return
     import torch
     from oracle import oracle as O
-    from lis_b200.workloads import attention_bytes
     b2 = import_package()
     O.load()
     nthreads = os.cpu_count() or 1
     # Inputs are generated exactly as for the GPU arm (host copy of input set 0).
     if torch.cuda.is_available():
-        wl = b2_workload(b2, torch.device("cuda:0"), seed=0, n_sets=1)
-        pool, bt, ctx, q = host_subset(wl, 0, None)
+        wl = b2_workload(b2, torch.device("cuda:0"), seed=0, n_sets=1, pool_blocks=WL.pool_blocks)
+        pool, bt, ctx, q = host_subset(wl, 0, cpu_sample_seqs())
+        n_batch = wl.batch
         del wl
         torch.cuda.empty_cache()
     else:
-        pool, bt, ctx, q = host_workload(seed=0)
-    nbytes_full = attention_bytes(ctx, N_HEAD, N_HEAD, HEAD_DIM, 2, 2, 2)
+        pool, bt, ctx, q = host_workload(seed=0, n_seq=cpu_sample_seqs())
+        n_batch = WL.batch
+    nbytes_full = call_bytes(ctx)
     t0 = time.perf_counter()
-    O.paged_attention(O.F16, q, N_HEAD * HEAD_DIM, pool, bt, ctx, n_head=N_HEAD, n_kv_head=N_HEAD, head_dim=HEAD_DIM,
-                      max_blocks_per_seq=bt.shape[1], layer_idx=0, n_layer=1, nthreads=nthreads)
+    cpu_call(O, q, pool, bt, ctx, nthreads)
     t_full = time.perf_counter() - t0
     # Size each step so K+W steps stay within ~2 minutes.
     n_seq = len(ctx)
     budget = 120.0
     if (args.steps + args.warmup) * t_full > budget:
         n_seq = max(1, int(len(ctx) * budget / ((args.steps + args.warmup) * t_full)))
-    ctx_s, bt_s, q_s = ctx[:n_seq], bt[:n_seq], q[: n_seq * N_HEAD * HEAD_DIM]
-    nbytes = attention_bytes(ctx_s, N_HEAD, N_HEAD, HEAD_DIM, 2, 2, 2)
+    row = WL.n_head * WL.head_dim
+    ctx_s, bt_s, q_s = ctx[:n_seq], bt[:n_seq], q[: n_seq * row]
+    nbytes = call_bytes(ctx_s)
     for _ in range(args.warmup):
-        O.paged_attention(O.F16, q_s, N_HEAD * HEAD_DIM, pool, bt_s, ctx_s, n_head=N_HEAD, n_kv_head=N_HEAD,
-                          head_dim=HEAD_DIM, max_blocks_per_seq=bt.shape[1], layer_idx=0, n_layer=1,
-                          nthreads=nthreads)
+        cpu_call(O, q_s, pool, bt_s, ctx_s, nthreads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        O.paged_attention(O.F16, q_s, N_HEAD * HEAD_DIM, pool, bt_s, ctx_s, n_head=N_HEAD, n_kv_head=N_HEAD,
-                          head_dim=HEAD_DIM, max_blocks_per_seq=bt.shape[1], layer_idx=0, n_layer=1,
-                          nthreads=nthreads)
+        cpu_call(O, q_s, pool, bt_s, ctx_s, nthreads)
     el = time.perf_counter() - t0
     value = nbytes * args.steps / el / 1e9
-    sample = (f"{n_seq} of {len(ctx)} sequences of one batch per step ({nbytes / 1e6:.1f} MB of "
-              f"{nbytes_full / 1e6:.1f} MB), oracle port of cpu_model.cpp:131-162 through the block table")
+    sample = (f"{n_seq} of the {n_batch} sequences of one batch per step ({nbytes / 1e6:.1f} MB of KV; the first "
+              f"{len(ctx)} sequences hold {nbytes_full / 1e6:.1f} MB), oracle port of cpu_model.cpp:131-162 "
+              f"through the block table")
     line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": WL.dtype, "data": "synthetic",
             "config": workload_config(1),
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
                              "sample": sample},
@@ -222,27 +280,33 @@ def run_reference_arm(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def host_workload(seed: int):
-    """Host-only generation of one batch (used when no GPU is present)."""
+def host_workload(seed: int, n_seq=None):
+    """Host-only generation of one batch, or its first n_seq sequences (used
+    when no GPU is present)."""
     from oracle import oracle as O
     rng = np.random.Generator(np.random.PCG64(seed))
-    ctx = rng.integers(128, 1025, size=BATCH).astype(np.int32)
+    if WL.log_uniform:
+        ctx = np.exp(rng.uniform(np.log(WL.ctx_lo), np.log(WL.ctx_hi), size=WL.batch)).astype(np.int32)
+    else:
+        ctx = rng.integers(WL.ctx_lo, WL.ctx_hi + 1, size=WL.batch).astype(np.int32)
+    ctx = ctx[:n_seq] if n_seq else ctx
     nb = (ctx + 15) // 16
-    bt = np.zeros((BATCH, 64), np.int32)
+    bt = np.zeros((len(ctx), (WL.ctx_hi + 15) // 16), np.int32)
     o = 0
-    for b in range(BATCH):
+    for b in range(len(ctx)):
         bt[b, : nb[b]] = np.arange(o, o + nb[b])
         o += int(nb[b])
-    pool = O.round_to(O.F16, rng.standard_normal(o * 2 * 16 * N_HEAD * HEAD_DIM, dtype=np.float32))
-    q = O.round_to(O.F16, rng.standard_normal(BATCH * N_HEAD * HEAD_DIM, dtype=np.float32))
+    dt = oracle_dtype()
+    pool = O.round_to(dt, rng.standard_normal(o * 2 * 16 * WL.n_kv_head * WL.head_dim, dtype=np.float32))
+    q = O.round_to(dt, rng.standard_normal(len(ctx) * WL.n_head * WL.head_dim, dtype=np.float32))
     return pool, bt, ctx, q
 
 
-def b2_workload(b2, device, seed: int, n_sets: int, pool_blocks: int = 65536):
-    import torch
+def b2_workload(b2, device, seed: int, n_sets: int, pool_blocks: int, batch: int | None = None):
     from lis_b200.workloads import make_attention_workload
-    return make_attention_workload(device, seed=seed, n_sets=n_sets, batch=BATCH, n_head=N_HEAD, n_kv_head=N_HEAD,
-                                   head_dim=HEAD_DIM, dtype=torch.float16, pool_blocks=pool_blocks)
+    return make_attention_workload(device, seed=seed, n_sets=n_sets, batch=batch or WL.batch, n_head=WL.n_head,
+                                   n_kv_head=WL.n_kv_head, head_dim=WL.head_dim, ctx_lo=WL.ctx_lo, ctx_hi=WL.ctx_hi,
+                                   pool_blocks=pool_blocks, dtype=torch_dtype(), log_uniform=WL.log_uniform)
 
 
 def run_ours(args, rank: int, world: int, dist) -> None:
@@ -251,7 +315,8 @@ def run_ours(args, rank: int, world: int, dist) -> None:
     b2.load()
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
-    wl = b2_workload(b2, dev, seed=1000 + rank, n_sets=args.sets, pool_blocks=args.pool_blocks)
+    wl = b2_workload(b2, dev, seed=1000 + rank, n_sets=args.sets or WL.n_sets,
+                     pool_blocks=args.pool_blocks or WL.pool_blocks, batch=args.batch)
     # A non-default stream (graph capture needs one) that every torch op below uses too.
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
@@ -370,17 +435,20 @@ def run_ours(args, rank: int, world: int, dist) -> None:
     per_launch_s = ms * 1e-3 / args.steps
     achieved = per_launch_bytes / per_launch_s / 1e9
     traffic, traffic_alg = profiled_traffic()
+    tc_path = (WL.n_kv_head == 8 and WL.head_dim == 128 and
+               not os.environ.get("B2_ATTENTION_TENSOR_CORES", "1").startswith("0"))
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(t_max / args.steps, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": workload_config(world),
+        "scaling": "weak", "vs_baseline": None, "dtype": WL.dtype, "data": "synthetic",
+        "config": workload_config(world, len(wl.sets)),
         "pct_of_peak": round(100.0 * value / (peak * world), 2),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": traffic, "traffic_note": "dram read+write bytes per launch from the committed ncu "
-                                                         "summary (profiles/paged_decode_microbench.md)"
+                     "traffic": traffic, "traffic_note": "dram read+write bytes per launch of the attention kernel "
+                                                         f"from the committed ncu summary (profiles/{WL.profile})"
                      if traffic else "no ncu summary committed yet",
+                     "kernel": "paged_decode_tc_kernel (tcgen05)" if tc_path else "paged_decode_kernel",
                      "algorithmic_bytes_per_launch": int(per_launch_bytes),
                      "vs_nominal_8TBs": round(achieved / 8000.0, 4)},
         "cpu_baseline": cpu,
@@ -389,7 +457,7 @@ def run_ours(args, rank: int, world: int, dist) -> None:
                 "path": "b2_paged_attention via ctypes; pinned-host q/block tables/seq_lens up, output down, "
                         "stream sync every step"},
         "clocks": clk.summary(),
-        "gpu_launches": args.steps,
+        "gpu_launches": 2 * args.steps,  # split attention kernel + merge kernel per step
         "device_errors": errs,
     }
     print(json.dumps(line), flush=True)
@@ -403,11 +471,16 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--sets", type=int, default=N_SETS, help="rotating input sets (profiling uses fewer)")
-    ap.add_argument("--pool-blocks", type=int, default=65536, help="KV pool size in blocks (profiling uses fewer)")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mha",
+                    help="mha: the headline microbench; gqa: grouped-query long contexts (tensor-core kernel)")
+    ap.add_argument("--sets", type=int, default=None, help="rotating input sets (profiling uses fewer)")
+    ap.add_argument("--pool-blocks", type=int, default=None, help="KV pool size in blocks (profiling uses fewer)")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (profiling uses fewer)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    global WL
+    WL = WORKLOADS[args.workload]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
