@@ -463,28 +463,113 @@ def run_ours(args, rank: int, world: int, dist) -> None:
     print(json.dumps(line), flush=True)
 
 
+ENGINE_NAMES = ("gpt2-xl", "gpt2-medium")
+
+
+def run_engine(args, rank: int, world: int, dist) -> None:
+    """GPT-2 decode tokens/s through b2_engine_decode_step (engine_bench.py)."""
+    import torch
+    import_package()
+    from lis_b200 import engine_bench as EB
+    w = EB.ENGINE_WORKLOADS[args.workload]
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    samplers: list[ClockSampler] = []
+
+    def timed_region():  # clocks are sampled during the timed steps of each wave only
+        samplers.append(ClockSampler(dev.index))
+        return samplers[-1]
+
+    r = EB.run(w, args.steps, args.warmup, rank, world, dist, dev, timed_region)
+    clk = samplers[0]
+    for extra in samplers[1:]:
+        clk.samples.extend(extra.samples)
+
+    def reduce(x: float, op) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    import torch.distributed as tdist
+    t_max = reduce(r["ms"], tdist.ReduceOp.MAX if dist else None)
+    tokens = reduce(float(r["tokens"]), tdist.ReduceOp.SUM if dist else None)
+    nbytes = reduce(r["bytes"], tdist.ReduceOp.SUM if dist else None)
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    value = tokens / (t_max * 1e-3)
+    achieved = nbytes / (t_max * 1e-3) / 1e9  # whole job, GB/s
+    frac = achieved / (peak * world)
+    steps_total = args.steps * r["waves"]
+    es = EB.elem_bytes(w.dtype)
+    mbps = (w.n_ctx + 15) // 16
+    ours_per_step = 1 + 6 * w.n_layer + 2  # embedding, per layer LN/append/attention x2/LN/GELU, final LN, argmax
+    line = {
+        "metric": "GPT-2 decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_max / steps_total, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": {BF16_CODE: "bf16", 1: "f16", 0: "f32"}[w.dtype], "data": "synthetic",
+        "config": {"workload": w.description, "name": w.name, "global_batch": w.global_batch,
+                   "per_gpu_batch": r["per_rank"], "waves_per_gpu": r["waves"], "wave": r["wave"],
+                   "l2": "inputs larger than L2: every step reads all weights (GB) and every cached KV row",
+                   "parallelism": f"sequence-sharded x{world}, one engine and KV pool per GPU, no collective"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved / world, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(frac, 4), "peak_kind": peak_kind, "traffic": None,
+                     "traffic_note": "per GPU; algorithmic bytes per step = all weights + every cached K/V row "
+                                     "of every layer + the appended rows",
+                     "roofline_tok_s": round(value / frac, 1)},
+        "cpu_baseline": None,
+        "e2e": {"value": round(value, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * (3 * r["wave"] + r["wave"] * mbps),
+                "d2h_bytes_per_step": 4 * r["wave"],
+                "path": "value is already end to end: b2_engine_decode_step (host block tables, one upload, graph "
+                        "replay, download of next tokens, stream sync) timed with CUDA events on the engine stream"},
+        "clocks": clk.summary(),
+        "gpu_launches": ours_per_step * steps_total,
+        "elem_bytes": es,
+    }
+    print(json.dumps(line), flush=True)
+
+
+BF16_CODE = 2
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 5000; 20 for engine workloads)")
+    ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (default 50; 3 for engine workloads)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mha",
-                    help="mha: the headline microbench; gqa: grouped-query long contexts (tensor-core kernel)")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + list(ENGINE_NAMES), default="mha",
+                    help="mha: the headline microbench; gqa: grouped-query long contexts (tensor-core kernel); "
+                         "gpt2-xl / gpt2-medium: GPT-2 decode tokens/s through the engine")
     ap.add_argument("--sets", type=int, default=None, help="rotating input sets (profiling uses fewer)")
     ap.add_argument("--pool-blocks", type=int, default=None, help="KV pool size in blocks (profiling uses fewer)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (profiling uses fewer)")
     args = ap.parse_args()
+    engine = args.workload in ENGINE_NAMES
+    if args.steps is None:
+        args.steps = 20 if engine else 5000
+    if args.warmup is None:
+        args.warmup = 3 if engine else 50
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     global WL
-    WL = WORKLOADS[args.workload]
+    if not engine:
+        WL = WORKLOADS[args.workload]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
+        if engine:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference CPU arm is timed for the "
+                                  "attention workloads; engine workloads report no CPU arm"}), flush=True)
+            return
         run_reference_arm(args, rank, world)
         return
     dist = None
@@ -497,7 +582,10 @@ def main() -> None:
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         dist = tdist
     try:
-        run_ours(args, rank, world, dist)
+        if engine:
+            run_engine(args, rank, world, dist)
+        else:
+            run_ours(args, rank, world, dist)
     finally:
         if dist is not None:
             dist.destroy_process_group()

@@ -223,6 +223,13 @@ B2_API int b2_embedding(int32_t dtype, void* out, const void* wte, const void* w
 B2_API int b2_argmax(int32_t dtype, int32_t* out_tokens, const void* logits, int32_t batch,
               int32_t vocab, b2_stream_t stream);
 
+/* b2_argmax over rows row_stride elements apart (row_stride >= vocab).  No
+ * reference counterpart: a caller that pads each logits row to a multiple of
+ * 16 bytes (so GEMMs writing them stay vector-aligned) gets 16-byte vector
+ * reads here. */
+B2_API int b2_argmax_rows(int32_t dtype, int32_t* out_tokens, const void* logits, int64_t row_stride,
+                          int32_t batch, int32_t vocab, b2_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

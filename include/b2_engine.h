@@ -59,7 +59,9 @@ B2_API int b2_engine_create(const char* weights_dir, const B2EngineConfig* cfg, 
 
 /* Bench hook: weights drawn on the device, every matrix, embedding and bias
  * ~ N(0, std) from a counter-based generator keyed by seed, LayerNorm gamma 1
- * and beta 0 -- for model sizes where writing weight files is pointless. */
+ * and beta 0 -- for model sizes where writing weight files is pointless.  The
+ * KV pool is filled with N(0, 1) values, so sequences added with
+ * b2_engine_add_sequence_cached attend over random keys and values. */
 B2_API int b2_engine_create_synthetic(const B2ModelShape* shape, uint64_t seed, float std,
                                       const B2EngineConfig* cfg, b2_engine** out);
 

@@ -30,7 +30,7 @@ DECODE_SYMBOLS = (
     "b2_version", "b2_last_error_string", "b2_device_errors", "b2_kv_append",
     "b2_paged_attention_workspace_bytes", "b2_paged_attention",
     "b2_add_layernorm", "b2_bias_gelu", "b2_add_bias", "b2_add_one", "b2_embedding", "b2_argmax",
-    "b2_paged_attention_noalloc",
+    "b2_paged_attention_noalloc", "b2_argmax_rows",
 )
 
 _c_int, _c_float, _vp = ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
@@ -86,6 +86,7 @@ def load() -> ctypes.CDLL:
     lib.b2_add_one.argtypes = [_vp, _vp, _c_int, _vp]
     lib.b2_embedding.argtypes = [_c_int, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]
     lib.b2_argmax.argtypes = [_c_int, _vp, _vp, _c_int, _c_int, _vp]
+    lib.b2_argmax_rows.argtypes = [_c_int, _vp, _vp, ctypes.c_int64, _c_int, _c_int, _vp]
     _lib = lib
     return lib
 
@@ -179,6 +180,14 @@ def embedding(out, wte, wpe, token_ids, positions, stream=None):
                                _stream(stream)))
 
 
-def argmax(out_tokens, logits, stream=None):
+def argmax(out_tokens, logits, stream=None, vocab=None):
+    """Row-wise greedy argmax.  A contiguous [batch, vocab] tensor goes through
+    b2_argmax; with vocab < logits.shape[1] (padded rows) or a strided view,
+    through b2_argmax_rows."""
     b, v = logits.shape
-    _check(load().b2_argmax(dtype_code(logits.dtype), _ptr(out_tokens), _ptr(logits), b, v, _stream(stream)))
+    vocab = v if vocab is None else vocab
+    if vocab == v and logits.is_contiguous():
+        _check(load().b2_argmax(dtype_code(logits.dtype), _ptr(out_tokens), _ptr(logits), b, v, _stream(stream)))
+    else:
+        _check(load().b2_argmax_rows(dtype_code(logits.dtype), _ptr(out_tokens), _ptr(logits), logits.stride(0), b,
+                                     vocab, _stream(stream)))

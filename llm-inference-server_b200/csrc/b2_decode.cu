@@ -616,20 +616,22 @@ int b2_add_layernorm(int32_t dtype, void* out, void* residual_out, const void* x
     if (!aligned16(out) || !aligned16(residual_in) || !aligned16(gamma) || !aligned16(beta) ||
         (x && !aligned16(x)) || (bias && !aligned16(bias)) || (residual_out && !aligned16(residual_out)))
         return fail(B2_ERR_ALIGN, "pointers must be 16-byte aligned");
-    const int per_lane = (d_model / E + 31) / 32;
-    if (per_lane > 16) return fail(B2_ERR_UNSUPPORTED, "d_model too large for the one-warp-per-row kernel");
-    const int grid = (batch + 3) / 4;
+    // One CTA per row, one to four 16-byte chunks per thread.
+    const int nch = d_model / E;
+    const int per_thread = nch <= 1024 ? 1 : (nch <= 2048 ? 2 : 4);
+    if (nch > 4 * 1024) return fail(B2_ERR_UNSUPPORTED, "d_model too large for the one-CTA-per-row kernel");
+    const int threads = static_cast<int>(align_up(static_cast<size_t>((nch + per_thread - 1) / per_thread), 32));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define B2_LN_LAUNCH(T, N)                                                                                     \
-    add_layernorm_kernel<T, N><<<grid, 128, 0, s>>>(static_cast<T*>(out), static_cast<T*>(residual_out),      \
-                                                    static_cast<const T*>(x), static_cast<const T*>(bias),       \
-                                                    static_cast<const T*>(residual_in), static_cast<const T*>(gamma), \
-                                                    static_cast<const T*>(beta), batch, d_model, eps)
-#define B2_LN_DISPATCH(T)              \
-    if (per_lane <= 2) B2_LN_LAUNCH(T, 2);      \
-    else if (per_lane <= 4) B2_LN_LAUNCH(T, 4); \
-    else if (per_lane <= 8) B2_LN_LAUNCH(T, 8); \
-    else B2_LN_LAUNCH(T, 16);
+#define B2_LN_LAUNCH(T, N)                                                                                         \
+    add_layernorm_kernel<T, N><<<batch, threads, 0, s>>>(static_cast<T*>(out), static_cast<T*>(residual_out),    \
+                                                         static_cast<const T*>(x), static_cast<const T*>(bias),     \
+                                                         static_cast<const T*>(residual_in),                        \
+                                                         static_cast<const T*>(gamma), static_cast<const T*>(beta), \
+                                                         d_model, eps)
+#define B2_LN_DISPATCH(T)                      \
+    if (per_thread == 1) B2_LN_LAUNCH(T, 1);      \
+    else if (per_thread == 2) B2_LN_LAUNCH(T, 2); \
+    else B2_LN_LAUNCH(T, 4);
     if (dtype == B2_F32) {
         B2_LN_DISPATCH(float)
     } else if (dtype == B2_F16) {
@@ -730,21 +732,28 @@ int b2_embedding(int32_t dtype, void* out, const void* wte, const void* wpe, con
     return launch_status();
 }
 
-int b2_argmax(int32_t dtype, int32_t* out_tokens, const void* logits, int32_t batch, int32_t vocab,
-              b2_stream_t stream) {
+int b2_argmax_rows(int32_t dtype, int32_t* out_tokens, const void* logits, int64_t row_stride, int32_t batch,
+                   int32_t vocab, b2_stream_t stream) {
     if (!dtype_ok(dtype)) return fail(B2_ERR_DTYPE, "unknown dtype");
-    if (batch < 0 || vocab <= 0) return fail(B2_ERR_SHAPE, "bad sizes");
+    if (batch < 0 || vocab <= 0 || row_stride < vocab) return fail(B2_ERR_SHAPE, "bad sizes (row_stride < vocab?)");
     if (batch == 0) return B2_OK;
     if (!out_tokens || !logits) return fail(B2_ERR_NULL, "out_tokens and logits are required");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (dtype == B2_F32)
-        argmax_kernel<float><<<batch, 256, 0, s>>>(out_tokens, static_cast<const float*>(logits), vocab);
-    else if (dtype == B2_F16)
-        argmax_kernel<__half><<<batch, 256, 0, s>>>(out_tokens, static_cast<const __half*>(logits), vocab);
-    else
-        argmax_kernel<__nv_bfloat16><<<batch, 256, 0, s>>>(out_tokens, static_cast<const __nv_bfloat16*>(logits),
-                                                           vocab);
+    const bool vec = aligned16(logits) && (row_stride * dtype_size(dtype)) % 16 == 0;
+    const long long st = row_stride;
+#define B2_ARGMAX(T)                                                                                     \
+    (vec ? argmax_kernel<T, true><<<batch, 512, 0, s>>>(out_tokens, static_cast<const T*>(logits), vocab, st) \
+         : argmax_kernel<T, false><<<batch, 512, 0, s>>>(out_tokens, static_cast<const T*>(logits), vocab, st))
+    if (dtype == B2_F32) B2_ARGMAX(float);
+    else if (dtype == B2_F16) B2_ARGMAX(__half);
+    else B2_ARGMAX(__nv_bfloat16);
+#undef B2_ARGMAX
     return launch_status();
+}
+
+int b2_argmax(int32_t dtype, int32_t* out_tokens, const void* logits, int32_t batch, int32_t vocab,
+              b2_stream_t stream) {
+    return b2_argmax_rows(dtype, out_tokens, logits, vocab, batch, vocab, stream);
 }
 
 }  // extern "C"

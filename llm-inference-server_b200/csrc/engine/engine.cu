@@ -197,17 +197,37 @@ struct Engine {
         if (cfg.dtype != B2_F32 && cfg.dtype != B2_F16 && cfg.dtype != B2_BF16) throw Error(B2_ERR_DTYPE, "unknown dtype");
     }
 
-    // Weight arena: every tensor at a 256-byte aligned offset, in file order.
+    // Vocabulary rounded up to a multiple of 8: wte (the tied lm_head) gets
+    // zero rows up to it and the logits rows are that long, so the lm_head GEMM
+    // has 16-byte aligned rows and columns.  With the odd GPT-2 vocabulary
+    // (50257) cuBLAS otherwise falls back to its slow unaligned kernels.
+    int vocab_padded() const { return (shape.vocab_size + 7) / 8 * 8; }
+
+    // Weight arena: every tensor at a 256-byte aligned offset, in file order
+    // (wte sized for vocab_padded() rows).
     std::vector<size_t> layout(const std::vector<TensorSpec>& specs, size_t* total) const {
         std::vector<size_t> off;
         size_t o = 0;
-        for (const auto& t : specs) {
+        for (size_t i = 0; i < specs.size(); ++i) {
             off.push_back(o);
-            o = align256(o + numel(t.shape) * es);
+            const size_t n = i == 0 ? static_cast<size_t>(vocab_padded()) * shape.d_model : numel(specs[i].shape);
+            o = align256(o + n * es);
         }
         *total = o;
         return off;
     }
+
+    // The KV cache is layer-major: layer l owns a contiguous
+    // [num_blocks][K|V][16][n_head][head_dim] region (the paged layout of
+    // gpu-engine/include/engine/kv_cache.h:6-8 with n_layer = 1), and a block
+    // id names the same slot in every layer.  With all layers inside each
+    // block, the slabs one layer's attention reads sit a whole block (4.9 MB
+    // for GPT-2 XL) apart, each on its own 2 MB page; over a 100 GB pool the
+    // page-translation misses cost attention ~30% of its bandwidth.
+    size_t layer_bytes() const {
+        return static_cast<size_t>(num_blocks) * 2 * B2_BLOCK_TOKENS * shape.n_head * head_dim * es;
+    }
+    void* layer_pool(int l) const { return static_cast<char*>(pool) + static_cast<size_t>(l) * layer_bytes(); }
 
     void bind_tensors(const std::vector<size_t>& off) {
         auto at = [&](size_t i) { return static_cast<const void*>(static_cast<char*>(weights) + off[i]); };
@@ -254,10 +274,8 @@ struct Engine {
         const int B = cfg.max_batch, D = shape.d_model, V = shape.vocab_size;
         mbps = (cfg.max_seq_len + B2_BLOCK_TOKENS - 1) / B2_BLOCK_TOKENS;
         num_blocks = cfg.kv_block_budget;
-        const size_t block_bytes =
-            static_cast<size_t>(shape.n_layer) * 2 * B2_BLOCK_TOKENS * shape.n_head * head_dim * es;
-        cuda_ok(cudaMalloc(&pool, block_bytes * num_blocks), "malloc KV pool");
-        cuda_ok(cudaMemsetAsync(pool, 0, block_bytes * num_blocks, stream), "memset KV pool");
+        cuda_ok(cudaMalloc(&pool, layer_bytes() * shape.n_layer), "malloc KV pool");
+        cuda_ok(cudaMemsetAsync(pool, 0, layer_bytes() * shape.n_layer, stream), "memset KV pool");
         blocks = std::make_unique<BlockPool>(num_blocks);
         const size_t in_ints = 3 * static_cast<size_t>(B) + static_cast<size_t>(B) * mbps;
         cuda_ok(cudaMalloc(&d_in, in_ints * 4), "malloc step inputs");
@@ -275,7 +293,7 @@ struct Engine {
         act(&d_attn_out, D, "malloc proj out");
         act(&d_ff, 4 * static_cast<size_t>(D), "malloc ff");
         act(&d_ff_out, D, "malloc ff out");
-        act(&d_logits, V, "malloc logits");
+        act(&d_logits, static_cast<size_t>(vocab_padded()), "malloc logits");
         B2PagedAttnArgs a = attn_args(B, 0);
         attn_ws_bytes = b2_paged_attention_workspace_bytes(&a);
         if (attn_ws_bytes == 0) throw Error(B2_ERR_UNSUPPORTED, std::string("attention shape: ") + b2_last_error_string());
@@ -290,7 +308,7 @@ struct Engine {
         a.out_dtype = dt;
         a.q = d_qkv;
         a.q_row_stride = 3 * shape.d_model;
-        a.kv_pool = pool;
+        a.kv_pool = layer_pool(layer);
         a.block_tables = in_tables();
         a.seq_lens = d_seq_post;
         a.out = d_attn;
@@ -299,19 +317,20 @@ struct Engine {
         a.n_kv_head = shape.n_head;
         a.head_dim = head_dim;
         a.max_blocks_per_seq = mbps;
-        a.layer_idx = layer;
-        a.n_layer = shape.n_layer;
+        a.layer_idx = 0;
+        a.n_layer = 1;
         a.num_blocks = num_blocks;
         return a;
     }
 
     // Row-major Y[batch, O] = X[batch, I] . W^T with W row-major [O, I]: the
-    // convention of gpu-engine/include/engine/kernels.h:9-20.
-    void gemm(int batch, int I, int O, const void* X, const void* W, void* Y) {
+    // convention of gpu-engine/include/engine/kernels.h:9-20.  ldy (>= O) is the
+    // row stride of Y.
+    void gemm(int batch, int I, int O, const void* X, const void* W, void* Y, int ldy = 0) {
         const float alpha = 1.0f, beta = 0.0f;
         const cudaDataType_t t = dt == B2_F32 ? CUDA_R_32F : (dt == B2_F16 ? CUDA_R_16F : CUDA_R_16BF);
-        cublas_ok(cublasGemmEx(cublas, CUBLAS_OP_T, CUBLAS_OP_N, O, batch, I, &alpha, W, t, I, X, t, I, &beta, Y, t, O,
-                               CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
+        cublas_ok(cublasGemmEx(cublas, CUBLAS_OP_T, CUBLAS_OP_N, O, batch, I, &alpha, W, t, I, X, t, I, &beta, Y, t,
+                               ldy > 0 ? ldy : O, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
                   "cublasGemmEx");
     }
 
@@ -329,7 +348,7 @@ struct Engine {
             gemm(bucket, D, 3 * D, d_x, w.qkv_w, d_qkv);
             B2KvAppendArgs ka{};
             ka.dtype = dt;
-            ka.kv_pool = pool;
+            ka.kv_pool = layer_pool(l);
             ka.k = qkv + static_cast<size_t>(D) * es;
             ka.v = qkv + 2 * static_cast<size_t>(D) * es;
             ka.kv_row_stride = 3 * D;
@@ -342,8 +361,8 @@ struct Engine {
             ka.n_kv_head = shape.n_head;
             ka.head_dim = head_dim;
             ka.max_blocks_per_seq = mbps;
-            ka.layer_idx = l;
-            ka.n_layer = L;
+            ka.layer_idx = 0;
+            ka.n_layer = 1;
             ka.num_blocks = num_blocks;
             b2_ok(b2_kv_append(&ka, s), "kv_append");
             B2PagedAttnArgs aa = attn_args(bucket, l);
@@ -358,8 +377,10 @@ struct Engine {
             delta_bias = w.fc_proj_b;
         }
         b2_ok(b2_add_layernorm(dt, d_x, d_resid, delta, delta_bias, d_resid, lnf_g, lnf_b, bucket, D, eps, s), "ln_f");
-        gemm(bucket, D, V, d_x, wte, d_logits);  // lm_head tied to wte
-        b2_ok(b2_argmax(dt, d_next, d_logits, bucket, V, s), "argmax");
+        // lm_head tied to wte, over the padded vocabulary (pad logits are 0 and
+        // never read by the argmax)
+        gemm(bucket, D, vocab_padded(), d_x, wte, d_logits, vocab_padded());
+        b2_ok(b2_argmax_rows(dt, d_next, d_logits, vocab_padded(), bucket, V, s), "argmax");
     }
 
     cudaGraphExec_t graph_for(int bucket) {
@@ -492,6 +513,7 @@ void load_weights(Engine& e, const std::string& dir) {
     char* staging = nullptr;
     cuda_ok(cudaMallocHost(&staging, total), "pinned weight staging");
     std::unique_ptr<char, void (*)(char*)> guard(staging, [](char* p) { cudaFreeHost(p); });
+    std::memset(staging, 0, total);  // padding, including wte's zero rows past the vocabulary
     double checksum = 0.0;
     for (size_t i = 0; i < specs.size(); ++i) {
         auto it = by_name.find(specs[i].name);
@@ -528,6 +550,7 @@ void synth_weights(Engine& e, uint64_t seed, float stdev) {
     size_t total = 0;
     const auto off = e.layout(specs, &total);
     cuda_ok(cudaMalloc(&e.weights, total), "malloc weights");
+    cuda_ok(cudaMemsetAsync(e.weights, 0, total, e.stream), "memset weights");  // wte's zero rows past the vocabulary
     for (size_t i = 0; i < specs.size(); ++i) {
         void* dst = static_cast<char*>(e.weights) + off[i];
         const size_t n = numel(specs[i].shape);
@@ -550,6 +573,19 @@ void synth_weights(Engine& e, uint64_t seed, float stdev) {
     }
     cuda_ok(cudaStreamSynchronize(e.stream), "synthetic weights");
     e.bind_tensors(off);
+}
+
+// Bench hook: the KV pool of a synthetic engine holds N(0, 1) values instead
+// of zeros, so cached contexts look like real keys and values.
+void synth_pool(Engine& e, uint64_t seed) {
+    const size_t n = static_cast<size_t>(e.shape.n_layer) * 2 * B2_BLOCK_TOKENS * e.shape.d_model * e.num_blocks;
+    const uint64_t key = seed * 0x9e3779b97f4a7c15ull + 0x6b7650ull;
+    const int grid = 148 * 32;
+    if (e.dt == B2_F32) synth_normal_kernel<float><<<grid, 256, 0, e.stream>>>(static_cast<float*>(e.pool), n, key, 1.0f);
+    else if (e.dt == B2_F16) synth_normal_kernel<__half><<<grid, 256, 0, e.stream>>>(static_cast<__half*>(e.pool), n, key, 1.0f);
+    else synth_normal_kernel<__nv_bfloat16><<<grid, 256, 0, e.stream>>>(static_cast<__nv_bfloat16*>(e.pool), n, key, 1.0f);
+    cuda_ok(cudaGetLastError(), "synthetic KV pool");
+    cuda_ok(cudaStreamSynchronize(e.stream), "synthetic KV pool");
 }
 
 template <typename F>
@@ -615,6 +651,7 @@ int b2_engine_create_synthetic(const B2ModelShape* shape, uint64_t seed, float s
         e->setup_device();
         b2::eng::synth_weights(*e, seed, stdev);
         e->setup_buffers();
+        b2::eng::synth_pool(*e, seed);
     });
     if (rc == B2_OK) *out = e.release();
     return rc;

@@ -13,28 +13,47 @@
 namespace b2 {
 
 // ------------------------------------------------------ add + LayerNorm
-// r = x + bias + residual_in; residual_out = r; out = LN(r) * gamma + beta.
-// One warp per row; each lane keeps up to NCH 16-byte chunks of r in
-// registers, so the row is read once and written once.  Mean and variance
-// are accumulated in double and the normalised value is formed as
+// r = residual_in + (x + bias); residual_out = r; out = LN(r) * gamma + beta.
+// One CTA per row, each thread holding NCH 16-byte chunks of r in registers
+// (the row is read once and written once).  Mean and variance are
+// accumulated in double and the normalised value is formed as
 // float((r - mean) * inv_std) * gamma + beta, the expression of
 // cpu_model.cpp:33-45 (layernorm.cu:34-38 instead re-reads the half-rounded
 // residual; this kernel does not).
+
+// Sum over the CTA; every thread gets the result.  red needs 33 doubles.
+__device__ __forceinline__ double block_sum(double v, double* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = (blockDim.x + 31) >> 5;
+        double w = lane < nw ? red[lane] : 0.0;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) w += __shfl_xor_sync(0xffffffffu, w, off);
+        if (lane == 0) red[32] = w;
+    }
+    __syncthreads();
+    const double total = red[32];
+    __syncthreads();  // red is reused by the next call
+    return total;
+}
+
 template <typename T, int NCH>
-__global__ void __launch_bounds__(128) add_layernorm_kernel(T* out, T* residual_out, const T* x, const T* bias,
-                                                            const T* residual_in, const T* gamma, const T* beta,
-                                                            int batch, int d, float eps) {
+__global__ void __launch_bounds__(1024) add_layernorm_kernel(T* out, T* residual_out, const T* x, const T* bias,
+                                                             const T* residual_in, const T* gamma, const T* beta,
+                                                             int d, float eps) {
     constexpr int E = Elem<T>::kPer16B;
-    const int row = static_cast<int>((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= batch) return;
+    __shared__ double red[33];
     const int nch = d / E;
-    const size_t base = static_cast<size_t>(row) * d;
+    const size_t base = static_cast<size_t>(blockIdx.x) * d;
     float v[NCH][E];
     double sum = 0.0;
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
-        const int c = lane + 32 * i;
+        const int c = threadIdx.x + i * static_cast<int>(blockDim.x);
         if (c < nch) {
             // r = residual + (x + bias): the bias belongs to the GEMM output x,
             // as in the reference (add_bias before the residual add,
@@ -64,13 +83,11 @@ __global__ void __launch_bounds__(128) add_layernorm_kernel(T* out, T* residual_
             }
         }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    const double mean = sum / d;
+    const double mean = block_sum(sum, red) / d;
     double var = 0.0;
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
-        const int c = lane + 32 * i;
+        const int c = threadIdx.x + i * static_cast<int>(blockDim.x);
         if (c < nch) {
 #pragma unroll
             for (int e = 0; e < E; ++e) {
@@ -79,13 +96,11 @@ __global__ void __launch_bounds__(128) add_layernorm_kernel(T* out, T* residual_
             }
         }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) var += __shfl_xor_sync(0xffffffffu, var, off);
-    var /= d;
+    var = block_sum(var, red) / d;
     const float inv_std = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
-        const int c = lane + 32 * i;
+        const int c = threadIdx.x + i * static_cast<int>(blockDim.x);
         if (c < nch) {
             float gf[E], bf[E], y[E];
             unpack16<T>(__ldg(reinterpret_cast<const uint4*>(gamma) + c), gf);
@@ -173,28 +188,55 @@ __global__ void __launch_bounds__(256) embedding_kernel(T* out, const T* wte, co
 
 // ------------------------------------------------------ greedy argmax
 // One CTA per row; ties go to the lowest index (cpu_model.cpp:190 keeps the
-// first maximum).  Rows need not be 16-byte aligned (vocab 50257 is odd), so
-// loads are per element, coalesced across the CTA.
-template <typename T>
-__global__ void __launch_bounds__(256) argmax_kernel(int* out_tokens, const T* logits, int vocab) {
-    const T* row = logits + static_cast<size_t>(blockIdx.x) * vocab;
+// first maximum).  Rows that start on a 16-byte boundary (a row stride that
+// is a multiple of 16 bytes, as the engine pads its logits) are read in
+// 16-byte vectors, several in flight per thread; otherwise (vocab 50257 as the
+// row stride) element by element, coalesced across the CTA.
+__device__ __forceinline__ void argmax_take(float x, int i, float& best, int& best_i) {
+    if (x > best || (x == best && i < best_i)) {
+        best = x;
+        best_i = i;
+    }
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(512) argmax_kernel(int* out_tokens, const T* logits, int vocab, long long stride) {
+    const T* row = logits + static_cast<long long>(blockIdx.x) * stride;
     float best = -INFINITY;
     int best_i = 0x7fffffff;
-    for (int v = threadIdx.x; v < vocab; v += blockDim.x) {
-        const float x = Elem<T>::to_f(row[v]);
-        if (x > best) {
-            best = x;
-            best_i = v;
+    if constexpr (VEC) {
+        constexpr int E = Elem<T>::kPer16B;
+        constexpr int U = 4;  // vectors in flight per thread
+        const int nvec = vocab / E;
+        const uint4* rv = reinterpret_cast<const uint4*>(row);
+        for (int base = threadIdx.x; base < nvec; base += U * blockDim.x) {
+            uint4 raw[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int idx = base + u * static_cast<int>(blockDim.x);
+                raw[u] = idx < nvec ? __ldg(rv + idx) : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int idx = base + u * static_cast<int>(blockDim.x);
+                if (idx < nvec) {
+                    float f[E];
+                    unpack16<T>(raw[u], f);
+#pragma unroll
+                    for (int e = 0; e < E; ++e) argmax_take(f[e], idx * E + e, best, best_i);
+                }
+            }
         }
+        for (int v = nvec * E + static_cast<int>(threadIdx.x); v < vocab; v += blockDim.x)
+            argmax_take(Elem<T>::to_f(row[v]), v, best, best_i);
+    } else {
+        for (int v = threadIdx.x; v < vocab; v += blockDim.x) argmax_take(Elem<T>::to_f(row[v]), v, best, best_i);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, best, off);
         const int oi = __shfl_xor_sync(0xffffffffu, best_i, off);
-        if (ob > best || (ob == best && oi < best_i)) {
-            best = ob;
-            best_i = oi;
-        }
+        argmax_take(ob, oi, best, best_i);
     }
     __shared__ float s_best[32];
     __shared__ int s_idx[32];
@@ -212,10 +254,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(int* out_tokens, const T* l
         for (int off = 16; off > 0; off >>= 1) {
             const float ob = __shfl_xor_sync(0xffffffffu, best, off);
             const int oi = __shfl_xor_sync(0xffffffffu, best_i, off);
-            if (ob > best || (ob == best && oi < best_i)) {
-                best = ob;
-                best_i = oi;
-            }
+            argmax_take(ob, oi, best, best_i);
         }
         if (lane == 0) out_tokens[blockIdx.x] = best_i == 0x7fffffff ? 0 : best_i;
     }

@@ -93,7 +93,7 @@ def test_row_kernel_host_checks(b2):
     lib = b2.load()
     assert lib.b2_add_layernorm(5, 16, 16, 16, None, 16, 16, 16, 4, 768, 1e-5, None) == -2
     assert lib.b2_add_layernorm(1, 16, 16, 16, None, 16, 16, 16, 4, 770, 1e-5, None) == -3
-    assert lib.b2_add_layernorm(1, 16, 16, 16, None, 16, 16, 16, 4, 8 * 32 * 17, 1e-5, None) == -6
+    assert lib.b2_add_layernorm(1, 16, 16, 16, None, 16, 16, 16, 4, 8 * 4097, 1e-5, None) == -6  # > 4096 chunks
     assert lib.b2_add_layernorm(1, None, 16, 16, None, 16, 16, 16, 4, 768, 1e-5, None) == -1
     assert lib.b2_bias_gelu(1, 16, 16, 18, 2, 3072, None) == -4
     assert lib.b2_add_bias(0, 16, 16, 16, 2, 6, None) == -3

@@ -321,6 +321,14 @@ def test_embedding_and_argmax(b2, cuda, dt):
     b2.argmax(toks, to_dev(dt, logits))
     torch.cuda.synchronize()
     assert toks.cpu().numpy().tolist() == O.argmax(dt, logits).tolist()
+    # padded rows (the engine's 16-byte row stride): vector path, padding ignored
+    padded = np.zeros((B, 50264), dtype=logits.dtype)
+    padded[:, :50257] = logits
+    padded[:, 50257:] = O.round_to(dt, np.full((B, 7), 1e4, np.float32))  # larger than any logit
+    toks2 = torch.empty(B, dtype=torch.int32, device="cuda")
+    b2.argmax(toks2, to_dev(dt, padded.ravel()).view(B, 50264), vocab=50257)
+    torch.cuda.synchronize()
+    assert toks2.cpu().numpy().tolist() == O.argmax(dt, logits).tolist()
 
 
 def test_add_one(b2, cuda):
