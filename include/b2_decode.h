@@ -123,12 +123,17 @@ B2_API int b2_kv_append(const B2KvAppendArgs* args, b2_stream_t stream);
  * The work is split over the whole GPU by key rows (every CTA streams the
  * same number of K/V rows, whatever the per-sequence lengths), so one
  * sequence may be cut into pieces handled by several CTAs.  Each piece's
- * partial softmax state goes to a caller-provided workspace, and a second,
- * small kernel merges the pieces and writes `out`.  Size the workspace with
- * b2_paged_attention_workspace_bytes; it needs no initialisation.  One
- * workspace serves any number of launches on one stream; launches that may
- * run concurrently need their own.  Both kernels use programmatic dependent
- * launch, so each may start while the kernel before it finishes.
+ * partial softmax state goes to a caller-provided workspace; the CTA that
+ * finishes a sequence's last piece merges them and writes `out` (the
+ * tensor-core kernel for 8 kv heads of head_dim 128 instead launches a second,
+ * small merge kernel).  Size the workspace with
+ * b2_paged_attention_workspace_bytes and ZERO IT ONCE before its first use
+ * (cudaMemset): it holds per-sequence piece counters, and every launch that
+ * completes leaves them at zero again.  After a launch that reported
+ * B2_DEVERR_TIMEOUT, zero it again.  One workspace serves any number of
+ * launches on one stream; launches that may run concurrently need their own.
+ * The kernels use programmatic dependent launch, so each may start while the
+ * kernel before it finishes.
  * ---------------------------------------------------------------------- */
 typedef struct B2PagedAttnArgs {
     int32_t dtype;     /* b2_dtype of q and the pool */
@@ -175,11 +180,11 @@ B2_API int b2_paged_attention(const B2PagedAttnArgs* args, void* workspace, size
  *
  * The first call on a device looks up the array's device address for that
  * device (cudaGetSymbolAddress); make that first call before any stream
- * capture.  All calls share the one array, and each call fully rewrites the
- * part it reads before reading it, so nothing needs clearing -- but calls
- * whose kernels overlap on the GPU (different streams, no ordering between
- * them) race on it: order them on one stream, or use b2_paged_attention with
- * a workspace per stream.
+ * capture.  All calls share the one array; it starts zeroed (module load) and
+ * every completed call leaves its piece counters at zero, so it never needs
+ * clearing -- but calls whose kernels overlap on the GPU (different streams,
+ * no ordering between them) race on it: order them on one stream, or use
+ * b2_paged_attention with a workspace per stream.
  * ---------------------------------------------------------------------- */
 #define B2_NOALLOC_SCRATCH_BYTES (4u << 20) /* 4 MiB */
 

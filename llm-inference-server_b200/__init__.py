@@ -141,12 +141,14 @@ def attn_args(q, q_row_stride, kv_pool, block_tables, seq_lens, out, *, n_head, 
 
 
 def attention_workspace(args: PagedAttnArgs):
-    """Allocates (torch) a workspace for launches shaped like args; it needs no initialisation."""
+    """Allocates (torch) a zeroed workspace for launches shaped like args (the
+    per-sequence piece counters in it must start at zero; launches leave them
+    at zero)."""
     import torch
     n = load().b2_paged_attention_workspace_bytes(ctypes.byref(args))
     if n == 0:
         raise B2Error(-3, load().b2_last_error_string().decode() or "workspace size query failed")
-    return torch.empty(n, dtype=torch.uint8, device="cuda")
+    return torch.zeros(n, dtype=torch.uint8, device="cuda")
 
 
 def paged_attention(args: PagedAttnArgs, workspace, stream=None) -> None:

@@ -26,11 +26,14 @@
 //    its slice of the accumulator in registers, rescaling once per batch of
 //    up to four tokens.  Warps meet only at the stage mbarriers.
 //  * Merge.  At a segment's end every token subgroup stores its (m, l, acc)
-//    to the workspace slot of (CTA, sequence, subgroup) and moves on: the
-//    attention kernel has no barrier, fence or atomic at its tail.  A small
-//    combine kernel, launched right behind it with programmatic dependent
-//    launch, merges each sequence's slots with the max-rescaled sum and
-//    writes the output in the output dtype.
+//    to the workspace slot of (CTA, sequence, subgroup) and hands the piece
+//    to the CTA's bookkeeping warp, which counts it on the sequence's
+//    counter with one acquire-release atomic.  The CTA that completes the
+//    count merges the sequence's slots (max-rescaled sums) and writes the
+//    output in the output dtype: the bookkeeping warp for pieces in the
+//    middle of the CTA's range, all softmax threads for the final piece,
+//    which is on the kernel's tail.  One kernel per call; the counters are
+//    left at zero for the next launch.
 //
 // Every wait is bounded (b2_common.cuh): on timeout the CTA flags
 // B2_DEVERR_TIMEOUT, drains its own copies in flight and returns.
@@ -57,9 +60,11 @@ struct AttnParams {
     int q_bytes;     // n_head * head_dim * sizeof(T)
     int off_meta;    // within a stage
     int off_misc, off_bars;
-    int2* seq_info;   // [batch] (first CTA, number of segments) for the combine
+    int2* seq_info;   // [batch] (first CTA, number of segments) for the combine kernel
     float2* part_ml;  // [(grid + batch) * ksplit][n_head] (m, l)
     float* part_acc;  // [(grid + batch) * ksplit][n_head][head_dim]
+    unsigned int* counters;  // [batch] pieces finished per sequence; zero between launches
+    void* out;               // [batch, n_head, head_dim] in OutT
 };
 
 struct CombineParams {
@@ -114,13 +119,111 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-template <typename T, int DH, int QG, int MAXT>
+// Merges the partials (m, l, acc) of sequence b -- slots (i0 + b) * ks ...
+// (i0 + nseg + b) * ks - 1, one per (CTA, token subgroup) -- with a running
+// maximum and writes out[b] in OutT.  Each (head, E-element chunk) item is
+// taken by TPI adjacent threads, thread k of them folding slots k, k + TPI,
+// ...; the loads of SB slots per thread are issued together, so TPI * SB
+// slots cost one L2 round trip, and the TPI states are then folded with xor
+// shuffles.  A subgroup that saw no rows has l == 0 and is skipped.
+// Partials are read through L2 (__ldcg): other CTAs wrote them.  nthr must be
+// a multiple of 32 and tid / nthr cover whole warps.
+__device__ __forceinline__ void fold_state(float& m, float& l, float* a, int E, float m2, float l2, const float* a2) {
+    if (!(l2 > 0.0f)) return;
+    const float mn = fmaxf(m, m2);
+    const float wo = exp2f(m - mn);  // 0 while m is -inf
+    const float wn = exp2f(m2 - mn);
+    m = mn;
+    l = fmaf(l2, wn, l * wo);
+    for (int e = 0; e < E; ++e) a[e] = fmaf(a2[e], wn, a[e] * wo);
+}
+
+template <int DH, int E, int TPI, typename OutT>
+__device__ __forceinline__ void merge_partials(const float2* part_ml, const float* part_acc, OutT* out, int H,
+                                               int ks, int b, int i0, int nseg, int tid, int nthr) {
+    constexpr int GL = DH / E;
+    constexpr int SB = 8;
+    const int nslots = nseg * ks;
+    const size_t slot0 = (static_cast<size_t>(i0) + b) * ks;
+    const int items = H * GL;
+    const int per_round = nthr / TPI;
+    const int sub = tid % TPI;
+    const int iters = (items + per_round - 1) / per_round;  // the same for every thread (full-warp shuffles)
+    for (int it = 0; it < iters; ++it) {
+        const int item = tid / TPI + it * per_round;
+        const bool valid = item < items;
+        const int h = valid ? item / GL : 0;
+        const int dc = valid ? item - h * GL : 0;
+        float mrun = -INFINITY, l = 0.0f, a[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) a[e] = 0.0f;
+        for (int s0 = 0; s0 < nslots; s0 += SB * TPI) {
+            float2 ml[SB];
+            float4 v[SB][E / 4];
+#pragma unroll
+            for (int j = 0; j < SB; ++j) {
+                const int s = s0 + j * TPI + sub;
+                ml[j] = make_float2(-INFINITY, 0.0f);
+                if (valid && s < nslots) {
+                    const size_t sl = slot0 + s;
+                    ml[j] = __ldcg(part_ml + sl * H + h);
+                    const float4* src = reinterpret_cast<const float4*>(part_acc + (sl * H + h) * DH + dc * E);
+#pragma unroll
+                    for (int q = 0; q < E / 4; ++q) v[j][q] = __ldcg(src + q);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < SB; ++j) {
+                float a2[E];
+#pragma unroll
+                for (int q = 0; q < E / 4; ++q) {
+                    a2[4 * q] = v[j][q].x;
+                    a2[4 * q + 1] = v[j][q].y;
+                    a2[4 * q + 2] = v[j][q].z;
+                    a2[4 * q + 3] = v[j][q].w;
+                }
+                fold_state(mrun, l, a, E, ml[j].x, ml[j].y, a2);
+            }
+        }
+#pragma unroll
+        for (int off = 1; off < TPI; off <<= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, mrun, off);
+            const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
+            float a2[E];
+#pragma unroll
+            for (int e = 0; e < E; ++e) a2[e] = __shfl_xor_sync(0xffffffffu, a[e], off);
+            fold_state(mrun, l, a, E, m2, l2, a2);
+        }
+        if (valid && sub == 0) {
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+            for (int e = 0; e < E; ++e) a[e] *= inv;
+            store_row<OutT, E>(out + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
+        }
+    }
+}
+
+// Counts one finished piece of a sequence: release (publishes the partials
+// this CTA wrote before it) and acquire (the other pieces' partials are
+// visible after it) at GPU scope.  Returns the previous count.
+__device__ __forceinline__ unsigned count_piece(unsigned* counter) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+    return old;
+}
+
+// Shared-memory ring between the softmax threads and the bookkeeping warp:
+// one entry per finished sequence piece.
+constexpr int kPieceRing = 8;
+
+template <typename T, int DH, int QG, int MAXT, typename OutT>
 __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams p) {
     constexpr int E = Elem<T>::kPer16B;
     constexpr int GL = DH / E;  // lanes sharing one head row
     static_assert(GL >= 2 && GL <= 32 && (32 % GL) == 0, "head_dim / dtype combination");
     constexpr int ES = static_cast<int>(sizeof(T));
     constexpr int TB = 4;  // tokens per online-softmax rescale
+    constexpr int R = kPieceRing;
 
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
@@ -130,21 +233,33 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     const int cta = blockIdx.x;
     const int B = p.batch;
     const int S = p.stages;
+    const int ncw = p.ncons / 32;  // softmax warps
 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
     uint64_t* empty = full + S;
+    uint64_t* piece_full = empty + S;  // [R], one arrival per softmax warp
+    uint64_t* piece_empty = piece_full + R;  // [R]
+    uint64_t* book_done = piece_empty + R;
     int* misc = reinterpret_cast<int*>(smem + p.off_misc);  // [0..1] first sequence and its row prefix, [2..34] scan
+    int4* pieces = reinterpret_cast<int4*>(smem + p.off_misc + 160);  // [R] (b, i0, nseg, final)
+    int* final_merge = misc + 36;  // [0] merge the final piece's sequence here, [1] b, [2] i0, [3] nseg
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], static_cast<uint32_t>(p.ncons / 32));
+            mbar_init(&empty[s], static_cast<uint32_t>(ncw));
         }
+        for (int s = 0; s < R; ++s) {
+            mbar_init(&piece_full[s], static_cast<uint32_t>(ncw));
+            mbar_init(&piece_empty[s], 1);
+        }
+        mbar_init(book_done, 1);
+        final_merge[0] = 0;
         fence_mbar_init();
     }
 
-    // Programmatic dependent launch: the combine kernel behind us may be
-    // scheduled right away; we wait here until the kernels before us (which
-    // produce q, the pool and seq_lens) have completed.
+    // Programmatic dependent launch: the kernel behind us may be scheduled
+    // right away; we wait here until the kernels before us (which produce q,
+    // the pool and seq_lens) have completed.
     pdl_launch_dependents();
     pdl_wait();
 
@@ -168,16 +283,15 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 misc[1] = run;
             }
             if (b % static_cast<int>(gridDim.x) == cta) {
-                // One CTA per sequence records where its partials live; no
-                // keys gives (0, 0) and the combine writes 0, like the
-                // reference (l == 0).
                 if (raw != cl) flag_error(B2_DEVERR_SEQ_LEN);
-                int2 info = make_int2(0, 0);
-                if (cl > 0) {
-                    const int i0 = cta_of_unit(run, N, G);
-                    info = make_int2(i0, cta_of_unit(run + cl - 1, N, G) - i0 + 1);
+                if (cl == 0) {
+                    // no keys: the output is 0, like the reference (l == 0)
+                    OutT* o = static_cast<OutT*>(p.out) + static_cast<size_t>(b) * H * DH;
+                    float z[E];
+#pragma unroll
+                    for (int e = 0; e < E; ++e) z[e] = 0.0f;
+                    for (int i = 0; i < H * DH; i += E) store_row<OutT, E>(o + i, z);
                 }
-                p.seq_info[b] = info;
             }
             run += cl;
         }
@@ -188,8 +302,9 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     const size_t row_elems = static_cast<size_t>(Hkv) * DH;
     const size_t slab_elems = row_elems * kBlockTokens;
     const int row_bytes = static_cast<int>(row_elems) * ES;
+    const int warp = tid >> 5;
 
-    if (tid >= p.ncons) {
+    if (warp == ncw) {
         // ================================================= producer warp
         // Walks the sequences of [s_unit, e_unit) in windows of 32 (one lane
         // each) and issues one stage per (sequence, block) run of rows.  The
@@ -223,6 +338,9 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 const int t_lo = static_cast<int>(u - Ps);                     // first row of the segment
                 const int t_hi = static_cast<int>(min(e_unit, Ps + cs) - Ps);  // one past its last row
                 const int j0 = t_lo / kBlockTokens, j1 = (t_hi - 1) / kBlockTokens + 1;
+                // CTAs sharing this sequence: every piece computes the same pair
+                const int i0 = cta_of_unit(Ps, N, G);
+                const int nseg = cta_of_unit(Ps + cs - 1, N, G) - i0 + 1;
                 for (int jc = j0; jc < j1 && !failed; jc += 32) {
                     const int jj = jc + lane;
                     int blk_l = 0;
@@ -253,7 +371,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                                 const int finalf = (Ps + j * kBlockTokens + r_hi == e_unit) ? 4 : 0;
                                 unsigned char* stage = smem + static_cast<size_t>(st) * p.stage_bytes;
                                 *reinterpret_cast<int4*>(stage + p.off_meta) =
-                                    make_int4(bs, nrows | ((first | lastf | finalf) << 8), 0, 0);
+                                    make_int4(bs, nrows | ((first | lastf | finalf) << 8), i0, nseg);
                                 const uint32_t kv_bytes = static_cast<uint32_t>(nrows * row_bytes);
                                 mbar_arrive_expect_tx(&full[st], 2u * kv_bytes + (first ? p.q_bytes : 0));
                                 const char* src = pool + (static_cast<size_t>(blk) * block_elems + layer_off +
@@ -292,6 +410,47 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         return;
     }
 
+    if (warp == ncw + 1) {
+        // ============================================== bookkeeping warp
+        // For each finished piece: publish it (fence, then count it on the
+        // sequence's counter); the CTA whose count completes the sequence
+        // merges it -- here, one warp, while the softmax warps stream on,
+        // except for this CTA's final piece, whose merge is left to the
+        // softmax threads once they are done (it is on the kernel's tail).
+        const int lane = tid & 31;
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
+            const int rk = k % R;
+            ok = mbar_wait_bounded(&piece_full[rk], static_cast<uint32_t>(k / R) & 1u);
+            if (!ok) break;
+            const int4 pc = pieces[rk];
+            __syncwarp();  // every lane has read the entry before it is released
+            if (lane == 0) mbar_arrive(&piece_empty[rk]);
+            int last = 0;
+            if (lane == 0) last = count_piece(p.counters + pc.x) == static_cast<unsigned>(pc.z - 1) ? 1 : 0;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                if (pc.w) {
+                    if (lane == 0) {
+                        final_merge[0] = 1;
+                        final_merge[1] = pc.x;
+                        final_merge[2] = pc.y;
+                        final_merge[3] = pc.z;
+                    }
+                } else {
+                    merge_partials<DH, E, 1, OutT>(p.part_ml, p.part_acc, static_cast<OutT*>(p.out), H, p.ksplit,
+                                                   pc.x, pc.y, pc.z, lane, 32);
+                    if (lane == 0) p.counters[pc.x] = 0u;  // every launch leaves the counters at zero
+                }
+            }
+            if (pc.w) break;
+        }
+        if (!ok && lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(book_done);  // also on failure: nobody waits on a dead warp
+        return;
+    }
+
     // ===================================================== consumer threads
     const int ks = p.ksplit;
     const int ts = tid / C;
@@ -316,6 +475,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     }
     const float scale_log2 = p.scale_log2;
 
+    int npieces = 0;
     for (int n = 0;; ++n) {
         const int st = n % S;
         const uint32_t ph = static_cast<uint32_t>(n / S) & 1u;
@@ -412,23 +572,61 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
 
-        if (last && active) {
-            // ---- segment end: this subgroup's partial goes to the workspace.
+        if (last) {
+            // ---- piece end: this subgroup's partial goes to the workspace.
             // Slot (cta + b) is unique per (CTA, sequence) pair: along the CTA
             // order both indices only grow, so cta + b never repeats.
-            const size_t slot = (static_cast<size_t>(cta) + b) * ks + ts;
+            if (active) {
+                const size_t slot = (static_cast<size_t>(cta) + b) * ks + ts;
 #pragma unroll
-            for (int g = 0; g < QG; ++g) {
-                const int h = hk * QG + g;
-                float* dst = p.part_acc + (slot * H + h) * DH + dg * E;
+                for (int g = 0; g < QG; ++g) {
+                    const int h = hk * QG + g;
+                    float* dst = p.part_acc + (slot * H + h) * DH + dg * E;
 #pragma unroll
-                for (int e = 0; e < E; e += 4)
-                    __stcg(reinterpret_cast<float4*>(dst + e),
-                           make_float4(acc[g][e], acc[g][e + 1], acc[g][e + 2], acc[g][e + 3]));
-                if (dg == 0) __stcg(p.part_ml + slot * H + h, make_float2(m_run[g], l_run[g]));
+                    for (int e = 0; e < E; e += 4)
+                        __stcg(reinterpret_cast<float4*>(dst + e),
+                               make_float4(acc[g][e], acc[g][e + 1], acc[g][e + 2], acc[g][e + 3]));
+                    if (dg == 0) __stcg(p.part_ml + slot * H + h, make_float2(m_run[g], l_run[g]));
+                }
             }
+            // Hand the piece to the bookkeeping warp (ring slot npieces % R):
+            // thread 0 writes the entry, and every warp arrives once its
+            // partial stores are issued.  The arrivals are CTA-scope releases;
+            // the bookkeeper's GPU-scope fence before its counter update then
+            // publishes all of them (the release pattern of a CTA barrier
+            // followed by one thread's fence and atomic).
+            const int rk = npieces % R;
+            if (tid == 0) {
+                if (!mbar_wait_bounded(&piece_empty[rk], (static_cast<uint32_t>(npieces / R) & 1u) ^ 1u))
+                    flag_error(B2_DEVERR_TIMEOUT);
+                pieces[rk] = make_int4(b, meta.z, meta.w, final_stage ? 1 : 0);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&piece_full[rk]);
+            ++npieces;
         }
         if (final_stage) break;
+    }
+
+    // ---- tail: merge the final piece's sequence if this CTA completed it.
+    // Every thread waits for the bookkeeper on its own (bounded); no CTA
+    // barrier, since a warp that timed out above has already left.
+    if (!mbar_wait_bounded(book_done, 0)) {
+        if (tid == 0) flag_error(B2_DEVERR_TIMEOUT);
+        return;
+    }
+    if (final_merge[0]) {
+        // The bookkeeper's acquire on the counter, then its arrival on
+        // book_done, order the other CTAs' partials before these reads.
+        const int fb = final_merge[1], fi0 = final_merge[2], fn = final_merge[3];
+        OutT* o = static_cast<OutT*>(p.out);
+        if (p.ncons >= 4 * H * GL)
+            merge_partials<DH, E, 4, OutT>(p.part_ml, p.part_acc, o, H, ks, fb, fi0, fn, tid, p.ncons);
+        else if (p.ncons >= 2 * H * GL)
+            merge_partials<DH, E, 2, OutT>(p.part_ml, p.part_acc, o, H, ks, fb, fi0, fn, tid, p.ncons);
+        else
+            merge_partials<DH, E, 1, OutT>(p.part_ml, p.part_acc, o, H, ks, fb, fi0, fn, tid, p.ncons);
+        if (tid == 0) p.counters[fb] = 0u;  // every launch leaves the counters at zero
     }
 }
 

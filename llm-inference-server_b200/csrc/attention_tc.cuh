@@ -181,7 +181,7 @@ __device__ __forceinline__ void tc_sync(int id) {
     named_sync(id, kTcConsumers);
 }
 
-// 4-D tiled TMA load (no multicast) completing on `bar`.
+// 4-D tiled TMA load into this CTA's own shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint64_t* bar) {
     asm volatile(

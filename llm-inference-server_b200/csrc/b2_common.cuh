@@ -275,8 +275,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // One-dimensional bulk async copy global -> shared, completing on an mbarrier
-// (the TMA engine's untiled form; no tensor map, no multicast).  dst, src and
-// bytes must be multiples of 16.
+// (the TMA engine's untiled form; no tensor map; into this CTA's own shared
+// memory).  dst, src and bytes must be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

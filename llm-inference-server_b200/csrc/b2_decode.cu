@@ -92,7 +92,7 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // the register cap at 128 per thread.
 constexpr int kAttnMaxThreads = 512;
 // Shared bytes of the attention kernel's misc area (first sequence, scan).
-constexpr int kMiscBytes = 256;
+constexpr int kMiscBytes = 320;
 
 // ---------------------------------------------------------- attention plan
 
@@ -102,7 +102,8 @@ struct AttnPlan {
     bool tensor_cores = false;  // paged_decode_tc_kernel instead of paged_decode_kernel
     int tc_stages = 0;
     AttnParams prm{};
-    size_t ws_info = 0, ws_ml = 0, ws_acc = 0, ws_total = 0;
+    // workspace: [piece counters][seq_info][(m, l) partials][acc partials]
+    size_t ws_cnt = 0, ws_info = 0, ws_ml = 0, ws_acc = 0, ws_total = 0;
 };
 
 // The tensor-core kernel serves 16-bit K/V with 8 kv heads of head_dim 128
@@ -184,10 +185,11 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
             pl->combine_threads = static_cast<int>(align_up(static_cast<size_t>(H) * GL, 32));
             pl->prm.ksplit = 1;
             const size_t slots = static_cast<size_t>(pl->grid) + a->batch;
+            pl->ws_cnt = align_up(static_cast<size_t>(a->batch) * sizeof(unsigned), 256);
             pl->ws_info = align_up(static_cast<size_t>(a->batch) * sizeof(int2), 256);
             pl->ws_ml = align_up(slots * H * sizeof(float2), 256);
             pl->ws_acc = align_up(slots * H * a->head_dim * sizeof(float), 256);
-            pl->ws_total = pl->ws_info + pl->ws_ml + pl->ws_acc;
+            pl->ws_total = pl->ws_cnt + pl->ws_info + pl->ws_ml + pl->ws_acc;
             return B2_OK;
         }
     }
@@ -204,7 +206,7 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
         const int thread_cap = cps == 1 ? maxt : 256;
         for (int k : {4, 2, 1}) {
             const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * C, 32));
-            if (ncons + 32 > thread_cap) continue;
+            if (ncons + 64 > thread_cap) continue;  // + producer warp + bookkeeping warp
             if (k > 1 && k * C > 512) continue;  // enough warps
             int s = (smem_cap - kMiscBytes - 512) / stage;  // 512: barriers + alignment padding
             if (s > 8) s = 8;
@@ -232,18 +234,19 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     p.off_misc = off;
     off += kMiscBytes;
     p.off_bars = off;
-    off += 2 * best_s * 8;
+    off += (2 * best_s + 2 * kPieceRing + 1) * 8;
     pl->smem = off;
-    pl->threads = p.ncons + 32;
+    pl->threads = p.ncons + 64;
     pl->grid = di.sms * best_cps;
     pl->combine_threads = static_cast<int>(align_up(static_cast<size_t>(H) * GL, 32));
 
     // One partial per (CTA, sequence) pair and token subgroup; cta + b < grid + batch.
     const size_t slots = (static_cast<size_t>(pl->grid) + a->batch) * best_k;
+    pl->ws_cnt = align_up(static_cast<size_t>(a->batch) * sizeof(unsigned), 256);
     pl->ws_info = align_up(static_cast<size_t>(a->batch) * sizeof(int2), 256);
     pl->ws_ml = align_up(slots * H * sizeof(float2), 256);
     pl->ws_acc = align_up(slots * H * a->head_dim * sizeof(float), 256);
-    pl->ws_total = pl->ws_info + pl->ws_ml + pl->ws_acc;
+    pl->ws_total = pl->ws_cnt + pl->ws_info + pl->ws_ml + pl->ws_acc;
     return B2_OK;
 }
 
@@ -331,10 +334,10 @@ int launch_tc(const AttnPlan& pl, const TcParams& tp, const CUtensorMap& map, in
     return fail(B2_ERR_UNSUPPORTED, "no tensor-core kernel for this head shape");
 }
 
-template <typename T, int DH, int QG>
-int launch_attn_t(const AttnPlan& pl, cudaStream_t stream) {
+template <typename T, int DH, int QG, typename OutT>
+int launch_attn_o(const AttnPlan& pl, cudaStream_t stream) {
     constexpr int MAXT = kAttnMaxThreads;
-    auto kern = paged_decode_kernel<T, DH, QG, MAXT>;
+    auto kern = paged_decode_kernel<T, DH, QG, MAXT, OutT>;
     static std::atomic<uint64_t> smem_set{0};  // one flag word per instantiation
     int dev = -1;
     const DeviceInfo di = device_info(&dev);
@@ -344,24 +347,32 @@ int launch_attn_t(const AttnPlan& pl, cudaStream_t stream) {
                       stream, pl.prm);
 }
 
+// out_dtype is F32, or the input dtype (checked by check_attn_args).
+template <typename T, int DH, int QG>
+int launch_attn_t(const AttnPlan& pl, int out_dtype, cudaStream_t stream) {
+    if (out_dtype == B2_F32) return launch_attn_o<T, DH, QG, float>(pl, stream);
+    if constexpr (sizeof(T) == 2) return launch_attn_o<T, DH, QG, T>(pl, stream);
+    return fail(B2_ERR_DTYPE, "16-bit output needs 16-bit inputs");
+}
+
 template <typename T>
-int launch_attn_dh(const AttnPlan& pl, int dh, int qg, cudaStream_t s) {
+int launch_attn_dh(const AttnPlan& pl, int dh, int qg, int out_dtype, cudaStream_t s) {
     if (dh == 64) {
         switch (qg) {
-            case 1: return launch_attn_t<T, 64, 1>(pl, s);
-            case 2: return launch_attn_t<T, 64, 2>(pl, s);
-            case 4: return launch_attn_t<T, 64, 4>(pl, s);
+            case 1: return launch_attn_t<T, 64, 1>(pl, out_dtype, s);
+            case 2: return launch_attn_t<T, 64, 2>(pl, out_dtype, s);
+            case 4: return launch_attn_t<T, 64, 4>(pl, out_dtype, s);
             case 8:
-                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 64, 8>(pl, s);
+                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 64, 8>(pl, out_dtype, s);
                 break;
         }
     } else {
         switch (qg) {
-            case 1: return launch_attn_t<T, 128, 1>(pl, s);
-            case 2: return launch_attn_t<T, 128, 2>(pl, s);
-            case 4: return launch_attn_t<T, 128, 4>(pl, s);
+            case 1: return launch_attn_t<T, 128, 1>(pl, out_dtype, s);
+            case 2: return launch_attn_t<T, 128, 2>(pl, out_dtype, s);
+            case 4: return launch_attn_t<T, 128, 4>(pl, out_dtype, s);
             case 8:
-                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 128, 8>(pl, s);
+                if constexpr (sizeof(T) == 4) return launch_attn_t<T, 128, 8>(pl, out_dtype, s);
                 break;
         }
     }
@@ -507,9 +518,11 @@ int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_s
     const float scale = a->scale > 0.0f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     p.scale_log2 = scale * 1.4426950408889634f;
     char* base = static_cast<char*>(ws);
-    p.seq_info = reinterpret_cast<int2*>(base);
-    p.part_ml = reinterpret_cast<float2*>(base + pl.ws_info);
-    p.part_acc = reinterpret_cast<float*>(base + pl.ws_info + pl.ws_ml);
+    p.counters = reinterpret_cast<unsigned int*>(base);
+    p.seq_info = reinterpret_cast<int2*>(base + pl.ws_cnt);
+    p.part_ml = reinterpret_cast<float2*>(base + pl.ws_cnt + pl.ws_info);
+    p.part_acc = reinterpret_cast<float*>(base + pl.ws_cnt + pl.ws_info + pl.ws_ml);
+    p.out = a->out;
     const int qg = a->n_head / a->n_kv_head;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (pl.tensor_cores) {
@@ -533,12 +546,11 @@ int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_s
         tp.part_ml = p.part_ml;
         tp.part_acc = p.part_acc;
         rc = a->dtype == B2_F16 ? launch_tc<__half>(pl, tp, map, qg, s) : launch_tc<__nv_bfloat16>(pl, tp, map, qg, s);
-    } else if (a->dtype == B2_F32) {
-        rc = launch_attn_dh<float>(pl, a->head_dim, qg, s);
-    } else if (a->dtype == B2_F16) {
-        rc = launch_attn_dh<__half>(pl, a->head_dim, qg, s);
     } else {
-        rc = launch_attn_dh<__nv_bfloat16>(pl, a->head_dim, qg, s);
+        // The CUDA-core kernel merges each sequence's pieces itself.
+        if (a->dtype == B2_F32) return launch_attn_dh<float>(pl, a->head_dim, qg, a->out_dtype, s);
+        if (a->dtype == B2_F16) return launch_attn_dh<__half>(pl, a->head_dim, qg, a->out_dtype, s);
+        return launch_attn_dh<__nv_bfloat16>(pl, a->head_dim, qg, a->out_dtype, s);
     }
     if (rc != B2_OK) return rc;
     CombineParams cp;

@@ -298,6 +298,7 @@ struct Engine {
         attn_ws_bytes = b2_paged_attention_workspace_bytes(&a);
         if (attn_ws_bytes == 0) throw Error(B2_ERR_UNSUPPORTED, std::string("attention shape: ") + b2_last_error_string());
         cuda_ok(cudaMalloc(&attn_ws, attn_ws_bytes), "malloc attention workspace");
+        cuda_ok(cudaMemsetAsync(attn_ws, 0, attn_ws_bytes, stream), "zero attention workspace");
         bucket_cap = B;
         cuda_ok(cudaStreamSynchronize(stream), "engine set-up");
     }
