@@ -463,7 +463,7 @@ def run_ours(args, rank: int, world: int, dist) -> None:
     print(json.dumps(line), flush=True)
 
 
-ENGINE_NAMES = ("gpt2-xl", "gpt2-medium")
+ENGINE_NAMES = ("gpt2-xl", "gpt2-medium", "gpt2-xl-heads")
 
 
 def run_engine(args, rank: int, world: int, dist) -> None:
@@ -505,7 +505,9 @@ def run_engine(args, rank: int, world: int, dist) -> None:
     steps_total = args.steps * r["waves"]
     es = EB.elem_bytes(w.dtype)
     mbps = (w.n_ctx + 15) // 16
-    ours_per_step = 1 + 6 * w.n_layer + 2  # embedding, per layer LN/append/attention x2/LN/GELU, final LN, argmax
+    # embedding, per layer LN/append/attention/LN/GELU, final LN, argmax (+ epoch bump and a barrier per
+    # layer when head-sharded)
+    ours_per_step = 1 + 5 * w.n_layer + 2 + (1 + w.n_layer if w.head_sharded and world > 1 else 0)
     line = {
         "metric": "GPT-2 decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_max / steps_total, 4),
@@ -514,7 +516,9 @@ def run_engine(args, rank: int, world: int, dist) -> None:
         "config": {"workload": w.description, "name": w.name, "global_batch": w.global_batch,
                    "per_gpu_batch": r["per_rank"], "waves_per_gpu": r["waves"], "wave": r["wave"],
                    "l2": "inputs larger than L2: every step reads all weights (GB) and every cached KV row",
-                   "parallelism": f"sequence-sharded x{world}, one engine and KV pool per GPU, no collective"},
+                   "parallelism": (f"head-sharded x{world}: attention output all-gathered over NVLink in the "
+                                   "attention epilogue, one flag barrier per layer" if w.head_sharded else
+                                   f"sequence-sharded x{world}, one engine and KV pool per GPU, no collective")},
         "roofline": {"bound": "hbm", "achieved": round(achieved / world, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(frac, 4), "peak_kind": peak_kind, "traffic": None,
                      "traffic_note": "per GPU; algorithmic bytes per step = all weights + every cached K/V row "

@@ -165,6 +165,41 @@ B2_API int b2_paged_attention(const B2PagedAttnArgs* args, void* workspace, size
                               b2_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Paged decode attention whose output is all-gathered in its epilogue.
+ * No counterpart in the reference (its engine is single-GPU).  For
+ * head-sharded decode: a rank computes attention for its own heads and stores
+ * each output row straight into n_outs arrays -- its own and its peers'
+ * gathered attention outputs, peers reached through their UVA (IPC-mapped)
+ * addresses over NVLink -- at row b * row_stride + col_offset.  Nothing else
+ * changes; use b2_tp_barrier afterwards so every rank's slice has landed
+ * before the gathered array is read.
+ * ---------------------------------------------------------------------- */
+#define B2_MAX_GATHER 8
+
+typedef struct B2OutputGather {
+    void* const* outs;  /* device array of n_outs base pointers (local or peer) */
+    int32_t n_outs;     /* 1 .. B2_MAX_GATHER */
+    int64_t row_stride; /* elements between batch rows of every output array */
+    int64_t col_offset; /* element column where this call's head 0 goes */
+} B2OutputGather;
+
+B2_API int b2_paged_attention_gather(const B2PagedAttnArgs* args, void* workspace, size_t workspace_bytes,
+                                     const B2OutputGather* gather, b2_stream_t stream);
+
+/* Cross-GPU barrier for head-sharded ranks, one launch of one small CTA.
+ * Every rank r of n publishes `*epoch` into slot[r] of each peer's flag array
+ * (peer_flags[p] + slot * n, written with release semantics at system scope
+ * after a system-scope fence, so the rank's earlier stores to peers are
+ * visible first) and then waits until its own local_flags[slot * n + p]
+ * reach *epoch for every p.  The wait is bounded (2 s); a timeout sets
+ * B2_DEVERR_TIMEOUT and returns.  flag arrays start zeroed; epochs only grow. */
+B2_API int b2_tp_barrier(uint32_t* local_flags, uint32_t* const* peer_flags, int32_t rank, int32_t n,
+                         const uint32_t* epoch, int32_t slot, b2_stream_t stream);
+
+/* *epoch += 1 (one thread): the start of a new step for b2_tp_barrier. */
+B2_API int b2_tp_epoch_bump(uint32_t* epoch, b2_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Paged decode attention without any device allocation.
  * No counterpart in the reference: it exists for callers that cannot allocate
  * device memory when they run attention -- for example a plugin whose host

@@ -38,6 +38,8 @@ typedef struct B2EngineConfig {
     int32_t dtype;           /* b2_dtype of weights, activations and KV */
     int32_t use_cuda_graphs; /* 1: capture and replay one graph per batch bucket */
     int32_t device;          /* CUDA device ordinal; -1 = the current device */
+    int32_t tp_rank;         /* head-sharded engines: this rank (0 .. tp_size-1) */
+    int32_t tp_size;         /* 0 or 1: one engine holds every head; 2..8: head-sharded */
 } B2EngineConfig;
 
 /* gpu-engine/include/engine/model.h:7-18 (GPT2Config). */
@@ -104,6 +106,24 @@ B2_API const char* b2_engine_last_error(void);
 
 #define B2_ERR_POOL (-8) /* the KV block pool ran out during decode_step */
 #define B2_ERR_IO (-9)   /* a weight file is missing, short or inconsistent */
+
+/* Head-sharded decode (no reference counterpart; the reference engine is
+ * single-GPU).  tp_size engines, one per GPU (each created with its
+ * tp_rank), each own ceil(n_head / tp_size) heads: their slice of the QKV
+ * projection and of every layer's KV cache.  LayerNorms, the output
+ * projection, the MLP and the lm_head are replicated.  Each layer's attention
+ * stores its heads' output rows into every rank's gathered buffer over NVLink
+ * (b2_paged_attention_gather) and the ranks meet at b2_tp_barrier before the
+ * output projection reads it.  All ranks must make the same calls with the
+ * same sequences in the same order; each computes the same next tokens.
+ *
+ * Set-up, once, after creation on every rank: exchange the
+ * B2_TP_HANDLE_BYTES blob of b2_engine_tp_handle between the ranks (any
+ * host transport), then pass all of them, in rank order, to
+ * b2_engine_tp_connect.  decode_step before that returns B2_ERR_SHAPE. */
+#define B2_TP_HANDLE_BYTES 128 /* two cudaIpcMemHandle_t: gathered buffer, barrier flags */
+B2_API int b2_engine_tp_handle(const b2_engine* eng, void* out);
+B2_API int b2_engine_tp_connect(b2_engine* eng, const void* handles);
 
 /* The engine's paged-block allocator, exposed so its behaviour can be checked
  * against the reference's BlockPool (gpu-engine/src/kv_cache_pool.cpp:6-28):

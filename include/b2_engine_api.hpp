@@ -30,6 +30,8 @@ struct EngineConfig {
     int dtype = B2_F16;  // the reference engine is fp16
     bool use_cuda_graphs = true;
     int device = -1;  // -1: the device current on the calling thread
+    int tp_rank = 0;  // head-sharded engines (include/b2_engine.h)
+    int tp_size = 1;
 };
 
 class Engine {
@@ -43,7 +45,7 @@ public:
         b2_engine_destroy(eng_);
         eng_ = nullptr;
         const B2EngineConfig c{cfg.max_batch, cfg.max_seq_len, cfg.kv_block_budget, cfg.dtype,
-                               cfg.use_cuda_graphs ? 1 : 0, cfg.device};
+                               cfg.use_cuda_graphs ? 1 : 0, cfg.device, cfg.tp_rank, cfg.tp_size};
         return b2_engine_create(weights_dir.c_str(), &c, &eng_) == B2_OK;
     }
 

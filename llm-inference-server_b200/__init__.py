@@ -30,7 +30,8 @@ DECODE_SYMBOLS = (
     "b2_version", "b2_last_error_string", "b2_device_errors", "b2_kv_append",
     "b2_paged_attention_workspace_bytes", "b2_paged_attention",
     "b2_add_layernorm", "b2_bias_gelu", "b2_add_bias", "b2_add_one", "b2_embedding", "b2_argmax",
-    "b2_paged_attention_noalloc", "b2_argmax_rows",
+    "b2_paged_attention_noalloc", "b2_argmax_rows", "b2_paged_attention_gather", "b2_tp_barrier",
+    "b2_tp_epoch_bump",
 )
 
 _c_int, _c_float, _vp = ctypes.c_int32, ctypes.c_float, ctypes.c_void_p

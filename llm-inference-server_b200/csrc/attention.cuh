@@ -43,6 +43,31 @@
 
 namespace b2 {
 
+// Where attention outputs go.  n == 0: one packed [batch, n_head, head_dim]
+// array at `out`.  n > 0: the same values are stored into each of the n
+// arrays outs[0..n) (this GPU's memory or a peer's, through its UVA
+// address), row b at b * row_stride + col_offset elements -- so a
+// head-sharded rank writes its heads' slice of every rank's gathered
+// attention output directly (the all-gather happens in the epilogue).
+struct OutSpec {
+    void* out;
+    void* const* outs;  // device array of n bases
+    int n;
+    long long row_stride, col_offset;
+};
+
+template <typename OutT, int E>
+__device__ __forceinline__ void store_out(const OutSpec& o, int b, int H, int h, int DH, int dc, const float* a) {
+    if (o.n == 0) {
+        store_row<OutT, E>(static_cast<OutT*>(o.out) + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
+        return;
+    }
+    const long long off = static_cast<long long>(b) * o.row_stride + o.col_offset + static_cast<long long>(h) * DH +
+                          static_cast<long long>(dc) * E;
+    for (int i = 0; i < o.n; ++i) store_row<OutT, E>(static_cast<OutT*>(o.outs[i]) + off, a);
+    __threadfence_system();  // peers read these after the next barrier
+}
+
 struct AttnParams {
     const void* q;
     long long q_row_stride;  // elements
@@ -64,14 +89,14 @@ struct AttnParams {
     float2* part_ml;  // [(grid + batch) * ksplit][n_head] (m, l)
     float* part_acc;  // [(grid + batch) * ksplit][n_head][head_dim]
     unsigned int* counters;  // [batch] pieces finished per sequence; zero between launches
-    void* out;               // [batch, n_head, head_dim] in OutT
+    OutSpec out;
 };
 
 struct CombineParams {
     const int2* seq_info;
     const float2* part_ml;
     const float* part_acc;
-    void* out;  // [batch, n_head, head_dim]
+    OutSpec out;
     int n_head, ksplit;
 };
 
@@ -139,7 +164,7 @@ __device__ __forceinline__ void fold_state(float& m, float& l, float* a, int E, 
 }
 
 template <int DH, int E, int TPI, typename OutT>
-__device__ __forceinline__ void merge_partials(const float2* part_ml, const float* part_acc, OutT* out, int H,
+__device__ __forceinline__ void merge_partials(const float2* part_ml, const float* part_acc, const OutSpec& out, int H,
                                                int ks, int b, int i0, int nseg, int tid, int nthr) {
     constexpr int GL = DH / E;
     constexpr int SB = 8;
@@ -198,7 +223,7 @@ __device__ __forceinline__ void merge_partials(const float2* part_ml, const floa
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll
             for (int e = 0; e < E; ++e) a[e] *= inv;
-            store_row<OutT, E>(out + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
+            store_out<OutT, E>(out, b, H, h, DH, dc, a);
         }
     }
 }
@@ -286,11 +311,10 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 if (raw != cl) flag_error(B2_DEVERR_SEQ_LEN);
                 if (cl == 0) {
                     // no keys: the output is 0, like the reference (l == 0)
-                    OutT* o = static_cast<OutT*>(p.out) + static_cast<size_t>(b) * H * DH;
                     float z[E];
 #pragma unroll
                     for (int e = 0; e < E; ++e) z[e] = 0.0f;
-                    for (int i = 0; i < H * DH; i += E) store_row<OutT, E>(o + i, z);
+                    for (int i = 0; i < H * DH; i += E) store_out<OutT, E>(p.out, b, H, i / DH, DH, (i % DH) / E, z);
                 }
             }
             run += cl;
@@ -438,7 +462,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                         final_merge[3] = pc.z;
                     }
                 } else {
-                    merge_partials<DH, E, 1, OutT>(p.part_ml, p.part_acc, static_cast<OutT*>(p.out), H, p.ksplit,
+                    merge_partials<DH, E, 1, OutT>(p.part_ml, p.part_acc, p.out, H, p.ksplit,
                                                    pc.x, pc.y, pc.z, lane, 32);
                     if (lane == 0) p.counters[pc.x] = 0u;  // every launch leaves the counters at zero
                 }
@@ -619,7 +643,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         // The bookkeeper's acquire on the counter, then its arrival on
         // book_done, order the other CTAs' partials before these reads.
         const int fb = final_merge[1], fi0 = final_merge[2], fn = final_merge[3];
-        OutT* o = static_cast<OutT*>(p.out);
+        const OutSpec& o = p.out;
         if (p.ncons >= 4 * H * GL)
             merge_partials<DH, E, 4, OutT>(p.part_ml, p.part_acc, o, H, ks, fb, fi0, fn, tid, p.ncons);
         else if (p.ncons >= 2 * H * GL)
@@ -689,7 +713,7 @@ __global__ void __launch_bounds__(512) paged_decode_combine_kernel(const Combine
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll
     for (int e = 0; e < E; ++e) a[e] *= inv;
-    store_row<OutT, E>(static_cast<OutT*>(c.out) + (static_cast<size_t>(b) * H + h) * DH + dc * E, a);
+    store_out<OutT, E>(c.out, b, H, h, DH, dc, a);
 }
 
 }  // namespace b2

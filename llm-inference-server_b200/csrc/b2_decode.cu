@@ -22,6 +22,7 @@
 #include "attention_tc.cuh"
 #include "b2_common.cuh"
 #include "rows.cuh"
+#include "tp.cuh"
 
 namespace b2 {
 namespace {
@@ -492,9 +493,26 @@ size_t b2_paged_attention_workspace_bytes(const B2PagedAttnArgs* a) {
     return pl.ws_total;
 }
 
-int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_stream_t stream) {
+}  // extern "C"
+
+namespace b2 {
+namespace {
+// b2_paged_attention with the output going to `gather`'s arrays when non-NULL.
+int paged_attention_impl(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, const B2OutputGather* gather,
+                         b2_stream_t stream) {
     int rc = check_attn_args(a);
     if (rc != B2_OK) return rc;
+    if (gather != nullptr) {
+        const long long es_out = a->out_dtype == B2_F32 ? 4 : 2;
+        if (gather->n_outs < 1 || gather->n_outs > B2_MAX_GATHER || gather->outs == nullptr)
+            return fail(B2_ERR_SHAPE, "gather needs 1..B2_MAX_GATHER output arrays");
+        if (gather->col_offset < 0 ||
+            gather->row_stride < gather->col_offset + static_cast<long long>(a->n_head) * a->head_dim)
+            return fail(B2_ERR_SHAPE, "gather row_stride must cover col_offset + n_head*head_dim");
+        if ((gather->row_stride * es_out) % 16 != 0 || (gather->col_offset * es_out) % 16 != 0 ||
+            !aligned16(gather->outs))
+            return fail(B2_ERR_ALIGN, "gather row_stride and col_offset must be 16-byte multiples");
+    }
     if (a->batch == 0) return B2_OK;
     AttnPlan pl;
     rc = plan_attention(a, &pl);
@@ -522,7 +540,11 @@ int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_s
     p.seq_info = reinterpret_cast<int2*>(base + pl.ws_cnt);
     p.part_ml = reinterpret_cast<float2*>(base + pl.ws_cnt + pl.ws_info);
     p.part_acc = reinterpret_cast<float*>(base + pl.ws_cnt + pl.ws_info + pl.ws_ml);
-    p.out = a->out;
+    p.out.out = a->out;
+    p.out.outs = gather ? gather->outs : nullptr;
+    p.out.n = gather ? gather->n_outs : 0;
+    p.out.row_stride = gather ? gather->row_stride : 0;
+    p.out.col_offset = gather ? gather->col_offset : 0;
     const int qg = a->n_head / a->n_kv_head;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (pl.tensor_cores) {
@@ -557,10 +579,38 @@ int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_s
     cp.seq_info = p.seq_info;
     cp.part_ml = p.part_ml;
     cp.part_acc = p.part_acc;
-    cp.out = a->out;
+    cp.out = p.out;
     cp.n_head = a->n_head;
     cp.ksplit = p.ksplit;
     return launch_combine(cp, a->dtype, a->out_dtype, a->head_dim, a->batch, pl.combine_threads, s);
+}
+}  // namespace
+}  // namespace b2
+
+extern "C" {
+
+int b2_paged_attention(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, b2_stream_t stream) {
+    return b2::paged_attention_impl(a, ws, ws_bytes, nullptr, stream);
+}
+
+int b2_paged_attention_gather(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, const B2OutputGather* gather,
+                              b2_stream_t stream) {
+    if (gather == nullptr) return fail(B2_ERR_NULL, "gather is NULL");
+    return b2::paged_attention_impl(a, ws, ws_bytes, gather, stream);
+}
+
+int b2_tp_barrier(uint32_t* local_flags, uint32_t* const* peer_flags, int32_t rank, int32_t n, const uint32_t* epoch,
+                  int32_t slot, b2_stream_t stream) {
+    if (!local_flags || !peer_flags || !epoch) return fail(B2_ERR_NULL, "local_flags, peer_flags and epoch are required");
+    if (n < 1 || n > B2_MAX_GATHER || rank < 0 || rank >= n || slot < 0) return fail(B2_ERR_SHAPE, "bad rank / n / slot");
+    tp_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(local_flags, peer_flags, rank, n, epoch, slot);
+    return launch_status();
+}
+
+int b2_tp_epoch_bump(uint32_t* epoch, b2_stream_t stream) {
+    if (!epoch) return fail(B2_ERR_NULL, "epoch is NULL");
+    tp_epoch_bump_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(epoch);
+    return launch_status();
 }
 
 }  // extern "C"

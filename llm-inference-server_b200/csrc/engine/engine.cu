@@ -23,6 +23,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -166,6 +167,21 @@ struct Engine {
     int next_id = 0;
     bool use_graphs = true;
     std::map<int, cudaGraphExec_t> graphs;
+    // Head sharding (tp > 1): this engine holds heads [tp_rank * hl, tp_rank * hl + hl)
+    // (hl = ceil(n_head / tp); heads past n_head are zero padding), their QKV slice,
+    // a zero-padded copy of every output projection, the gathered attention output
+    // [max_batch, tp * hl * head_dim] and the barrier flags [n_layer][tp] (both
+    // IPC-shared with the peers), and the peers' addresses of both.
+    int tp = 1, tp_rank = 0, hl = 0;  // hl: heads held here (all of them when tp == 1)
+    void* tp_weights = nullptr;
+    std::vector<const void*> qkv_w_loc, qkv_b_loc, proj_w_pad;
+    void* d_gath = nullptr;
+    uint32_t* d_flags = nullptr;
+    uint32_t* d_epoch = nullptr;
+    void** d_peer_outs = nullptr;
+    uint32_t** d_peer_flags = nullptr;
+    std::vector<void*> peer_mapped;  // IPC-opened peer bases, closed at destruction
+    bool tp_connected = false;
 
     int32_t* in_tokens() const { return d_in; }
     int32_t* in_positions() const { return d_in + cfg.max_batch; }
@@ -177,12 +193,55 @@ struct Engine {
         for (auto& g : graphs) cudaGraphExecDestroy(g.second);
         if (cublas) cublasDestroy(cublas);
         if (stream) cudaStreamDestroy(stream);
+        for (void* p : peer_mapped) cudaIpcCloseMemHandle(p);
         void* dev_ptrs[] = {weights, pool, cublas_ws, d_in, d_seq_post, d_next, d_resid, d_x, d_qkv,
-                            d_attn, d_attn_out, d_ff, d_ff_out, d_logits, attn_ws};
+                            d_attn, d_attn_out, d_ff, d_ff_out, d_logits, attn_ws, tp_weights, d_gath,
+                            d_flags, d_epoch, d_peer_outs, d_peer_flags};
         for (void* p : dev_ptrs)
             if (p) cudaFree(p);
         if (h_in) cudaFreeHost(h_in);
         if (h_next) cudaFreeHost(h_next);
+    }
+
+    // This rank's slices of the full weights: QKV rows of its heads (zero rows
+    // for padding heads) and the output projection widened with zero input
+    // columns for the padding heads, so it reads the gathered buffer as is.
+    void build_tp_weights() {
+        if (tp == 1) return;
+        const int D = shape.d_model, L = shape.n_layer;
+        const size_t QD = static_cast<size_t>(hl) * head_dim;
+        const int h0 = tp_rank * hl;
+        const int nreal = std::max(0, std::min(shape.n_head, h0 + hl) - h0);
+        const size_t rows = static_cast<size_t>(nreal) * head_dim;
+        const size_t w_qkv = align256(3 * QD * D * es), b_qkv = align256(3 * QD * es);
+        const size_t w_proj = align256(static_cast<size_t>(D) * tp * QD * es);
+        const size_t per = w_qkv + b_qkv + w_proj;
+        cuda_ok(cudaMalloc(&tp_weights, per * L), "malloc head-sharded weights");
+        cuda_ok(cudaMemsetAsync(tp_weights, 0, per * L, stream), "memset head-sharded weights");
+        for (int l = 0; l < L; ++l) {
+            const LayerW& w = layers[static_cast<size_t>(l)];
+            char* base = static_cast<char*>(tp_weights) + static_cast<size_t>(l) * per;
+            char* qw = base;
+            char* qb = base + w_qkv;
+            char* pw = base + w_qkv + b_qkv;
+            for (int part = 0; part < 3; ++part) {  // q, k, v rows of heads [h0, h0 + nreal)
+                const size_t src_row = static_cast<size_t>(part) * D + static_cast<size_t>(h0) * head_dim;
+                if (rows == 0) break;
+                cuda_ok(cudaMemcpyAsync(qw + part * QD * D * es, static_cast<const char*>(w.qkv_w) + src_row * D * es,
+                                        rows * D * es, cudaMemcpyDeviceToDevice, stream),
+                        "slice qkv_w");
+                cuda_ok(cudaMemcpyAsync(qb + part * QD * es, static_cast<const char*>(w.qkv_b) + src_row * es, rows * es,
+                                        cudaMemcpyDeviceToDevice, stream),
+                        "slice qkv_b");
+            }
+            cuda_ok(cudaMemcpy2DAsync(pw, tp * QD * es, w.proj_w, static_cast<size_t>(D) * es,
+                                      static_cast<size_t>(D) * es, D, cudaMemcpyDeviceToDevice, stream),
+                    "pad proj_w");
+            qkv_w_loc.push_back(qw);
+            qkv_b_loc.push_back(qb);
+            proj_w_pad.push_back(pw);
+        }
+        cuda_ok(cudaStreamSynchronize(stream), "head-sharded weights");
     }
 
     void check_shape() {
@@ -195,6 +254,11 @@ struct Engine {
         if (cfg.max_batch <= 0 || cfg.max_seq_len <= 0 || cfg.max_seq_len > s.n_ctx || cfg.kv_block_budget <= 0)
             throw Error(B2_ERR_SHAPE, "invalid engine config (max_batch, max_seq_len <= n_ctx, kv_block_budget)");
         if (cfg.dtype != B2_F32 && cfg.dtype != B2_F16 && cfg.dtype != B2_BF16) throw Error(B2_ERR_DTYPE, "unknown dtype");
+        tp = cfg.tp_size <= 1 ? 1 : cfg.tp_size;
+        tp_rank = tp == 1 ? 0 : cfg.tp_rank;
+        if (tp > B2_MAX_GATHER || tp_rank < 0 || tp_rank >= tp)
+            throw Error(B2_ERR_SHAPE, "tp_size must be 1..8 and tp_rank in [0, tp_size)");
+        hl = (s.n_head + tp - 1) / tp;
     }
 
     // Vocabulary rounded up to a multiple of 8: wte (the tied lm_head) gets
@@ -225,7 +289,7 @@ struct Engine {
     // for GPT-2 XL) apart, each on its own 2 MB page; over a 100 GB pool the
     // page-translation misses cost attention ~30% of its bandwidth.
     size_t layer_bytes() const {
-        return static_cast<size_t>(num_blocks) * 2 * B2_BLOCK_TOKENS * shape.n_head * head_dim * es;
+        return static_cast<size_t>(num_blocks) * 2 * B2_BLOCK_TOKENS * hl * head_dim * es;
     }
     void* layer_pool(int l) const { return static_cast<char*>(pool) + static_cast<size_t>(l) * layer_bytes(); }
 
@@ -288,7 +352,19 @@ struct Engine {
         auto act = [&](void** p, size_t cols, const char* what) { cuda_ok(cudaMalloc(p, static_cast<size_t>(B) * cols * es), what); };
         act(&d_resid, D, "malloc residual");
         act(&d_x, D, "malloc ln out");
-        act(&d_qkv, 3 * static_cast<size_t>(D), "malloc qkv");
+        act(&d_qkv, 3 * static_cast<size_t>(hl) * head_dim, "malloc qkv");
+        if (tp > 1) {
+            const size_t gath = static_cast<size_t>(B) * tp * hl * head_dim * es;
+            cuda_ok(cudaMalloc(&d_gath, gath), "malloc gathered attention output");
+            cuda_ok(cudaMemsetAsync(d_gath, 0, gath, stream), "memset gathered attention output");
+            const size_t nflags = static_cast<size_t>(shape.n_layer) * tp;
+            cuda_ok(cudaMalloc(&d_flags, nflags * 4), "malloc barrier flags");
+            cuda_ok(cudaMemsetAsync(d_flags, 0, nflags * 4, stream), "memset barrier flags");
+            cuda_ok(cudaMalloc(&d_epoch, 4), "malloc epoch");
+            cuda_ok(cudaMemsetAsync(d_epoch, 0, 4, stream), "memset epoch");
+            cuda_ok(cudaMalloc(&d_peer_outs, tp * sizeof(void*)), "malloc peer table");
+            cuda_ok(cudaMalloc(&d_peer_flags, tp * sizeof(void*)), "malloc peer table");
+        }
         act(&d_attn, D, "malloc attention out");
         act(&d_attn_out, D, "malloc proj out");
         act(&d_ff, 4 * static_cast<size_t>(D), "malloc ff");
@@ -308,14 +384,14 @@ struct Engine {
         a.dtype = dt;
         a.out_dtype = dt;
         a.q = d_qkv;
-        a.q_row_stride = 3 * shape.d_model;
+        a.q_row_stride = 3 * hl * head_dim;
         a.kv_pool = layer_pool(layer);
         a.block_tables = in_tables();
         a.seq_lens = d_seq_post;
-        a.out = d_attn;
+        a.out = tp > 1 ? d_gath : d_attn;
         a.batch = bucket;
-        a.n_head = shape.n_head;
-        a.n_kv_head = shape.n_head;
+        a.n_head = hl;
+        a.n_kv_head = hl;
         a.head_dim = head_dim;
         a.max_blocks_per_seq = mbps;
         a.layer_idx = 0;
@@ -340,26 +416,31 @@ struct Engine {
         const float eps = shape.layer_norm_epsilon;
         b2_stream_t s = stream;
         const char* qkv = static_cast<const char*>(d_qkv);
+        if (tp > 1) b2_ok(b2_tp_epoch_bump(d_epoch, s), "tp_epoch_bump");  // a new step for the barriers
         b2_ok(b2_embedding(dt, d_resid, wte, wpe, in_tokens(), in_positions(), bucket, D, V, shape.n_ctx, s), "embedding");
         const void* delta = nullptr;
         const void* delta_bias = nullptr;
         for (int l = 0; l < L; ++l) {
             const LayerW& w = layers[static_cast<size_t>(l)];
             b2_ok(b2_add_layernorm(dt, d_x, d_resid, delta, delta_bias, d_resid, w.ln1_g, w.ln1_b, bucket, D, eps, s), "ln1");
-            gemm(bucket, D, 3 * D, d_x, w.qkv_w, d_qkv);
+            // this engine's heads: all of them, or its slice when head-sharded
+            const int QD = hl * head_dim;
+            const void* qkv_w = tp > 1 ? qkv_w_loc[static_cast<size_t>(l)] : w.qkv_w;
+            const char* qkv_b = static_cast<const char*>(tp > 1 ? qkv_b_loc[static_cast<size_t>(l)] : w.qkv_b);
+            gemm(bucket, D, 3 * QD, d_x, qkv_w, d_qkv);
             B2KvAppendArgs ka{};
             ka.dtype = dt;
             ka.kv_pool = layer_pool(l);
-            ka.k = qkv + static_cast<size_t>(D) * es;
-            ka.v = qkv + 2 * static_cast<size_t>(D) * es;
-            ka.kv_row_stride = 3 * D;
-            ka.k_bias = static_cast<const char*>(w.qkv_b) + static_cast<size_t>(D) * es;
-            ka.v_bias = static_cast<const char*>(w.qkv_b) + 2 * static_cast<size_t>(D) * es;
+            ka.k = qkv + static_cast<size_t>(QD) * es;
+            ka.v = qkv + 2 * static_cast<size_t>(QD) * es;
+            ka.kv_row_stride = 3 * QD;
+            ka.k_bias = qkv_b + static_cast<size_t>(QD) * es;
+            ka.v_bias = qkv_b + 2 * static_cast<size_t>(QD) * es;
             ka.block_tables = in_tables();
             ka.seq_lens = in_seq_lens();
             ka.seq_lens_post = l == 0 ? d_seq_post : nullptr;  // same for every layer
             ka.batch = bucket;
-            ka.n_kv_head = shape.n_head;
+            ka.n_kv_head = hl;
             ka.head_dim = head_dim;
             ka.max_blocks_per_seq = mbps;
             ka.layer_idx = 0;
@@ -367,9 +448,17 @@ struct Engine {
             ka.num_blocks = num_blocks;
             b2_ok(b2_kv_append(&ka, s), "kv_append");
             B2PagedAttnArgs aa = attn_args(bucket, l);
-            aa.q_bias = w.qkv_b;
-            b2_ok(b2_paged_attention(&aa, attn_ws, attn_ws_bytes, s), "paged_attention");
-            gemm(bucket, D, D, d_attn, w.proj_w, d_attn_out);
+            aa.q_bias = qkv_b;
+            if (tp > 1) {
+                // all-gather in the attention epilogue, then meet the peers
+                B2OutputGather g{d_peer_outs, tp, static_cast<int64_t>(tp) * QD, static_cast<int64_t>(tp_rank) * QD};
+                b2_ok(b2_paged_attention_gather(&aa, attn_ws, attn_ws_bytes, &g, s), "paged_attention_gather");
+                b2_ok(b2_tp_barrier(d_flags, d_peer_flags, tp_rank, tp, d_epoch, l, s), "tp_barrier");
+                gemm(bucket, tp * QD, D, d_gath, proj_w_pad[static_cast<size_t>(l)], d_attn_out);
+            } else {
+                b2_ok(b2_paged_attention(&aa, attn_ws, attn_ws_bytes, s), "paged_attention");
+                gemm(bucket, D, D, d_attn, w.proj_w, d_attn_out);
+            }
             b2_ok(b2_add_layernorm(dt, d_x, d_resid, d_attn_out, w.proj_b, d_resid, w.ln2_g, w.ln2_b, bucket, D, eps, s), "ln2");
             gemm(bucket, D, 4 * D, d_x, w.fc_w, d_ff);
             b2_ok(b2_bias_gelu(dt, d_ff, d_ff, w.fc_b, bucket, 4 * D, s), "bias_gelu");
@@ -415,6 +504,7 @@ struct Engine {
 
     void decode_step(const int32_t* ids, int batch, int32_t* out) {
         if (batch <= 0 || batch > cfg.max_batch) throw Error(B2_ERR_SHAPE, "batch must be in [1, max_batch]");
+        if (tp > 1 && !tp_connected) throw Error(B2_ERR_SHAPE, "head-sharded engine is not connected (b2_engine_tp_connect)");
         std::vector<Seq*> sv(static_cast<size_t>(batch));
         int need = 0;
         for (int i = 0; i < batch; ++i) {
@@ -579,7 +669,7 @@ void synth_weights(Engine& e, uint64_t seed, float stdev) {
 // Bench hook: the KV pool of a synthetic engine holds N(0, 1) values instead
 // of zeros, so cached contexts look like real keys and values.
 void synth_pool(Engine& e, uint64_t seed) {
-    const size_t n = static_cast<size_t>(e.shape.n_layer) * 2 * B2_BLOCK_TOKENS * e.shape.d_model * e.num_blocks;
+    const size_t n = e.layer_bytes() / e.es * e.shape.n_layer;
     const uint64_t key = seed * 0x9e3779b97f4a7c15ull + 0x6b7650ull;
     const int grid = 148 * 32;
     if (e.dt == B2_F32) synth_normal_kernel<float><<<grid, 256, 0, e.stream>>>(static_cast<float*>(e.pool), n, key, 1.0f);
@@ -631,6 +721,7 @@ int b2_engine_create(const char* weights_dir, const B2EngineConfig* cfg, b2_engi
         e->check_shape();
         e->setup_device();
         b2::eng::load_weights(*e, weights_dir);
+        e->build_tp_weights();
         e->setup_buffers();
     });
     if (rc == B2_OK) *out = e.release();
@@ -651,6 +742,7 @@ int b2_engine_create_synthetic(const B2ModelShape* shape, uint64_t seed, float s
         e->check_shape();
         e->setup_device();
         b2::eng::synth_weights(*e, seed, stdev);
+        e->build_tp_weights();
         e->setup_buffers();
         b2::eng::synth_pool(*e, seed);
     });
@@ -737,6 +829,53 @@ int b2_engine_stream(const b2_engine* eng, b2_stream_t* out) {
     if (!eng || !out) return B2_ERR_NULL;
     *out = eng->stream;
     return B2_OK;
+}
+
+int b2_engine_tp_handle(const b2_engine* eng, void* out) {
+    if (!eng || !out) return B2_ERR_NULL;
+    static_assert(2 * sizeof(cudaIpcMemHandle_t) == B2_TP_HANDLE_BYTES, "IPC handle size");
+    return guarded([&] {
+        if (eng->tp <= 1) throw Error(B2_ERR_SHAPE, "not a head-sharded engine");
+        b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
+        cudaIpcMemHandle_t h[2];
+        b2::eng::cuda_ok(cudaIpcGetMemHandle(&h[0], eng->d_gath), "cudaIpcGetMemHandle (gathered buffer)");
+        b2::eng::cuda_ok(cudaIpcGetMemHandle(&h[1], eng->d_flags), "cudaIpcGetMemHandle (flags)");
+        std::memcpy(out, h, sizeof(h));
+    });
+}
+
+int b2_engine_tp_connect(b2_engine* eng, const void* handles) {
+    if (!eng || !handles) return B2_ERR_NULL;
+    return guarded([&] {
+        if (eng->tp <= 1) throw Error(B2_ERR_SHAPE, "not a head-sharded engine");
+        if (eng->tp_connected) throw Error(B2_ERR_SHAPE, "already connected");
+        b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
+        std::vector<void*> outs(static_cast<size_t>(eng->tp)), flags(static_cast<size_t>(eng->tp));
+        const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+        for (int p = 0; p < eng->tp; ++p) {
+            if (p == eng->tp_rank) {
+                outs[p] = eng->d_gath;
+                flags[p] = eng->d_flags;
+                continue;
+            }
+            void* o = nullptr;
+            void* f = nullptr;
+            b2::eng::cuda_ok(cudaIpcOpenMemHandle(&o, h[2 * p], cudaIpcMemLazyEnablePeerAccess),
+                             "cudaIpcOpenMemHandle (peer gathered buffer)");
+            eng->peer_mapped.push_back(o);
+            b2::eng::cuda_ok(cudaIpcOpenMemHandle(&f, h[2 * p + 1], cudaIpcMemLazyEnablePeerAccess),
+                             "cudaIpcOpenMemHandle (peer flags)");
+            eng->peer_mapped.push_back(f);
+            outs[p] = o;
+            flags[p] = f;
+        }
+        b2::eng::cuda_ok(cudaMemcpy(eng->d_peer_outs, outs.data(), outs.size() * sizeof(void*), cudaMemcpyHostToDevice),
+                         "upload peer table");
+        b2::eng::cuda_ok(cudaMemcpy(eng->d_peer_flags, flags.data(), flags.size() * sizeof(void*),
+                                    cudaMemcpyHostToDevice),
+                         "upload peer table");
+        eng->tp_connected = true;
+    });
 }
 
 b2_block_pool* b2_block_pool_create(int32_t num_blocks) { return num_blocks >= 0 ? new b2_block_pool(num_blocks) : nullptr; }

@@ -25,8 +25,10 @@ ENGINE_SYMBOLS = (
     "b2_engine_add_sequence_cached", "b2_engine_decode_step", "b2_engine_free_sequence",
     "b2_engine_free_blocks", "b2_engine_set_use_cuda_graphs", "b2_engine_shape", "b2_engine_stream",
     "b2_engine_last_error", "b2_block_pool_create", "b2_block_pool_destroy", "b2_block_pool_allocate",
-    "b2_block_pool_free", "b2_block_pool_num_free",
+    "b2_block_pool_free", "b2_block_pool_num_free", "b2_engine_tp_handle", "b2_engine_tp_connect",
 )
+
+TP_HANDLE_BYTES = 128
 
 ERR_POOL, ERR_IO = -8, -9
 
@@ -36,7 +38,7 @@ _i32, _vp = ctypes.c_int32, ctypes.c_void_p
 class EngineConfig(ctypes.Structure):
     """gpu-engine/include/engine/engine_api.h:9-13 plus dtype, graphs and device."""
     _fields_ = [("max_batch", _i32), ("max_seq_len", _i32), ("kv_block_budget", _i32), ("dtype", _i32),
-                ("use_cuda_graphs", _i32), ("device", _i32)]
+                ("use_cuda_graphs", _i32), ("device", _i32), ("tp_rank", _i32), ("tp_size", _i32)]
 
 
 class ModelShape(ctypes.Structure):
@@ -85,6 +87,8 @@ def load() -> ctypes.CDLL:
     lib.b2_block_pool_allocate.argtypes = [_vp]
     lib.b2_block_pool_free.argtypes = [_vp, _i32]
     lib.b2_block_pool_num_free.argtypes = [_vp]
+    lib.b2_engine_tp_handle.argtypes = [_vp, ctypes.c_char_p]
+    lib.b2_engine_tp_connect.argtypes = [_vp, ctypes.c_char_p]
     _lib = lib
     return lib
 
@@ -110,10 +114,12 @@ class Config:
     dtype: int = F16
     use_cuda_graphs: bool = True
     device: int = -1
+    tp_rank: int = 0   # head-sharded engines: this rank
+    tp_size: int = 1   # > 1: heads split over tp_size GPUs (see include/b2_engine.h)
 
     def to_c(self) -> EngineConfig:
         return EngineConfig(self.max_batch, self.max_seq_len, self.kv_block_budget, self.dtype,
-                            1 if self.use_cuda_graphs else 0, self.device)
+                            1 if self.use_cuda_graphs else 0, self.device, self.tp_rank, self.tp_size)
 
 
 class Engine:
@@ -173,6 +179,19 @@ class Engine:
 
     def set_use_cuda_graphs(self, enabled: bool) -> None:
         _check(self._lib.b2_engine_set_use_cuda_graphs(self._handle(), 1 if enabled else 0))
+
+    def tp_handle(self) -> bytes:
+        """This head-sharded rank's IPC handles, to be shared with every rank."""
+        buf = ctypes.create_string_buffer(TP_HANDLE_BYTES)
+        _check(self._lib.b2_engine_tp_handle(self._handle(), buf))
+        return buf.raw
+
+    def tp_connect(self, handles: Sequence[bytes]) -> None:
+        """Maps every rank's buffers (handles in rank order, this rank's included)."""
+        blob = b"".join(handles)
+        if any(len(h) != TP_HANDLE_BYTES for h in handles):
+            raise ValueError("each handle is TP_HANDLE_BYTES bytes")
+        _check(self._lib.b2_engine_tp_connect(self._handle(), blob))
 
     def shape(self) -> ModelShape:
         s = ModelShape()

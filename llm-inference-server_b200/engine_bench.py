@@ -39,6 +39,7 @@ class EngineWorkload:
     ctx_lo: int
     wave_cap: int
     description: str
+    head_sharded: bool = False  # every rank holds every sequence and ceil(H / ranks) of the heads
 
 
 ENGINE_WORKLOADS = {
@@ -51,6 +52,13 @@ ENGINE_WORKLOADS = {
         "gpt2-medium", 24, 16, 1024, 50257, 1024, F16, 128, 32, 128,
         "GPT-2 medium-shaped decode: 24 layers, 16 heads, d_model 1024, head_dim 64, fp16, weights N(0,0.02); "
         "batch 128 sequences per GPU, cached contexts U[32, 1024-steps], KV N(0,1), block 16"),
+    "gpt2-xl-heads": EngineWorkload(
+        "gpt2-xl-heads", 48, 25, 1600, 50257, 1024, BF16, 1024, 256, 1024,
+        "GPT-2 XL-shaped decode, head-sharded: 48 layers, 25 heads split ceil(25/N) per GPU, d_model 1600, "
+        "head_dim 64, bf16, weights N(0,0.02); global batch 1024 sequences on every GPU, cached contexts "
+        "U[256, 1024-steps], KV N(0,1) (each GPU holds its heads' slice), attention output all-gathered in the "
+        "attention epilogue over NVLink, flag barrier per layer; LN, projections, MLP and lm_head replicated",
+        head_sharded=True),
 }
 
 
@@ -64,13 +72,23 @@ def elem_bytes(dt: int) -> int:
     return 4 if dt == F32 else 2
 
 
-def step_bytes(w: EngineWorkload, ctx: np.ndarray) -> float:
-    """Algorithmic HBM bytes of one decode step over sequences with cached
-    contexts ctx (before the step): every weight once, every cached K/V row of
-    every layer once, the new K/V rows written once."""
+def step_bytes(w: EngineWorkload, ctx: np.ndarray, world: int = 1) -> float:
+    """Algorithmic HBM bytes of one decode step (on one GPU) over sequences
+    with cached contexts ctx (before the step): every weight it reads once,
+    every cached K/V row of every layer once, the new K/V rows written once.
+    A head-sharded GPU reads its QKV slice, a zero-padded output projection
+    and the replicated rest, and only its heads' K/V."""
     es = elem_bytes(w.dtype)
-    kv_row = w.n_layer * 2 * w.d_model * es
-    return float(weight_elems(w) * es + (ctx.astype(np.float64) + 1).sum() * kv_row)
+    D, L = w.d_model, w.n_layer
+    if w.head_sharded and world > 1:
+        hd = D // w.n_head
+        qd = -(-w.n_head // world) * hd  # this GPU's heads x head_dim
+        weights = weight_elems(w) - L * (3 * D * D + 3 * D + D * D) + L * (3 * qd * D + 3 * qd + D * world * qd)
+        kv_row = L * 2 * qd * es
+    else:
+        weights = weight_elems(w)
+        kv_row = L * 2 * D * es
+    return float(weights * es + (ctx.astype(np.float64) + 1).sum() * kv_row)
 
 
 def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist, device, timed_region=None) -> dict:
@@ -80,15 +98,18 @@ def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist,
 
     from . import engine as E
 
+    sharded = w.head_sharded and world > 1
+    if w.head_sharded and world == 1:
+        raise ValueError("the head-sharded workload needs 2 or more GPUs")
     if w.global_batch % world:
         raise ValueError(f"global batch {w.global_batch} does not split over {world} ranks")
-    per_rank = w.global_batch // world
+    per_rank = w.global_batch if sharded else w.global_batch // world
     wave = min(per_rank, w.wave_cap)
     n_waves = (per_rank + wave - 1) // wave
     total = warmup + steps
     if w.ctx_lo + total > w.n_ctx:
         raise ValueError("too many steps for the context range")
-    rng = np.random.Generator(np.random.PCG64(20_000 + rank))
+    rng = np.random.Generator(np.random.PCG64(20_000 + (0 if sharded else rank)))  # shards see the same batch
     ctx = rng.integers(w.ctx_lo, w.n_ctx - total + 1, size=per_rank)
     last_tok = rng.integers(0, w.vocab, size=per_rank)
     blocks_needed = max(int(((ctx[i:i + wave] + total + BLOCK_TOKENS - 1) // BLOCK_TOKENS).sum())
@@ -97,7 +118,13 @@ def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist,
                          layer_norm_epsilon=1e-5, eos_token_id=-1)
     eng = E.Engine()
     eng.init_synthetic(shape, E.Config(max_batch=wave, max_seq_len=w.n_ctx, kv_block_budget=blocks_needed + 64,
-                                       dtype=w.dtype, use_cuda_graphs=True, device=device.index), seed=1, std=0.02)
+                                       dtype=w.dtype, use_cuda_graphs=True, device=device.index,
+                                       tp_rank=rank if sharded else 0, tp_size=world if sharded else 1),
+                       seed=1, std=0.02)
+    if sharded:
+        handles = [None] * world
+        dist.all_gather_object(handles, eng.tp_handle())
+        eng.tp_connect(handles)
     stream = torch.cuda.ExternalStream(eng.stream_handle(), device=device)
 
     def barrier():
@@ -125,9 +152,11 @@ def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist,
         barrier()
         timed_ms += ev0.elapsed_time(ev1)
         c0 = ctx[lo:hi] + warmup
-        bytes_timed += sum(step_bytes(w, c0 + s) for s in range(steps))
+        bytes_timed += sum(step_bytes(w, c0 + s, world) for s in range(steps))
         for i in ids:
             eng.free_sequence(i)
     eng.close()
-    return {"ms": timed_ms, "tokens": per_rank * steps, "bytes": bytes_timed, "waves": n_waves, "wave": wave,
+    # a head-sharded job produces each sequence's token once (every rank holds a copy)
+    tokens = per_rank * steps / (world if sharded else 1)
+    return {"ms": timed_ms, "tokens": tokens, "bytes": bytes_timed, "waves": n_waves, "wave": wave,
             "per_rank": per_rank}

@@ -109,6 +109,10 @@ def test_engine_create_refuses_missing_and_bad_files(E, tmp_path):
     (bad / "config.json").write_text(json.dumps(cfg))
     assert eng.init(bad, E.Config(max_seq_len=32)) is False
     assert "head_dim" in eng.last_error()
+    # head-sharded configs outside 1..8 ranks, or a rank outside the group
+    for tp_size, tp_rank in ((9, 0), (2, 2), (2, -1)):
+        assert eng.init(d, E.Config(max_seq_len=32, tp_size=tp_size, tp_rank=tp_rank)) is False
+        assert "tp_size" in eng.last_error()
 
 
 CXX_CALLER = r"""
