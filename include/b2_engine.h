@@ -40,6 +40,7 @@ typedef struct B2EngineConfig {
     int32_t device;          /* CUDA device ordinal; -1 = the current device */
     int32_t tp_rank;         /* head-sharded engines: this rank (0 .. tp_size-1) */
     int32_t tp_size;         /* 0 or 1: one engine holds every head; 2..8: head-sharded */
+    int32_t max_prefill_tokens; /* prompt tokens one b2_engine_prefill call may carry; 0 = 2048 */
 } B2EngineConfig;
 
 /* gpu-engine/include/engine/model.h:7-18 (GPT2Config). */
@@ -86,6 +87,19 @@ B2_API int32_t b2_engine_add_sequence_cached(b2_engine* eng, int32_t ctx_len, in
  * block is taken when a sequence crosses a 16-token boundary; running out of
  * blocks returns B2_ERR_POOL (the reference throws) with nothing launched. */
 B2_API int b2_engine_decode_step(b2_engine* eng, const int32_t* seq_ids, int32_t batch, int32_t* out_next_tokens);
+
+/* Batched prefill (no reference counterpart: the reference walks every prompt
+ * token by token through decode_step at batch 1, gpu-engine/src/engine.cu:8-18
+ * and cpp-engine/src/gpu_engine_generator.cpp:28-42).  Runs the whole remaining
+ * prompt of each listed sequence in one pass -- every prompt token a row of the
+ * same GEMMs, each token's K/V appended at its position, each attending to the
+ * positions up to its own -- and writes each sequence's first generated token,
+ * as decode_step would after the last prompt token.  Afterwards the sequences
+ * continue with decode_step.  Every listed sequence must still be inside its
+ * prompt; the call's prompt tokens may not exceed cfg.max_prefill_tokens.
+ * Blocks are taken for all prompt positions up front (B2_ERR_POOL if they do
+ * not fit, with nothing changed).  Not available on head-sharded engines. */
+B2_API int b2_engine_prefill(b2_engine* eng, const int32_t* seq_ids, int32_t n, int32_t* out_next_tokens);
 
 /* Engine::free_sequence: returns the sequence's blocks; unknown ids are ignored. */
 B2_API int b2_engine_free_sequence(b2_engine* eng, int32_t seq_id);

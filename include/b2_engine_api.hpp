@@ -32,6 +32,7 @@ struct EngineConfig {
     int device = -1;  // -1: the device current on the calling thread
     int tp_rank = 0;  // head-sharded engines (include/b2_engine.h)
     int tp_size = 1;
+    int max_prefill_tokens = 0;  // 0: 2048
 };
 
 class Engine {
@@ -45,7 +46,8 @@ public:
         b2_engine_destroy(eng_);
         eng_ = nullptr;
         const B2EngineConfig c{cfg.max_batch, cfg.max_seq_len, cfg.kv_block_budget, cfg.dtype,
-                               cfg.use_cuda_graphs ? 1 : 0, cfg.device, cfg.tp_rank, cfg.tp_size};
+                               cfg.use_cuda_graphs ? 1 : 0, cfg.device, cfg.tp_rank, cfg.tp_size,
+                               cfg.max_prefill_tokens};
         return b2_engine_create(weights_dir.c_str(), &c, &eng_) == B2_OK;
     }
 
@@ -57,6 +59,12 @@ public:
 
     void decode_step(const int* seq_ids, int batch, int* out_next_tokens) {
         if (b2_engine_decode_step(handle(), seq_ids, batch, out_next_tokens) != B2_OK)
+            throw std::runtime_error(b2_engine_last_error());
+    }
+
+    // Batched prefill of the listed sequences' prompts (no reference counterpart).
+    void prefill(const int* seq_ids, int n, int* out_next_tokens) {
+        if (b2_engine_prefill(handle(), seq_ids, n, out_next_tokens) != B2_OK)
             throw std::runtime_error(b2_engine_last_error());
     }
 

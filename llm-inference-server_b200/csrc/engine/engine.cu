@@ -92,6 +92,15 @@ __global__ void fill_kernel(T* dst, size_t n, float v) {
         dst[i] = static_cast<T>(v);
 }
 
+// dst[i] = src[rows[i]] for n rows of `cols` 16-byte chunks (prefill: each
+// sequence's last prompt row goes on to the lm_head).
+__global__ void gather_rows_kernel(uint4* dst, const uint4* src, const int32_t* rows, int n, int cols) {
+    for (int i = blockIdx.x; i < n; i += gridDim.x) {
+        const uint4* s = src + static_cast<size_t>(rows[i]) * cols;
+        for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[static_cast<size_t>(i) * cols + c] = s[c];
+    }
+}
+
 // ------------------------------------------------------------- the engine
 
 struct LayerW {
@@ -182,6 +191,14 @@ struct Engine {
     uint32_t** d_peer_flags = nullptr;
     std::vector<void*> peer_mapped;  // IPC-opened peer bases, closed at destruction
     bool tp_connected = false;
+    // Batched prefill (allocated at the first b2_engine_prefill): per-row inputs
+    // [tokens | positions | seq_lens | last rows (max_batch) | tables (cap x mbps)],
+    // row activations, and the per-sequence tail (last rows, logits, next tokens).
+    int prefill_cap = 0;
+    int32_t *d_pin = nullptr, *h_pin = nullptr, *d_pseq_post = nullptr, *d_pnext = nullptr, *h_pnext = nullptr;
+    void *p_resid = nullptr, *p_x = nullptr, *p_qkv = nullptr, *p_attn = nullptr, *p_attn_out = nullptr,
+         *p_ff = nullptr, *p_ff_out = nullptr, *p_last = nullptr, *p_logits = nullptr, *p_attn_ws = nullptr;
+    size_t p_attn_ws_bytes = 0;
 
     int32_t* in_tokens() const { return d_in; }
     int32_t* in_positions() const { return d_in + cfg.max_batch; }
@@ -196,11 +213,15 @@ struct Engine {
         for (void* p : peer_mapped) cudaIpcCloseMemHandle(p);
         void* dev_ptrs[] = {weights, pool, cublas_ws, d_in, d_seq_post, d_next, d_resid, d_x, d_qkv,
                             d_attn, d_attn_out, d_ff, d_ff_out, d_logits, attn_ws, tp_weights, d_gath,
-                            d_flags, d_epoch, d_peer_outs, d_peer_flags};
+                            d_flags, d_epoch, d_peer_outs, d_peer_flags, d_pin, d_pseq_post, d_pnext,
+                            p_resid, p_x, p_qkv, p_attn, p_attn_out, p_ff, p_ff_out, p_last, p_logits,
+                            p_attn_ws};
         for (void* p : dev_ptrs)
             if (p) cudaFree(p);
         if (h_in) cudaFreeHost(h_in);
         if (h_next) cudaFreeHost(h_next);
+        if (h_pin) cudaFreeHost(h_pin);
+        if (h_pnext) cudaFreeHost(h_pnext);
     }
 
     // This rank's slices of the full weights: QKV rows of its heads (zero rows
@@ -502,6 +523,158 @@ struct Engine {
         return b < cfg.max_batch ? b : cfg.max_batch;
     }
 
+    void setup_prefill() {
+        if (prefill_cap > 0) return;
+        const int cap = cfg.max_prefill_tokens > 0 ? cfg.max_prefill_tokens : 2048;
+        const int B = cfg.max_batch, D = shape.d_model;
+        const size_t in_ints = 3 * static_cast<size_t>(cap) + B + static_cast<size_t>(cap) * mbps;
+        cuda_ok(cudaMalloc(&d_pin, in_ints * 4), "malloc prefill inputs");
+        cuda_ok(cudaMallocHost(&h_pin, in_ints * 4), "pinned prefill inputs");
+        std::memset(h_pin, 0, in_ints * 4);
+        cuda_ok(cudaMalloc(&d_pseq_post, static_cast<size_t>(cap) * 4), "malloc prefill seq_lens_post");
+        cuda_ok(cudaMalloc(&d_pnext, static_cast<size_t>(B) * 4), "malloc prefill next tokens");
+        cuda_ok(cudaMallocHost(&h_pnext, static_cast<size_t>(B) * 4), "pinned prefill next tokens");
+        auto act = [&](void** p, size_t rows, size_t cols, const char* what) {
+            cuda_ok(cudaMalloc(p, rows * cols * es), what);
+        };
+        const size_t QD = static_cast<size_t>(hl) * head_dim;
+        act(&p_resid, cap, D, "malloc prefill residual");
+        act(&p_x, cap, D, "malloc prefill ln out");
+        act(&p_qkv, cap, 3 * QD, "malloc prefill qkv");
+        act(&p_attn, cap, D, "malloc prefill attention out");
+        act(&p_attn_out, cap, D, "malloc prefill proj out");
+        act(&p_ff, cap, 4 * static_cast<size_t>(D), "malloc prefill ff");
+        act(&p_ff_out, cap, D, "malloc prefill ff out");
+        act(&p_last, B, D, "malloc prefill last rows");
+        act(&p_logits, B, static_cast<size_t>(vocab_padded()), "malloc prefill logits");
+        B2PagedAttnArgs a = attn_args(cap, 0);
+        p_attn_ws_bytes = b2_paged_attention_workspace_bytes(&a);
+        if (p_attn_ws_bytes == 0) throw Error(B2_ERR_UNSUPPORTED, std::string("prefill attention: ") + b2_last_error_string());
+        cuda_ok(cudaMalloc(&p_attn_ws, p_attn_ws_bytes), "malloc prefill attention workspace");
+        cuda_ok(cudaMemsetAsync(p_attn_ws, 0, p_attn_ws_bytes, stream), "zero prefill attention workspace");
+        prefill_cap = cap;
+    }
+
+    // One pass over every remaining prompt token of the listed sequences: the
+    // decode step's kernels with one row per token.  Row r of sequence s is
+    // position p = seq_len(s) + t; kv_append writes its K/V at p and attention
+    // reads positions [0, p] -- causal prefill from the decode kernels.
+    void prefill(const int32_t* ids, int n, int32_t* out) {
+        if (tp > 1) throw Error(B2_ERR_UNSUPPORTED, "batched prefill is not available on head-sharded engines");
+        if (n <= 0 || n > cfg.max_batch) throw Error(B2_ERR_SHAPE, "n must be in [1, max_batch]");
+        setup_prefill();
+        std::vector<Seq*> sv(static_cast<size_t>(n));
+        int rows = 0, need = 0;
+        for (int i = 0; i < n; ++i) {
+            auto it = seqs.find(ids[i]);
+            if (it == seqs.end()) throw Error(B2_ERR_SHAPE, "unknown sequence id " + std::to_string(ids[i]));
+            Seq& q = it->second;
+            for (int j = 0; j < i; ++j)
+                if (sv[static_cast<size_t>(j)] == &q) throw Error(B2_ERR_SHAPE, "sequence listed twice in one call");
+            const int t = static_cast<int>(q.prompt.size()) - q.prompt_pos;
+            if (t <= 0) throw Error(B2_ERR_SHAPE, "sequence " + std::to_string(ids[i]) + " is past its prompt");
+            if (q.seq_len + t > cfg.max_seq_len) throw Error(B2_ERR_SHAPE, "prompt longer than max_seq_len");
+            sv[static_cast<size_t>(i)] = &q;
+            rows += t;
+            const int have = static_cast<int>(q.table.ids.size());
+            const int want = (q.seq_len + t + B2_BLOCK_TOKENS - 1) / B2_BLOCK_TOKENS;
+            need += std::max(0, want - have);
+        }
+        if (rows > prefill_cap) throw Error(B2_ERR_SHAPE, "more prompt tokens than max_prefill_tokens in one call");
+        if (need > blocks->num_free()) throw Error(B2_ERR_POOL, "KV cache block pool exhausted");
+        const int cap = prefill_cap, B = cfg.max_batch, D = shape.d_model, V = shape.vocab_size, L = shape.n_layer;
+        int32_t* tok = h_pin;
+        int32_t* pos = h_pin + cap;
+        int32_t* sl = h_pin + 2 * cap;
+        int32_t* last = h_pin + 3 * cap;
+        int32_t* bt = h_pin + 3 * cap + B;
+        int r = 0;
+        for (int i = 0; i < n; ++i) {
+            Seq& q = *sv[static_cast<size_t>(i)];
+            const int t = static_cast<int>(q.prompt.size()) - q.prompt_pos;
+            while (static_cast<int>(q.table.ids.size()) * B2_BLOCK_TOKENS < q.seq_len + t)
+                q.table.ids.push_back(blocks->allocate());
+            for (int k = 0; k < t; ++k, ++r) {
+                tok[r] = q.prompt[static_cast<size_t>(q.prompt_pos + k)];
+                pos[r] = q.seq_len + k;
+                sl[r] = q.seq_len + k;
+                int32_t* row = bt + static_cast<size_t>(r) * mbps;
+                for (size_t j = 0; j < q.table.ids.size(); ++j) row[j] = q.table.ids[j];
+            }
+            last[i] = r - 1;
+        }
+        const size_t up = (3 * static_cast<size_t>(cap) + B + static_cast<size_t>(rows) * mbps) * 4;
+        cuda_ok(cudaMemcpyAsync(d_pin, h_pin, up, cudaMemcpyHostToDevice, stream), "upload prefill inputs");
+        const int32_t* d_tok = d_pin;
+        const int32_t* d_pos = d_pin + cap;
+        const int32_t* d_sl = d_pin + 2 * cap;
+        const int32_t* d_last = d_pin + 3 * cap;
+        const int32_t* d_bt = d_pin + 3 * cap + B;
+        const float eps = shape.layer_norm_epsilon;
+        b2_stream_t s = stream;
+        const char* qkv = static_cast<const char*>(p_qkv);
+        b2_ok(b2_embedding(dt, p_resid, wte, wpe, d_tok, d_pos, rows, D, V, shape.n_ctx, s), "embedding");
+        const void* delta = nullptr;
+        const void* delta_bias = nullptr;
+        for (int l = 0; l < L; ++l) {
+            const LayerW& w = layers[static_cast<size_t>(l)];
+            b2_ok(b2_add_layernorm(dt, p_x, p_resid, delta, delta_bias, p_resid, w.ln1_g, w.ln1_b, rows, D, eps, s), "ln1");
+            gemm(rows, D, 3 * D, p_x, w.qkv_w, p_qkv);
+            B2KvAppendArgs ka{};
+            ka.dtype = dt;
+            ka.kv_pool = layer_pool(l);
+            ka.k = qkv + static_cast<size_t>(D) * es;
+            ka.v = qkv + 2 * static_cast<size_t>(D) * es;
+            ka.kv_row_stride = 3 * D;
+            ka.k_bias = static_cast<const char*>(w.qkv_b) + static_cast<size_t>(D) * es;
+            ka.v_bias = static_cast<const char*>(w.qkv_b) + 2 * static_cast<size_t>(D) * es;
+            ka.block_tables = d_bt;
+            ka.seq_lens = d_sl;
+            ka.seq_lens_post = l == 0 ? d_pseq_post : nullptr;
+            ka.batch = rows;
+            ka.n_kv_head = hl;
+            ka.head_dim = head_dim;
+            ka.max_blocks_per_seq = mbps;
+            ka.layer_idx = 0;
+            ka.n_layer = 1;
+            ka.num_blocks = num_blocks;
+            b2_ok(b2_kv_append(&ka, s), "kv_append");
+            B2PagedAttnArgs aa = attn_args(rows, l);
+            aa.q = p_qkv;
+            aa.q_bias = w.qkv_b;
+            aa.block_tables = d_bt;
+            aa.seq_lens = d_pseq_post;
+            aa.out = p_attn;
+            b2_ok(b2_paged_attention(&aa, p_attn_ws, p_attn_ws_bytes, s), "paged_attention");
+            gemm(rows, D, D, p_attn, w.proj_w, p_attn_out);
+            b2_ok(b2_add_layernorm(dt, p_x, p_resid, p_attn_out, w.proj_b, p_resid, w.ln2_g, w.ln2_b, rows, D, eps, s),
+                  "ln2");
+            gemm(rows, D, 4 * D, p_x, w.fc_w, p_ff);
+            b2_ok(b2_bias_gelu(dt, p_ff, p_ff, w.fc_b, rows, 4 * D, s), "bias_gelu");
+            gemm(rows, 4 * D, D, p_ff, w.fc_proj_w, p_ff_out);
+            delta = p_ff_out;
+            delta_bias = w.fc_proj_b;
+        }
+        b2_ok(b2_add_layernorm(dt, p_x, p_resid, delta, delta_bias, p_resid, lnf_g, lnf_b, rows, D, eps, s), "ln_f");
+        const int cols = D * es / 16;
+        gather_rows_kernel<<<std::min(n, 1024), 128, 0, stream>>>(static_cast<uint4*>(p_last),
+                                                                  static_cast<const uint4*>(p_x), d_last, n, cols);
+        cuda_ok(cudaGetLastError(), "gather last rows");
+        gemm(n, D, vocab_padded(), p_last, wte, p_logits, vocab_padded());
+        b2_ok(b2_argmax_rows(dt, d_pnext, p_logits, vocab_padded(), n, V, s), "argmax");
+        cuda_ok(cudaMemcpyAsync(h_pnext, d_pnext, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, stream),
+                "download next tokens");
+        cuda_ok(cudaStreamSynchronize(stream), "prefill");
+        for (int i = 0; i < n; ++i) {
+            Seq& q = *sv[static_cast<size_t>(i)];
+            const int t = static_cast<int>(q.prompt.size()) - q.prompt_pos;
+            q.seq_len += t;
+            q.prompt_pos = static_cast<int>(q.prompt.size());
+            q.last_token = h_pnext[i];
+            out[i] = h_pnext[i];
+        }
+    }
+
     void decode_step(const int32_t* ids, int batch, int32_t* out) {
         if (batch <= 0 || batch > cfg.max_batch) throw Error(B2_ERR_SHAPE, "batch must be in [1, max_batch]");
         if (tp > 1 && !tp_connected) throw Error(B2_ERR_SHAPE, "head-sharded engine is not connected (b2_engine_tp_connect)");
@@ -798,6 +971,17 @@ int b2_engine_decode_step(b2_engine* eng, const int32_t* seq_ids, int32_t batch,
     return guarded([&] {
         b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
         eng->decode_step(seq_ids, batch, out_next_tokens);
+    });
+}
+
+int b2_engine_prefill(b2_engine* eng, const int32_t* seq_ids, int32_t n, int32_t* out_next_tokens) {
+    if (!eng || !seq_ids || !out_next_tokens) {
+        b2::eng::g_err = "engine, seq_ids and out_next_tokens are required";
+        return B2_ERR_NULL;
+    }
+    return guarded([&] {
+        b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
+        eng->prefill(seq_ids, n, out_next_tokens);
     });
 }
 

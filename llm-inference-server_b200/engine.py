@@ -26,6 +26,7 @@ ENGINE_SYMBOLS = (
     "b2_engine_free_blocks", "b2_engine_set_use_cuda_graphs", "b2_engine_shape", "b2_engine_stream",
     "b2_engine_last_error", "b2_block_pool_create", "b2_block_pool_destroy", "b2_block_pool_allocate",
     "b2_block_pool_free", "b2_block_pool_num_free", "b2_engine_tp_handle", "b2_engine_tp_connect",
+    "b2_engine_prefill",
 )
 
 TP_HANDLE_BYTES = 128
@@ -38,7 +39,8 @@ _i32, _vp = ctypes.c_int32, ctypes.c_void_p
 class EngineConfig(ctypes.Structure):
     """gpu-engine/include/engine/engine_api.h:9-13 plus dtype, graphs and device."""
     _fields_ = [("max_batch", _i32), ("max_seq_len", _i32), ("kv_block_budget", _i32), ("dtype", _i32),
-                ("use_cuda_graphs", _i32), ("device", _i32), ("tp_rank", _i32), ("tp_size", _i32)]
+                ("use_cuda_graphs", _i32), ("device", _i32), ("tp_rank", _i32), ("tp_size", _i32),
+                ("max_prefill_tokens", _i32)]
 
 
 class ModelShape(ctypes.Structure):
@@ -89,6 +91,7 @@ def load() -> ctypes.CDLL:
     lib.b2_block_pool_num_free.argtypes = [_vp]
     lib.b2_engine_tp_handle.argtypes = [_vp, ctypes.c_char_p]
     lib.b2_engine_tp_connect.argtypes = [_vp, ctypes.c_char_p]
+    lib.b2_engine_prefill.argtypes = [_vp, P(_i32), _i32, P(_i32)]
     _lib = lib
     return lib
 
@@ -116,10 +119,12 @@ class Config:
     device: int = -1
     tp_rank: int = 0   # head-sharded engines: this rank
     tp_size: int = 1   # > 1: heads split over tp_size GPUs (see include/b2_engine.h)
+    max_prefill_tokens: int = 0  # prompt tokens per prefill call; 0 = 2048
 
     def to_c(self) -> EngineConfig:
         return EngineConfig(self.max_batch, self.max_seq_len, self.kv_block_budget, self.dtype,
-                            1 if self.use_cuda_graphs else 0, self.device, self.tp_rank, self.tp_size)
+                            1 if self.use_cuda_graphs else 0, self.device, self.tp_rank, self.tp_size,
+                            self.max_prefill_tokens)
 
 
 class Engine:
@@ -169,6 +174,13 @@ class Engine:
     def decode_step(self, seq_ids: Sequence[int]) -> list[int]:
         out = (_i32 * max(1, len(seq_ids)))()
         _check(self._lib.b2_engine_decode_step(self._handle(), _ints(seq_ids), len(seq_ids), out))
+        return list(out[:len(seq_ids)])
+
+    def prefill(self, seq_ids: Sequence[int]) -> list[int]:
+        """Batched prefill: every remaining prompt token of each sequence in one
+        pass; returns each sequence's first generated token."""
+        out = (_i32 * max(1, len(seq_ids)))()
+        _check(self._lib.b2_engine_prefill(self._handle(), _ints(seq_ids), len(seq_ids), out))
         return list(out[:len(seq_ids)])
 
     def free_sequence(self, seq_id: int) -> None:

@@ -127,3 +127,56 @@ def test_engine_synthetic_cached_contexts(E):
     for n in (1, 3, 8, 16):
         out = eng.decode_step(ids[:n])
         assert len(out) == n and all(0 <= t < 1000 for t in out)
+
+
+def engine_greedy_prefill(eng, prompts, n_new, decode_first=0):
+    """Batched prefill of every prompt (after `decode_first` prompt tokens went
+    through decode_step), then decode steps; returns the n_new generated tokens."""
+    ids = [eng.add_sequence(p) for p in prompts]
+    for _ in range(decode_first):
+        eng.decode_step(ids)
+    gen = [[t] for t in eng.prefill(ids)]
+    while any(len(g) < n_new for g in gen):
+        active = [i for i in range(len(prompts)) if len(gen[i]) < n_new]
+        for i, tok in zip(active, eng.decode_step([ids[i] for i in active])):
+            gen[i].append(tok)
+    for i in ids:
+        eng.free_sequence(i)
+    return gen
+
+
+def test_engine_prefill_matches_reference_tokens_gpt2_small(E, golden, tmp_path_factory):
+    """Batched prefill (all prompt tokens of 8 sequences in one pass) and then
+    decode: the same greedy tokens as the reference's CPUModel."""
+    fx = golden("gpt2_small_greedy.json")
+    from lis_b200 import model_files as MF
+    d = MF.write_model_dir(tmp_path_factory.mktemp("small_pf"), MF.GPT2_SMALL, seed=fx["seed"], std=fx["std"])
+    eng = E.Engine()
+    assert eng.init(d, E.Config(max_batch=8, max_seq_len=256, kv_block_budget=256, dtype=0)), eng.last_error()
+    got = engine_greedy_prefill(eng, fx["prompts"], fx["n_new"])
+    for i, (g, want) in enumerate(zip(got, fx["generated"])):
+        assert g == want, f"prompt {i} diverged"
+    assert eng.free_blocks() == 256
+
+
+def test_engine_prefill_after_partial_decode_and_errors(E, golden, tmp_path_factory):
+    fx = golden("gpt2_tiny_greedy.json")
+    case = next(c for c in fx["cases"] if c["shape"]["d_model"] // c["shape"]["n_head"] in (64, 128))
+    d = _model_dir(tmp_path_factory, case["shape"], case["seed"], case["std"], "pf_tiny")
+    eng = E.Engine()
+    assert eng.init(d, E.Config(max_batch=4, max_seq_len=case["shape"]["n_ctx"], kv_block_budget=64, dtype=0,
+                                max_prefill_tokens=80)), eng.last_error()
+    # two prompt tokens through decode_step, the rest by prefill
+    prompts = [p for p in case["prompts"] if len(p) > 2]
+    want = [g for p, g in zip(case["prompts"], case["generated"]) if len(p) > 2]
+    assert engine_greedy_prefill(eng, prompts, case["n_new"], decode_first=2) == want
+    a = eng.add_sequence([1, 2, 3])
+    eng.prefill([a])
+    with pytest.raises(Exception):
+        eng.prefill([a])  # already past its prompt
+    b = eng.add_sequence(list(range(81)))
+    with pytest.raises(Exception):
+        eng.prefill([b])  # more tokens than max_prefill_tokens
+    eng.free_sequence(a)
+    eng.free_sequence(b)
+    assert eng.free_blocks() == 64
