@@ -540,6 +540,39 @@ def run_engine(args, rank: int, world: int, dist) -> None:
 BF16_CODE = 2
 
 
+def run_serve(args, rank: int, world: int) -> None:
+    """Continuous-batching serving trace through the engine (serve_bench.py), rank 0."""
+    if rank != 0:
+        return
+    import torch
+    import_package()
+    from lis_b200 import serve_bench as SB
+    torch.cuda.set_device(0)
+    samplers: list = []
+    with ClockSampler(0) as clk:
+        r = SB.run(args.requests, args.requests_compare)
+    b, bs, ts = r["batched"], r["batched_small"], r["token_small"]
+    line = {
+        "metric": "GPT-2 medium continuous-batching output tok/s", "value": b["output_tok_s"], "unit": "tok/s",
+        "n_gpus": 1, "steps": b["decode_steps"], "warmup": 4, "ms_per_step": round(b["makespan_s"] * 1e3 /
+                                                                                  max(1, b["decode_steps"]), 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "GPT-2 medium shape (24 layers, 16 heads, d_model 1024), fp16, weights N(0,0.02); "
+                               "Poisson 50 req/s, prompts U[32,512], outputs U[16,512], max batch 128, block 16; "
+                               "scheduler loop of ContinuousBatchScheduler (admit, prefill, decode, evict)",
+                   "requests": b["requests"], "prefill": "batched (b2_engine_prefill)"},
+        "ttft_p50_ms": b["ttft_p50_ms"], "ttft_p99_ms": b["ttft_p99_ms"], "makespan_s": b["makespan_s"],
+        "prefill_comparison": {"requests": bs["requests"], "batched": bs,
+                               "token_by_token (the reference's GpuEngineGenerator)": ts},
+        "roofline": None, "roofline_note": "serving trace: arrival-bound and host-driven, no single-kernel roofline",
+        "cpu_baseline": None,
+        "e2e": {"value": b["output_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+                "path": "already end to end through b2_engine_prefill / b2_engine_decode_step"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -548,14 +581,23 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + list(ENGINE_NAMES), default="mha",
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + list(ENGINE_NAMES) + ["serve-medium"], default="mha",
                     help="mha: the headline microbench; gqa: grouped-query long contexts (tensor-core kernel); "
                          "gpt2-xl / gpt2-medium: GPT-2 decode tokens/s through the engine")
     ap.add_argument("--sets", type=int, default=None, help="rotating input sets (profiling uses fewer)")
     ap.add_argument("--pool-blocks", type=int, default=None, help="KV pool size in blocks (profiling uses fewer)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (profiling uses fewer)")
+    ap.add_argument("--requests", type=int, default=200, help="serve-medium: requests in the trace")
+    ap.add_argument("--requests-compare", type=int, default=24,
+                    help="serve-medium: requests replayed with both prefill modes")
     args = ap.parse_args()
     engine = args.workload in ENGINE_NAMES
+    if args.workload == "serve-medium":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the serving trace has no CPU arm"}), flush=True)
+            return
+        run_serve(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
+        return
     if args.steps is None:
         args.steps = 20 if engine else 5000
     if args.warmup is None:
