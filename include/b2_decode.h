@@ -154,7 +154,23 @@ typedef struct B2PagedAttnArgs {
     int32_t n_layer;
     int32_t num_blocks; /* pool capacity in blocks (bounds check) */
     float scale;        /* 0 selects 1/sqrt(head_dim) */
+    int32_t flags;      /* 0, B2_ATTN_INPUTS_READY or B2_ATTN_NEWEST_ROW_PENDING */
 } B2PagedAttnArgs;
+
+/* flags: what the kernel may read before the kernel launched just before it
+ * on the stream has finished (programmatic dependent launch lets it start
+ * early).  0: nothing -- every input waits for that kernel.
+ * B2_ATTN_INPUTS_READY: nothing this call reads is written by that kernel, so
+ *   the set-up and the K/V streaming overlap its tail.
+ * B2_ATTN_NEWEST_ROW_PENDING: only the last key row of every sequence (its
+ *   newest position, from a kv_append launched just before) may be; seq_lens,
+ *   block_tables, q, q_bias and all earlier rows were complete before that
+ *   kernel started.  The block holding each sequence's last row is read after
+ *   the wait.
+ * Outputs and the workspace are always written after the wait.  The
+ * tensor-core kernel ignores flags. */
+#define B2_ATTN_INPUTS_READY 1
+#define B2_ATTN_NEWEST_ROW_PENDING 2
 
 /* Workspace bytes for launches with this batch and head shape on the
  * current device (depends on the SM count). */

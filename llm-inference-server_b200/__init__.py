@@ -23,6 +23,7 @@ F32, F16, BF16 = 0, 1, 2
 BLOCK_TOKENS = 16
 
 B2_OK = 0
+ATTN_INPUTS_READY, ATTN_NEWEST_ROW_PENDING = 1, 2  # B2PagedAttnArgs.flags
 DEVERR_BLOCK_ID, DEVERR_SEQ_LEN, DEVERR_TIMEOUT, DEVERR_TOKEN = 1, 2, 4, 8
 
 # Every symbol include/b2_decode.h declares.
@@ -49,7 +50,8 @@ class PagedAttnArgs(ctypes.Structure):
     _fields_ = [("dtype", _c_int), ("out_dtype", _c_int), ("q", _vp), ("q_row_stride", _c_int), ("q_bias", _vp),
                 ("kv_pool", _vp), ("block_tables", _vp), ("seq_lens", _vp), ("out", _vp), ("batch", _c_int),
                 ("n_head", _c_int), ("n_kv_head", _c_int), ("head_dim", _c_int), ("max_blocks_per_seq", _c_int),
-                ("layer_idx", _c_int), ("n_layer", _c_int), ("num_blocks", _c_int), ("scale", _c_float)]
+                ("layer_idx", _c_int), ("n_layer", _c_int), ("num_blocks", _c_int), ("scale", _c_float),
+                ("flags", _c_int)]
 
 
 class B2Error(RuntimeError):
@@ -135,10 +137,10 @@ def kv_append(kv_pool, k, v, kv_row_stride, block_tables, seq_lens, *, n_kv_head
 
 
 def attn_args(q, q_row_stride, kv_pool, block_tables, seq_lens, out, *, n_head, n_kv_head, head_dim,
-              max_blocks_per_seq, layer_idx, n_layer, num_blocks, scale=0.0, q_bias=None) -> PagedAttnArgs:
+              max_blocks_per_seq, layer_idx, n_layer, num_blocks, scale=0.0, q_bias=None, flags=0) -> PagedAttnArgs:
     return PagedAttnArgs(dtype_code(kv_pool.dtype), dtype_code(out.dtype), _ptr(q), q_row_stride, _ptr(q_bias),
                          _ptr(kv_pool), _ptr(block_tables), _ptr(seq_lens), _ptr(out), block_tables.shape[0], n_head,
-                         n_kv_head, head_dim, max_blocks_per_seq, layer_idx, n_layer, num_blocks, scale)
+                         n_kv_head, head_dim, max_blocks_per_seq, layer_idx, n_layer, num_blocks, scale, flags)
 
 
 def attention_workspace(args: PagedAttnArgs):

@@ -90,6 +90,7 @@ struct AttnParams {
     float* part_acc;  // [(grid + batch) * ksplit][n_head][head_dim]
     unsigned int* counters;  // [batch] pieces finished per sequence; zero between launches
     OutSpec out;
+    int early;  // 0 wait first; 1 inputs complete; 2 only each sequence's newest row pending
 };
 
 struct CombineParams {
@@ -283,10 +284,14 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     }
 
     // Programmatic dependent launch: the kernel behind us may be scheduled
-    // right away; we wait here until the kernels before us (which produce q,
-    // the pool and seq_lens) have completed.
+    // right away.  Unless the caller said the inputs are already complete
+    // (p.early), we wait here until the kernel before us has completed; with
+    // p.early the set-up and the K/V streaming overlap its tail, and every
+    // thread waits before its first global write (outputs, partials, counters)
+    // -- and, with p.early == 2, the producer before reading each sequence's
+    // newest key row.
     pdl_launch_dependents();
-    pdl_wait();
+    if (p.early == 0) pdl_wait();
 
     // ---- prologue: per-sequence row counts, global prefix, this CTA's range
     const int per = (B + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
@@ -311,6 +316,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 if (raw != cl) flag_error(B2_DEVERR_SEQ_LEN);
                 if (cl == 0) {
                     // no keys: the output is 0, like the reference (l == 0)
+                    if (p.early) pdl_wait();
                     float z[E];
 #pragma unroll
                     for (int e = 0; e < E; ++e) z[e] = 0.0f;
@@ -343,6 +349,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         long long Pb = misc[1];
         int n = 0;
         bool failed = false;
+        bool newest_ok = p.early != 2;  // may the newest key rows be read yet?
         while (u < e_unit && !failed && bb < B) {
             const int b = bb + lane;
             int cl = 0;
@@ -386,6 +393,10 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                                 ok = 0;
                             } else {
                                 const int j = jc + x;
+                                if (!newest_ok && j == (cs - 1) / kBlockTokens) {
+                                    pdl_wait();  // this block holds the sequence's newest row
+                                    newest_ok = true;
+                                }
                                 const int r_lo = max(t_lo - j * kBlockTokens, 0);
                                 const int r_hi = min(t_hi - j * kBlockTokens, kBlockTokens);
                                 const int nrows = r_hi - r_lo;
@@ -448,6 +459,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             ok = mbar_wait_bounded(&piece_full[rk], static_cast<uint32_t>(k / R) & 1u);
             if (!ok) break;
             const int4 pc = pieces[rk];
+            if (p.early) pdl_wait();  // counters and outputs are written below
             __syncwarp();  // every lane has read the entry before it is released
             if (lane == 0) mbar_arrive(&piece_empty[rk]);
             int last = 0;
@@ -597,6 +609,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         if (lane == 0) mbar_arrive(&empty[st]);
 
         if (last) {
+            if (p.early) pdl_wait();  // the workspace is written from here on
             // ---- piece end: this subgroup's partial goes to the workspace.
             // Slot (cta + b) is unique per (CTA, sequence) pair: along the CTA
             // order both indices only grow, so cta + b never repeats.

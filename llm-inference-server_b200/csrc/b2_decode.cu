@@ -156,6 +156,8 @@ int check_attn_args(const B2PagedAttnArgs* a) {
     if (static_cast<long long>(a->batch) * a->max_blocks_per_seq * B2_BLOCK_TOKENS >= (1LL << 31))
         return fail(B2_ERR_SHAPE, "batch * max_blocks_per_seq * 16 must stay below 2^31 token rows");
     if (a->q_row_stride < a->n_head * a->head_dim) return fail(B2_ERR_SHAPE, "q_row_stride < n_head*head_dim");
+    if (a->flags != 0 && a->flags != B2_ATTN_INPUTS_READY && a->flags != B2_ATTN_NEWEST_ROW_PENDING)
+        return fail(B2_ERR_SHAPE, "unknown flags");
     if (!aligned16(a->q) || !aligned16(a->kv_pool) || !aligned16(a->out) || (a->q_bias && !aligned16(a->q_bias)) ||
         (static_cast<long long>(a->q_row_stride) * es) % 16 != 0)
         return fail(B2_ERR_ALIGN, "q, q_bias, kv_pool and out must be 16-byte aligned, q_row_stride*elem 16-byte multiple");
@@ -545,6 +547,7 @@ int paged_attention_impl(const B2PagedAttnArgs* a, void* ws, size_t ws_bytes, co
     p.out.n = gather ? gather->n_outs : 0;
     p.out.row_stride = gather ? gather->row_stride : 0;
     p.out.col_offset = gather ? gather->col_offset : 0;
+    p.early = a->flags;
     const int qg = a->n_head / a->n_kv_head;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (pl.tensor_cores) {

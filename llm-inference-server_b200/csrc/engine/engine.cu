@@ -179,8 +179,11 @@ struct Engine {
     // Head sharding (tp > 1): this engine holds heads [tp_rank * hl, tp_rank * hl + hl)
     // (hl = ceil(n_head / tp); heads past n_head are zero padding), their QKV slice,
     // a zero-padded copy of every output projection, the gathered attention output
-    // [max_batch, tp * hl * head_dim] and the barrier flags [n_layer][tp] (both
-    // IPC-shared with the peers), and the peers' addresses of both.
+    // [2][max_batch, tp * hl * head_dim] (one half per layer parity: after barrier l a
+    // fast rank may write layer l + 1 while a peer still reads layer l; it cannot come
+    // back to a half before barrier l + 1, which that peer enters only after reading)
+    // and the barrier flags [n_layer][tp] (both IPC-shared with the peers), and the
+    // peers' addresses of both (d_peer_outs: [parity][rank]).
     int tp = 1, tp_rank = 0, hl = 0;  // hl: heads held here (all of them when tp == 1)
     void* tp_weights = nullptr;
     std::vector<const void*> qkv_w_loc, qkv_b_loc, proj_w_pad;
@@ -313,6 +316,9 @@ struct Engine {
         return static_cast<size_t>(num_blocks) * 2 * B2_BLOCK_TOKENS * hl * head_dim * es;
     }
     void* layer_pool(int l) const { return static_cast<char*>(pool) + static_cast<size_t>(l) * layer_bytes(); }
+    size_t gath_half_bytes() const {
+        return static_cast<size_t>(cfg.max_batch) * tp * hl * head_dim * es;
+    }
 
     void bind_tensors(const std::vector<size_t>& off) {
         auto at = [&](size_t i) { return static_cast<const void*>(static_cast<char*>(weights) + off[i]); };
@@ -375,7 +381,7 @@ struct Engine {
         act(&d_x, D, "malloc ln out");
         act(&d_qkv, 3 * static_cast<size_t>(hl) * head_dim, "malloc qkv");
         if (tp > 1) {
-            const size_t gath = static_cast<size_t>(B) * tp * hl * head_dim * es;
+            const size_t gath = 2 * gath_half_bytes();
             cuda_ok(cudaMalloc(&d_gath, gath), "malloc gathered attention output");
             cuda_ok(cudaMemsetAsync(d_gath, 0, gath, stream), "memset gathered attention output");
             const size_t nflags = static_cast<size_t>(shape.n_layer) * tp;
@@ -383,7 +389,7 @@ struct Engine {
             cuda_ok(cudaMemsetAsync(d_flags, 0, nflags * 4, stream), "memset barrier flags");
             cuda_ok(cudaMalloc(&d_epoch, 4), "malloc epoch");
             cuda_ok(cudaMemsetAsync(d_epoch, 0, 4, stream), "memset epoch");
-            cuda_ok(cudaMalloc(&d_peer_outs, tp * sizeof(void*)), "malloc peer table");
+            cuda_ok(cudaMalloc(&d_peer_outs, 2 * tp * sizeof(void*)), "malloc peer table");
             cuda_ok(cudaMalloc(&d_peer_flags, tp * sizeof(void*)), "malloc peer table");
         }
         act(&d_attn, D, "malloc attention out");
@@ -470,12 +476,18 @@ struct Engine {
             b2_ok(b2_kv_append(&ka, s), "kv_append");
             B2PagedAttnArgs aa = attn_args(bucket, l);
             aa.q_bias = qkv_b;
+            // Past layer 0, seq_lens_post, the block tables, q and every key row
+            // but the newest were complete before kv_append started.
+            if (l > 0) aa.flags = B2_ATTN_NEWEST_ROW_PENDING;
             if (tp > 1) {
                 // all-gather in the attention epilogue, then meet the peers
-                B2OutputGather g{d_peer_outs, tp, static_cast<int64_t>(tp) * QD, static_cast<int64_t>(tp_rank) * QD};
+                const int par = l & 1;  // gathered-buffer half of this layer
+                B2OutputGather g{d_peer_outs + par * tp, tp, static_cast<int64_t>(tp) * QD,
+                                 static_cast<int64_t>(tp_rank) * QD};
                 b2_ok(b2_paged_attention_gather(&aa, attn_ws, attn_ws_bytes, &g, s), "paged_attention_gather");
                 b2_ok(b2_tp_barrier(d_flags, d_peer_flags, tp_rank, tp, d_epoch, l, s), "tp_barrier");
-                gemm(bucket, tp * QD, D, d_gath, proj_w_pad[static_cast<size_t>(l)], d_attn_out);
+                gemm(bucket, tp * QD, D, static_cast<char*>(d_gath) + par * gath_half_bytes(),
+                     proj_w_pad[static_cast<size_t>(l)], d_attn_out);
             } else {
                 b2_ok(b2_paged_attention(&aa, attn_ws, attn_ws_bytes, s), "paged_attention");
                 gemm(bucket, D, D, d_attn, w.proj_w, d_attn_out);
@@ -1034,11 +1046,12 @@ int b2_engine_tp_connect(b2_engine* eng, const void* handles) {
         if (eng->tp <= 1) throw Error(B2_ERR_SHAPE, "not a head-sharded engine");
         if (eng->tp_connected) throw Error(B2_ERR_SHAPE, "already connected");
         b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
-        std::vector<void*> outs(static_cast<size_t>(eng->tp)), flags(static_cast<size_t>(eng->tp));
+        std::vector<void*> outs(2 * static_cast<size_t>(eng->tp)), flags(static_cast<size_t>(eng->tp));
         const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
         for (int p = 0; p < eng->tp; ++p) {
             if (p == eng->tp_rank) {
                 outs[p] = eng->d_gath;
+                outs[eng->tp + p] = static_cast<char*>(eng->d_gath) + eng->gath_half_bytes();
                 flags[p] = eng->d_flags;
                 continue;
             }
@@ -1051,6 +1064,7 @@ int b2_engine_tp_connect(b2_engine* eng, const void* handles) {
                              "cudaIpcOpenMemHandle (peer flags)");
             eng->peer_mapped.push_back(f);
             outs[p] = o;
+            outs[eng->tp + p] = static_cast<char*>(o) + eng->gath_half_bytes();
             flags[p] = f;
         }
         b2::eng::cuda_ok(cudaMemcpy(eng->d_peer_outs, outs.data(), outs.size() * sizeof(void*), cudaMemcpyHostToDevice),

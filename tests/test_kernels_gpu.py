@@ -376,3 +376,51 @@ def test_reference_kernel_kats(b2, cuda, golden):
     b2.argmax(toks, logits)
     torch.cuda.synchronize()
     assert toks.cpu().numpy().tolist() == a["expected"]
+
+
+@pytest.mark.parametrize("dt", [O.F16, O.BF16])
+def test_attention_early_start_after_kv_append(b2, cuda, dt):
+    """kv_append writes each sequence's newest row, then attention runs right
+    behind it with B2_ATTN_NEWEST_ROW_PENDING (it may start before kv_append
+    finishes and must still read the new rows); and with B2_ATTN_INPUTS_READY
+    on inputs written long before.  Both against the oracle over the appended
+    pool, several rounds."""
+    torch = _torch()
+    rng = np.random.Generator(np.random.PCG64(77))
+    H, Dh, L, layer = 12, 64, 2, 1
+    ctx_pre = rng.integers(0, 700, size=48).astype(np.int32)
+    pool, bt, mbps, nb = make_paged(rng, dt, (ctx_pre + 1).tolist(), H, Dh, L)
+    B = len(ctx_pre)
+    stride = 3 * H * Dh
+    qkv = O.round_to(dt, rng.standard_normal(B * stride, dtype=np.float32)).reshape(B, stride)
+    ref_pool = pool.copy()
+    kpad = np.zeros_like(qkv)
+    vpad = np.zeros_like(qkv)
+    kpad[:, : 2 * H * Dh] = qkv[:, H * Dh:]
+    vpad[:, : H * Dh] = qkv[:, 2 * H * Dh:]
+    O.kv_append(dt, ref_pool, kpad, vpad, stride, bt, ctx_pre, n_kv_head=H, head_dim=Dh, max_blocks_per_seq=mbps,
+                layer_idx=layer, n_layer=L, num_blocks=nb)
+    post = (ctx_pre + 1).tolist()
+    ref = O.paged_attention(dt, qkv.ravel(), stride, ref_pool, np.where(bt < 0, 0, bt), post, n_head=H, n_kv_head=H,
+                            head_dim=Dh, max_blocks_per_seq=mbps, layer_idx=layer, n_layer=L, nthreads=8)
+    qkvd = to_dev(dt, qkv.ravel()).view(B, stride)
+    btd, pre_d = ints_dev(bt), ints_dev(ctx_pre)
+    post_d = torch.zeros(B, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, H, Dh, dtype=torch.float32, device="cuda")
+    for flags in (b2.ATTN_NEWEST_ROW_PENDING, b2.ATTN_INPUTS_READY):
+        pd = to_dev(dt, pool)  # fresh pool without the new rows
+        args = b2.attn_args(qkvd, stride, pd, btd, post_d, out, n_head=H, n_kv_head=H, head_dim=Dh,
+                            max_blocks_per_seq=mbps, layer_idx=layer, n_layer=L, num_blocks=nb, flags=flags)
+        ws = b2.attention_workspace(args)
+        for _ in range(3):
+            out.fill_(float("nan"))
+            b2.kv_append(pd, qkvd[:, H * Dh:], qkvd[:, 2 * H * Dh:], stride, btd, pre_d, n_kv_head=H, head_dim=Dh,
+                         max_blocks_per_seq=mbps, layer_idx=layer, n_layer=L, num_blocks=nb, seq_lens_post=post_d)
+            if flags == b2.ATTN_INPUTS_READY:
+                torch.cuda.synchronize()  # READY promises nothing is written by the kernel just before
+            b2.paged_attention(args, ws)
+            torch.cuda.synchronize()
+            got = out.cpu().numpy()
+            assert np.isfinite(got).all()
+            assert np.max(np.abs(got - ref)) <= 2e-3
+    assert b2.device_errors() == 0
