@@ -286,6 +286,41 @@ B2_API int b2_argmax(int32_t dtype, int32_t* out_tokens, const void* logits, int
 B2_API int b2_argmax_rows(int32_t dtype, int32_t* out_tokens, const void* logits, int64_t row_stride,
                           int32_t batch, int32_t vocab, b2_stream_t stream);
 
+/* ------------------------------------------------------------------ linear layers
+ * y[b][n] = epilogue(sum_k x[b][k] * w[n][k]) on the tensor cores (tcgen05),
+ * for the decode step's small batches.  Replaces the engine's cuBLAS call
+ * gemm_rowmajor (gpu-engine/src/engine.cu:124-131: row-major Y = X * W^T, W
+ * stored [out][in]) together with the launch that follows it:
+ *   B2_LINEAR_STORE  y = T(x.W^T); with a bias, T(float(T(x.W^T)) + bias) --
+ *                    gemm_rowmajor + kernels::launch_add_bias (kernels.h:35-37)
+ *   B2_LINEAR_GELU   y = T(gelu_tanh(float(T(x.W^T)) + bias)) --
+ *                    gemm_rowmajor + kernels::launch_bias_gelu (kernels.h:46-49)
+ * fp32 accumulation; the sum's order differs from cuBLAS's, so results agree
+ * with it to rounding, not bit for bit.  F16 and BF16 only (B2_ERR_DTYPE for
+ * F32, whose callers keep cuBLAS).  x, w, y: 16-byte aligned; in_features,
+ * x_row_stride and y_row_stride multiples of 8.  The
+ * launch uses programmatic dependent launch: it starts streaming w while the
+ * previous kernel on the stream finishes (w must not be that kernel's
+ * output; x may be). */
+#define B2_LINEAR_STORE 0
+#define B2_LINEAR_GELU 1
+
+typedef struct B2LinearArgs {
+    int32_t dtype;        /* B2_F16 or B2_BF16, for x, w, bias and y */
+    const void* x;        /* [batch][x_row_stride] */
+    int64_t x_row_stride; /* elements */
+    const void* w;        /* [out_features][in_features], row-major */
+    const void* bias;     /* [out_features] or NULL (B2_LINEAR_GELU: NULL = no bias) */
+    void* y;              /* [batch][y_row_stride] */
+    int64_t y_row_stride; /* elements, >= out_features */
+    int32_t batch;        /* 1 .. 65535 * 256 */
+    int32_t in_features;
+    int32_t out_features;
+    int32_t epilogue;     /* B2_LINEAR_* */
+} B2LinearArgs;
+
+B2_API int b2_linear(const B2LinearArgs* args, b2_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

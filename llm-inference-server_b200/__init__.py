@@ -24,6 +24,7 @@ BLOCK_TOKENS = 16
 
 B2_OK = 0
 ATTN_INPUTS_READY, ATTN_NEWEST_ROW_PENDING = 1, 2  # B2PagedAttnArgs.flags
+LINEAR_STORE, LINEAR_GELU = 0, 1  # B2LinearArgs.epilogue
 DEVERR_BLOCK_ID, DEVERR_SEQ_LEN, DEVERR_TIMEOUT, DEVERR_TOKEN = 1, 2, 4, 8
 
 # Every symbol include/b2_decode.h declares.
@@ -32,7 +33,7 @@ DECODE_SYMBOLS = (
     "b2_paged_attention_workspace_bytes", "b2_paged_attention",
     "b2_add_layernorm", "b2_bias_gelu", "b2_add_bias", "b2_add_one", "b2_embedding", "b2_argmax",
     "b2_paged_attention_noalloc", "b2_argmax_rows", "b2_paged_attention_gather", "b2_tp_barrier",
-    "b2_tp_epoch_bump",
+    "b2_tp_epoch_bump", "b2_linear",
 )
 
 _c_int, _c_float, _vp = ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
@@ -52,6 +53,12 @@ class PagedAttnArgs(ctypes.Structure):
                 ("n_head", _c_int), ("n_kv_head", _c_int), ("head_dim", _c_int), ("max_blocks_per_seq", _c_int),
                 ("layer_idx", _c_int), ("n_layer", _c_int), ("num_blocks", _c_int), ("scale", _c_float),
                 ("flags", _c_int)]
+
+
+class LinearArgs(ctypes.Structure):
+    _fields_ = [("dtype", _c_int), ("x", _vp), ("x_row_stride", ctypes.c_int64), ("w", _vp), ("bias", _vp),
+                ("y", _vp), ("y_row_stride", ctypes.c_int64), ("batch", _c_int), ("in_features", _c_int),
+                ("out_features", _c_int), ("epilogue", _c_int)]
 
 
 class B2Error(RuntimeError):
@@ -90,6 +97,7 @@ def load() -> ctypes.CDLL:
     lib.b2_embedding.argtypes = [_c_int, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp]
     lib.b2_argmax.argtypes = [_c_int, _vp, _vp, _c_int, _c_int, _vp]
     lib.b2_argmax_rows.argtypes = [_c_int, _vp, _vp, ctypes.c_int64, _c_int, _c_int, _vp]
+    lib.b2_linear.argtypes = [ctypes.POINTER(LinearArgs), _vp]
     _lib = lib
     return lib
 
@@ -196,3 +204,13 @@ def argmax(out_tokens, logits, stream=None, vocab=None):
     else:
         _check(load().b2_argmax_rows(dtype_code(logits.dtype), _ptr(out_tokens), _ptr(logits), logits.stride(0), b,
                                      vocab, _stream(stream)))
+
+
+def linear(y, x, w, bias=None, epilogue=LINEAR_STORE, stream=None):
+    """y = epilogue(x @ w.T) on the tensor cores (b2_linear): x [batch, in],
+    w [out, in] contiguous, y [batch, out] (x and y rows may be strided)."""
+    if not w.is_contiguous() or x.stride(1) != 1 or y.stride(1) != 1:
+        raise ValueError("w must be contiguous and x, y must have unit column stride")
+    a = LinearArgs(dtype_code(w.dtype), _ptr(x), x.stride(0), _ptr(w), _ptr(bias), _ptr(y), y.stride(0), x.shape[0],
+                   w.shape[1], w.shape[0], epilogue)
+    _check(load().b2_linear(ctypes.byref(a), _stream(stream)))

@@ -140,11 +140,6 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* 
     return warp_sums[warp] + incl - v;
 }
 
-__device__ __forceinline__ void pdl_launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 // Merges the partials (m, l, acc) of sequence b -- slots (i0 + b) * ks ...
 // (i0 + nseg + b) * ks - 1, one per (CTA, token subgroup) -- with a running
 // maximum and writes out[b] in OutT.  Each (head, E-element chunk) item is

@@ -52,10 +52,9 @@
 // for its own MMAs and copies and frees its TMEM.
 #pragma once
 
-#include <cuda.h>
-
 #include "attention.cuh"
 #include "b2_common.cuh"
+#include "tcgen05.cuh"
 
 namespace b2 {
 
@@ -81,94 +80,6 @@ struct TcParams {
     float* part_acc;
 };
 
-// ---------------------------------------------------------------- PTX glue
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
-                 "r"(ncols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// D[tmem] (+)= A[smem] * B[smem], both described by shared-memory descriptors.
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
-        : "memory");
-}
-
-// Arrives on `bar` once every MMA this thread issued before it has completed.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-                 : "memory");
-}
-
-// 8 consecutive TMEM columns of this warp's 32 lanes (one lane per thread),
-// waited for inside the same statement so no use can precede the wait.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
-    uint32_t r0, r1, r2, r3, r4, r5, r6, r7;
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3), "=r"(r4), "=r"(r5), "=r"(r6), "=r"(r7)
-        : "r"(taddr)
-        : "memory");
-    v[0] = __uint_as_float(r0);
-    v[1] = __uint_as_float(r1);
-    v[2] = __uint_as_float(r2);
-    v[3] = __uint_as_float(r3);
-    v[4] = __uint_as_float(r4);
-    v[5] = __uint_as_float(r5);
-    v[6] = __uint_as_float(r6);
-    v[7] = __uint_as_float(r7);
-}
-__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
-    uint32_t r0, r1, r2, r3;
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-        : "r"(taddr)
-        : "memory");
-    v[0] = __uint_as_float(r0);
-    v[1] = __uint_as_float(r1);
-    v[2] = __uint_as_float(r2);
-    v[3] = __uint_as_float(r3);
-}
-__device__ __forceinline__ void tmem_ld2(uint32_t taddr, float* v) {
-    uint32_t r0, r1;
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r0), "=r"(r1)
-        : "r"(taddr)
-        : "memory");
-    v[0] = __uint_as_float(r0);
-    v[1] = __uint_as_float(r1);
-}
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
-        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
 // Barriers of the 128 softmax threads (ids 1..7; 0 is __syncthreads).  bar.red
 // is warp-aligned, so the warp is reconverged first (thread 0 runs extra
 // issuer code between barriers).
@@ -179,47 +90,6 @@ __device__ __forceinline__ bool tc_sync_or(int id, bool pred) {
 __device__ __forceinline__ void tc_sync(int id) {
     __syncwarp();
     named_sync(id, kTcConsumers);
-}
-
-// 4-D tiled TMA load into this CTA's own shared memory, completing on `bar`.
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
-        : "memory");
-}
-
-// Shared-memory matrix descriptor, SWIZZLE_128B layout (sm_100 format:
-// start >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride byte
-// offset >> 4 in 32-45, version 1 in 46-47, layout type 2 in 61-63).
-//   K-major operand: rows of 128 B (64 elements), 8-row groups 1024 B apart
-//     (SBO); the leading offset is unused (1).  One MMA (K = 16) reads 32 B
-//     of every row: advance the start by 32 B per K step.
-//   MN-major operand: 128-B rows run along M; 8 K-rows form a 1024-B atom
-//     (SBO = next 8 K-rows), LBO = next 64 elements of M.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
-           (static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16) |
-           (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
-}
-
-// Instruction descriptor of kind::f16 with fp32 accumulation: D format F32
-// (bits 4-5 = 1), A/B format F16 (0) or BF16 (1) in bits 7-9 / 10-12, A/B
-// major in bits 15 / 16 (1 = MN-major), N >> 3 in bits 17-22, M >> 4 in 24-28.
-template <typename T>
-__host__ __device__ constexpr uint32_t umma_idesc(int M, int N, bool a_mn, bool b_mn) {
-    return (1u << 4) | ((Elem<T>::kIsBf16 ? 1u : 0u) << 7) | ((Elem<T>::kIsBf16 ? 1u : 0u) << 10) |
-           ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
-           (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-// Byte offset of element (row, col) (col < 64) in a 128-B-row SWIZZLE_128B
-// tile whose base is 1024-B aligned: 16-B chunk index XOR (row % 8).
-__device__ __forceinline__ uint32_t sw128_offset(int row, int col, int es) {
-    const int byte = col * es;
-    return static_cast<uint32_t>(row * 128 + ((((byte >> 4) ^ row) & 7) << 4) + (byte & 15));
 }
 
 // Shared-memory plan shared by host and device (bytes from the 1024-aligned

@@ -310,4 +310,14 @@ __device__ __forceinline__ uint4 ld_shared16(const void* p) { return *reinterpre
 // consistent fence __threadfence() issues).
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// Programmatic dependent launch.  launch_dependents lets the next kernel on
+// the stream start its prologue; pdl_wait blocks until the previous kernel
+// has completed and its writes are visible (a no-op when the launch had no
+// programmatic dependency).  A kernel reads nothing the previous one writes,
+// and writes nothing it reads, before its pdl_wait.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace b2

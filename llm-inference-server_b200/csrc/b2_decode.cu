@@ -9,18 +9,22 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 
 #include "append.cuh"
 #include "attention.cuh"
 #include "attention_tc.cuh"
 #include "b2_common.cuh"
+#include "linear_tc.cuh"
 #include "rows.cuh"
 #include "tp.cuh"
 
@@ -822,3 +826,221 @@ int b2_argmax(int32_t dtype, int32_t* out_tokens, const void* logits, int32_t ba
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ linear layers
+namespace b2 {
+namespace {
+
+struct LinPlan {
+    int split = 1;    // CTAs per cluster, splitting K
+    int n_tiles = 0;  // 128-feature tiles
+    int chunks = 0;   // batch chunks of bn rows
+    int bn = 16;
+    int kb_total = 0;
+    int stages = 1;
+    int smem = 0;
+};
+
+// Clusters of `split` CTAs of `kern` (smem bytes each) the device holds at
+// once; cached per (kernel, device, split, smem).
+int linear_max_clusters(const void* kern, int dev, int split, int smem, int* out) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, int, int>, int> cache;
+    const auto key = std::make_tuple(kern, dev, split, smem);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            *out = it->second;
+            return B2_OK;
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(split));
+    cfg.blockDim = dim3(kLinThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(split);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        g_last_error = cudaGetErrorString(e);
+        return static_cast<int>(e);
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = n;
+    *out = n;
+    return B2_OK;
+}
+
+// Grid = split x n_tiles x chunks: `split` CTAs (one cluster) share each
+// 128-feature tile and split its K range, so narrow layers still spread their
+// weight stream over the GPU.
+int plan_linear(const B2LinearArgs* a, const void* kern, LinPlan* pl) {
+    int dev = -1;
+    const DeviceInfo di = device_info(&dev);
+    if (dev < 0 || di.sms <= 0) return fail(B2_ERR_DEVICE, "no current CUDA device");
+    pl->chunks = (a->batch + kLinMaxCols - 1) / kLinMaxCols;
+    const int per = (a->batch + pl->chunks - 1) / pl->chunks;
+    pl->bn = (std::max(per, 16) + 15) / 16 * 16;
+    pl->kb_total = (a->in_features + kLinKBlock - 1) / kLinKBlock;
+    pl->n_tiles = (a->out_features + kLinRows - 1) / kLinRows;
+    if (pl->n_tiles > 65535 || pl->chunks > 65535) return fail(B2_ERR_SHAPE, "out_features or batch too large");
+    // The split doubles while the grid is still smaller than the SM count and
+    // all its clusters fit on the device at once (one wave: the cluster
+    // scheduler places a cluster's CTAs on distinct SMs of one GPC, so the
+    // number of resident clusters drops as they grow).
+    const long long tiles = static_cast<long long>(pl->n_tiles) * pl->chunks;
+    bool have = false;
+    for (int split = 1; split <= kLinMaxSplit && split <= pl->kb_total; split *= 2) {
+        if (split > 1 && tiles * (split / 2) >= di.sms) break;
+        const int max_kb = (pl->kb_total + split - 1) / split;
+        int stages = std::min(max_kb, 6);
+        while (stages > 1 && LinLayout::bytes(pl->bn, stages, split) > di.max_smem_optin) --stages;
+        int smem = LinLayout::bytes(pl->bn, stages, split);
+        // The CTAs one SM can hold must fit in its 512 TMEM columns together:
+        // a CTA left waiting in tcgen05.alloc while the CTAs holding the
+        // columns wait for it at a cluster barrier would never proceed.
+        // Shared memory bounds the residency (1 KiB of it is reserved per CTA).
+        const int max_res = 512 / static_cast<int>(lin_tmem_cols(pl->bn));
+        smem = std::max(smem, di.smem_per_sm / (max_res + 1) + 1 - 1024);
+        if (smem > di.max_smem_optin) break;
+        if (split > 1) {
+            int fit = 0;
+            const int rc = linear_max_clusters(kern, dev, split, smem, &fit);
+            if (rc != B2_OK) return rc;
+            if (tiles > fit) break;
+        }
+        pl->split = split;
+        pl->stages = stages;
+        pl->smem = smem;
+        have = true;
+    }
+    if (!have) return fail(B2_ERR_UNSUPPORTED, "linear: tile does not fit in shared memory");
+    return B2_OK;
+}
+
+// Row-major [rows][inner] matrix (row stride `ld` elements) as a 2-D tensor
+// map with boxes of box_rows x 64 elements, 128-byte swizzled.  Boxes that
+// reach past the matrix read zeros.
+int encode_rows_map(CUtensorMap* map, int dtype, const void* base, long long inner, long long rows, long long ld,
+                    int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr) return fail(B2_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kLinKBlock), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, dtype == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(B2_ERR_DEVICE, "cuTensorMapEncodeTiled rejected a linear-layer operand");
+    return B2_OK;
+}
+
+// The output [batch][out_features] (row stride ld elements) as a 2-D tensor
+// map for TMA stores of box_cols x box_rows tiles, unswizzled (the staged tile
+// is row-major); parts of a box outside the matrix are not written.
+int encode_out_map(CUtensorMap* map, int dtype, void* base, long long cols, long long rows, long long ld, int box_cols,
+                   int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr) return fail(B2_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, dtype == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(B2_ERR_DEVICE, "cuTensorMapEncodeTiled rejected the linear-layer output");
+    return B2_OK;
+}
+
+// Plans, encodes the operand maps and launches one instantiation.
+template <typename T, int EPI, bool BIAS>
+int linear_t(const B2LinearArgs* a, cudaStream_t stream) {
+    auto kern = linear_tc_kernel<T, EPI, BIAS>;
+    static std::atomic<uint64_t> smem_set{0};
+    int dev = -1;
+    const DeviceInfo di = device_info(&dev);
+    int rc = ensure_max_smem(kern, smem_set, dev, di.max_smem_optin);
+    if (rc != B2_OK) return rc;
+    LinPlan pl;
+    rc = plan_linear(a, reinterpret_cast<const void*>(kern), &pl);
+    if (rc != B2_OK) return rc;
+    CUtensorMap wm, xm, ym;
+    rc = encode_rows_map(&wm, a->dtype, a->w, a->in_features, a->out_features, a->in_features, kLinRows);
+    if (rc != B2_OK) return rc;
+    rc = encode_rows_map(&xm, a->dtype, a->x, a->in_features, a->batch, a->x_row_stride, pl.bn);
+    if (rc != B2_OK) return rc;
+    rc = encode_out_map(&ym, a->dtype, a->y, a->out_features, a->batch, a->y_row_stride, kLinRows / pl.split, pl.bn);
+    if (rc != B2_OK) return rc;
+    LinParams lp;
+    lp.bias = a->bias;
+    lp.y = a->y;
+    lp.ldy = a->y_row_stride;
+    lp.batch = a->batch;
+    lp.n_out = a->out_features;
+    lp.bn = pl.bn;
+    lp.kb_total = pl.kb_total;
+    lp.stages = pl.stages;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(pl.split), static_cast<unsigned>(pl.n_tiles),
+                       static_cast<unsigned>(pl.chunks));
+    cfg.blockDim = dim3(kLinThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(pl.smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(pl.split);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pl.split > 1 ? 2 : 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, lp, wm, xm, ym);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        g_last_error = cudaGetErrorString(e);
+        return static_cast<int>(e);
+    }
+    return launch_status();
+}
+
+template <typename T>
+int linear_epi(const B2LinearArgs* a, cudaStream_t s) {
+    const bool bias = a->bias != nullptr;
+    if (a->epilogue == B2_LINEAR_GELU)
+        return bias ? linear_t<T, B2_LINEAR_GELU, true>(a, s) : linear_t<T, B2_LINEAR_GELU, false>(a, s);
+    return bias ? linear_t<T, B2_LINEAR_STORE, true>(a, s) : linear_t<T, B2_LINEAR_STORE, false>(a, s);
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" int b2_linear(const B2LinearArgs* a, b2_stream_t stream) {
+    using namespace b2;
+    if (a == nullptr) return fail(B2_ERR_NULL, "args is NULL");
+    if (a->dtype != B2_F16 && a->dtype != B2_BF16)
+        return fail(B2_ERR_DTYPE, "b2_linear runs F16 and BF16 on the tensor cores (F32 callers keep cuBLAS)");
+    if (a->epilogue != B2_LINEAR_STORE && a->epilogue != B2_LINEAR_GELU) return fail(B2_ERR_SHAPE, "unknown epilogue");
+    if (a->batch < 0 || a->in_features <= 0 || a->out_features <= 0) return fail(B2_ERR_SHAPE, "bad sizes");
+    if (a->batch == 0) return B2_OK;
+    if (!a->x || !a->w || !a->y) return fail(B2_ERR_NULL, "x, w and y are required");
+    if (a->x_row_stride < a->in_features || a->y_row_stride < a->out_features)
+        return fail(B2_ERR_SHAPE, "row strides must cover in_features / out_features");
+    if (a->in_features % 8 != 0 || a->x_row_stride % 8 != 0 || a->y_row_stride % 8 != 0 || !aligned16(a->x) ||
+        !aligned16(a->w) || !aligned16(a->y))
+        return fail(B2_ERR_ALIGN,
+                    "x, w and y must be 16-byte aligned with in_features, x_row_stride and y_row_stride multiples of 8");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return a->dtype == B2_F16 ? linear_epi<__half>(a, s) : linear_epi<__nv_bfloat16>(a, s);
+}
