@@ -594,6 +594,37 @@ def run_serve(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_prefill(args, rank: int, world: int) -> None:
+    """Prompt tokens/s of b2_engine_prefill (prefill_bench.py), rank 0."""
+    if rank != 0:
+        return
+    import torch
+    import_package()
+    from lis_b200 import prefill_bench as PB
+    torch.cuda.set_device(0)
+    n_prompts, prompt_len = args.batch or 8, 512
+    with ClockSampler(0) as clk:
+        r = PB.run(n_prompts, prompt_len, steps=args.steps or 5, warmup=args.warmup or 3)
+    tc, rows = r["tensor_cores"], r["decode_rows"]
+    line = {
+        "metric": "GPT-2 medium prefill prompt tok/s", "value": tc["prompt_tok_s"], "unit": "tok/s", "n_gpus": 1,
+        "steps": r["steps"], "warmup": r["warmup"], "ms_per_step": tc["ms_per_call"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"b2_engine_prefill of {n_prompts} prompts x {prompt_len} uniform random tokens, "
+                               "GPT-2 medium shape (24 layers, 16 heads, d_model 1024), fp16, weights N(0,0.02)",
+                   "attention": "b2_prefill_attention (tcgen05, 128-row query tiles)"},
+        "decode_rows": rows,
+        "speedup_vs_decode_rows": round(tc["prompt_tok_s"] / rows["prompt_tok_s"], 2),
+        "roofline": None, "roofline_note": "whole-model prefill call: GEMM-dominated; the attention kernel's "
+                                           "tensor-pipe use is in profiles/prefill_attention_tc.md",
+        "cpu_baseline": None,
+        "e2e": {"value": tc["prompt_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+                "path": "already end to end: each step is one blocking b2_engine_prefill call"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -602,7 +633,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + list(ENGINE_NAMES) + ["serve-medium"], default="mha",
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + list(ENGINE_NAMES) + ["serve-medium", "prefill-medium"],
+                    default="mha",
                     help="mha: the headline microbench; gqa: grouped-query long contexts (tensor-core kernel); "
                          "gpt2-xl / gpt2-medium: GPT-2 decode tokens/s through the engine")
     ap.add_argument("--sets", type=int, default=None, help="rotating input sets (profiling uses fewer)")
@@ -618,6 +650,12 @@ def main() -> None:
             print(json.dumps({"impl": "reference", "unavailable": "the serving trace has no CPU arm"}), flush=True)
             return
         run_serve(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
+        return
+    if args.workload == "prefill-medium":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no batched prefill"}), flush=True)
+            return
+        run_prefill(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         return
     if args.steps is None:
         args.steps = 20 if engine else 5000

@@ -286,6 +286,47 @@ B2_API int b2_argmax(int32_t dtype, int32_t* out_tokens, const void* logits, int
 B2_API int b2_argmax_rows(int32_t dtype, int32_t* out_tokens, const void* logits, int64_t row_stride,
                           int32_t batch, int32_t vocab, b2_stream_t stream);
 
+/* ------------------------------------------------------------------ prefill attention
+ * Causal attention of a prefill call's new rows over the paged KV cache, on
+ * the tensor cores (tcgen05), head_dim 64.  No reference counterpart: the
+ * reference prefills by walking each prompt token through Engine::decode_step
+ * at batch 1 (cpp-engine/src/gpu_engine_generator.cpp:28-42), i.e. through
+ * kernels::launch_paged_attention (kernels.h:67-87) once per prompt row.  For
+ * sequence b of the call, rows q_start[b] .. q_start[b] + q_len[b] - 1 of q and
+ * out are its new tokens at positions seq_lens_pre[b] + i; row i attends the
+ * keys at positions [0, seq_lens_pre[b] + i], which must already be in the pool
+ * (b2_kv_append of the same rows first).  Per row this is exactly what
+ * b2_paged_attention computes with seq_lens = position + 1; here each 128-row
+ * query tile reads its keys once.  q_bias (optional) is added to q first and
+ * rounded to the dtype, like b2_paged_attention.  F16 / BF16 only; 16-byte
+ * aligned pointers, row strides multiples of 8 elements.  Each launch is
+ * self-contained (no workspace).  Programmatic dependent launch as above. */
+typedef struct B2PrefillAttnArgs {
+    int32_t dtype;               /* B2_F16 or B2_BF16: q, pool and out */
+    const void* q;               /* [rows][q_row_stride]; head h at columns h * head_dim */
+    int32_t q_row_stride;
+    const void* q_bias;          /* optional [n_head * head_dim] */
+    const void* kv_pool;
+    const int32_t* block_tables; /* [n_seqs, max_blocks_per_seq] */
+    const int32_t* seq_lens_pre; /* [n_seqs] keys cached before this call's rows */
+    const int32_t* q_start;      /* [n_seqs] first row of each sequence in q and out */
+    const int32_t* q_len;        /* [n_seqs] new rows of each sequence */
+    void* out;                   /* [rows][out_row_stride], packed [n_head][head_dim] per row */
+    int32_t out_row_stride;
+    int32_t n_seqs;
+    int32_t n_head;
+    int32_t n_kv_head;
+    int32_t head_dim;            /* 64 */
+    int32_t max_blocks_per_seq;
+    int32_t layer_idx;
+    int32_t n_layer;
+    int32_t num_blocks;
+    int32_t max_q_len;           /* >= every q_len[b]: sizes the grid */
+    float scale;                 /* 0 selects 1/sqrt(head_dim) */
+} B2PrefillAttnArgs;
+
+B2_API int b2_prefill_attention(const B2PrefillAttnArgs* args, b2_stream_t stream);
+
 /* ------------------------------------------------------------------ linear layers
  * y[b][n] = epilogue(sum_k x[b][k] * w[n][k]) on the tensor cores (tcgen05),
  * for the decode step's small batches.  Replaces the engine's cuBLAS call

@@ -98,8 +98,15 @@ B2_API int b2_engine_decode_step(b2_engine* eng, const int32_t* seq_ids, int32_t
  * continue with decode_step.  Every listed sequence must still be inside its
  * prompt; the call's prompt tokens may not exceed cfg.max_prefill_tokens.
  * Blocks are taken for all prompt positions up front (B2_ERR_POOL if they do
- * not fit, with nothing changed).  Not available on head-sharded engines. */
+ * not fit, with nothing changed).  Not available on head-sharded engines.
+ * The attention of f16 / bf16 models of head_dim 64 runs as 128-row query
+ * tiles on the tensor cores (b2_prefill_attention); f32 models and the switch
+ * below use one decode-attention row per prompt token. */
 B2_API int b2_engine_prefill(b2_engine* eng, const int32_t* seq_ids, int32_t n, int32_t* out_next_tokens);
+
+/* Prefill attention on the tensor cores (default on; takes effect for f16 /
+ * bf16 models of head_dim 64).  0 selects the decode-attention rows instead. */
+B2_API int b2_engine_set_prefill_tensor_cores(b2_engine* eng, int32_t enabled);
 
 /* Engine::free_sequence: returns the sequence's blocks; unknown ids are ignored. */
 B2_API int b2_engine_free_sequence(b2_engine* eng, int32_t seq_id);

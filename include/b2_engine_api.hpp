@@ -75,6 +75,8 @@ public:
     size_t free_blocks() const { return static_cast<size_t>(b2_engine_free_blocks(eng_)); }
 
     void set_use_cuda_graphs(bool enabled) { b2_engine_set_use_cuda_graphs(handle(), enabled ? 1 : 0); }
+    // Prefill attention on the tensor cores (default) or as decode-attention rows.
+    void set_prefill_tensor_cores(bool enabled) { b2_engine_set_prefill_tensor_cores(handle(), enabled ? 1 : 0); }
 
     // Text of the failure behind the last false / exception (no reference counterpart).
     static std::string last_error() { return b2_engine_last_error(); }

@@ -33,7 +33,7 @@ DECODE_SYMBOLS = (
     "b2_paged_attention_workspace_bytes", "b2_paged_attention",
     "b2_add_layernorm", "b2_bias_gelu", "b2_add_bias", "b2_add_one", "b2_embedding", "b2_argmax",
     "b2_paged_attention_noalloc", "b2_argmax_rows", "b2_paged_attention_gather", "b2_tp_barrier",
-    "b2_tp_epoch_bump", "b2_linear",
+    "b2_tp_epoch_bump", "b2_linear", "b2_prefill_attention",
 )
 
 _c_int, _c_float, _vp = ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
@@ -59,6 +59,14 @@ class LinearArgs(ctypes.Structure):
     _fields_ = [("dtype", _c_int), ("x", _vp), ("x_row_stride", ctypes.c_int64), ("w", _vp), ("bias", _vp),
                 ("y", _vp), ("y_row_stride", ctypes.c_int64), ("batch", _c_int), ("in_features", _c_int),
                 ("out_features", _c_int), ("epilogue", _c_int)]
+
+
+class PrefillAttnArgs(ctypes.Structure):
+    _fields_ = [("dtype", _c_int), ("q", _vp), ("q_row_stride", _c_int), ("q_bias", _vp), ("kv_pool", _vp),
+                ("block_tables", _vp), ("seq_lens_pre", _vp), ("q_start", _vp), ("q_len", _vp), ("out", _vp),
+                ("out_row_stride", _c_int), ("n_seqs", _c_int), ("n_head", _c_int), ("n_kv_head", _c_int),
+                ("head_dim", _c_int), ("max_blocks_per_seq", _c_int), ("layer_idx", _c_int), ("n_layer", _c_int),
+                ("num_blocks", _c_int), ("max_q_len", _c_int), ("scale", _c_float)]
 
 
 class B2Error(RuntimeError):
@@ -98,6 +106,7 @@ def load() -> ctypes.CDLL:
     lib.b2_argmax.argtypes = [_c_int, _vp, _vp, _c_int, _c_int, _vp]
     lib.b2_argmax_rows.argtypes = [_c_int, _vp, _vp, ctypes.c_int64, _c_int, _c_int, _vp]
     lib.b2_linear.argtypes = [ctypes.POINTER(LinearArgs), _vp]
+    lib.b2_prefill_attention.argtypes = [ctypes.POINTER(PrefillAttnArgs), _vp]
     _lib = lib
     return lib
 
@@ -214,3 +223,15 @@ def linear(y, x, w, bias=None, epilogue=LINEAR_STORE, stream=None):
     a = LinearArgs(dtype_code(w.dtype), _ptr(x), x.stride(0), _ptr(w), _ptr(bias), _ptr(y), y.stride(0), x.shape[0],
                    w.shape[1], w.shape[0], epilogue)
     _check(load().b2_linear(ctypes.byref(a), _stream(stream)))
+
+
+def prefill_attention(out, q, q_row_stride, kv_pool, block_tables, seq_lens_pre, q_start, q_len, *, n_head, n_kv_head,
+                      head_dim, max_blocks_per_seq, layer_idx, n_layer, num_blocks, max_q_len, q_bias=None, scale=0.0,
+                      stream=None):
+    """b2_prefill_attention: causal attention of each sequence's new rows over
+    the paged pool (rows q_start[b] .. q_start[b] + q_len[b] - 1 of q / out)."""
+    a = PrefillAttnArgs(dtype_code(kv_pool.dtype), _ptr(q), q_row_stride, _ptr(q_bias), _ptr(kv_pool),
+                        _ptr(block_tables), _ptr(seq_lens_pre), _ptr(q_start), _ptr(q_len), _ptr(out), out.stride(0),
+                        seq_lens_pre.numel(), n_head, n_kv_head, head_dim, max_blocks_per_seq, layer_idx, n_layer,
+                        num_blocks, max_q_len, scale)
+    _check(load().b2_prefill_attention(ctypes.byref(a), _stream(stream)))

@@ -25,6 +25,7 @@
 #include "attention_tc.cuh"
 #include "b2_common.cuh"
 #include "linear_tc.cuh"
+#include "prefill_tc.cuh"
 #include "rows.cuh"
 #include "tp.cuh"
 
@@ -1043,4 +1044,91 @@ extern "C" int b2_linear(const B2LinearArgs* a, b2_stream_t stream) {
                     "x, w and y must be 16-byte aligned with in_features, x_row_stride and y_row_stride multiples of 8");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     return a->dtype == B2_F16 ? linear_epi<__half>(a, s) : linear_epi<__nv_bfloat16>(a, s);
+}
+
+// ------------------------------------------------------------ prefill attention
+namespace b2 {
+namespace {
+
+// The pool as a 4-D tensor for the prefill kernel's boxes: dim 0 head_dim (64,
+// one 128-byte swizzle row), dim 1 the 16 token rows of a slab (stride
+// n_kv_head * head_dim), dim 2 kv head, dim 3 slab ((block * n_layer + layer)
+// * 2 + K|V); box {64, 16, 1, 1} = one head's 16 rows of one slab.
+int encode_prefill_kv_map(const B2PrefillAttnArgs* a, CUtensorMap* map) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (enc == nullptr) return fail(B2_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t es = 2;
+    const cuuint64_t hd = static_cast<cuuint64_t>(a->head_dim), hk = static_cast<cuuint64_t>(a->n_kv_head);
+    const cuuint64_t dims[4] = {hd, 16, hk, static_cast<cuuint64_t>(a->num_blocks) * a->n_layer * 2};
+    const cuuint64_t strides[3] = {hk * hd * es, hd * es, 16 * hk * hd * es};
+    const cuuint32_t box[4] = {64, 16, 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(map, a->dtype == B2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           4, const_cast<void*>(a->kv_pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(B2_ERR_DEVICE, "cuTensorMapEncodeTiled rejected the KV pool layout");
+    return B2_OK;
+}
+
+template <typename T>
+int launch_prefill_t(const B2PrefillAttnArgs* a, const PfParams& pp, const CUtensorMap& map, cudaStream_t stream) {
+    auto kern = prefill_attn_tc_kernel<T>;
+    static std::atomic<uint64_t> smem_set{0};
+    int dev = -1;
+    const DeviceInfo di = device_info(&dev);
+    const int rc = ensure_max_smem(kern, smem_set, dev, di.max_smem_optin);
+    if (rc != B2_OK) return rc;
+    if (PfLayout::bytes > di.max_smem_optin) return fail(B2_ERR_UNSUPPORTED, "prefill attention: shared memory");
+    const dim3 grid(static_cast<unsigned>((a->max_q_len + kPfRows - 1) / kPfRows), static_cast<unsigned>(a->n_head),
+                    static_cast<unsigned>(a->n_seqs));
+    return launch_pdl(kern, grid, dim3(kPfThreads), PfLayout::bytes, stream, pp, map);
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" int b2_prefill_attention(const B2PrefillAttnArgs* a, b2_stream_t stream) {
+    using namespace b2;
+    if (a == nullptr) return fail(B2_ERR_NULL, "args is NULL");
+    if (a->dtype != B2_F16 && a->dtype != B2_BF16) return fail(B2_ERR_DTYPE, "prefill attention runs F16 and BF16");
+    if (a->n_seqs < 0 || a->max_q_len < 0) return fail(B2_ERR_SHAPE, "n_seqs and max_q_len must be >= 0");
+    if (a->n_seqs == 0 || a->max_q_len == 0) return B2_OK;
+    if (!a->q || !a->kv_pool || !a->block_tables || !a->seq_lens_pre || !a->q_start || !a->q_len || !a->out)
+        return fail(B2_ERR_NULL, "q, kv_pool, block_tables, seq_lens_pre, q_start, q_len and out are required");
+    if (a->head_dim != kPfHeadDim) return fail(B2_ERR_UNSUPPORTED, "prefill attention: head_dim must be 64");
+    if (a->n_kv_head <= 0 || a->n_head <= 0 || a->n_head % a->n_kv_head != 0)
+        return fail(B2_ERR_SHAPE, "n_head must be a positive multiple of n_kv_head");
+    if (a->n_seqs > 65535 || a->n_head > 65535) return fail(B2_ERR_SHAPE, "n_seqs and n_head must be <= 65535");
+    if (a->max_blocks_per_seq <= 0 || a->n_layer <= 0 || a->layer_idx < 0 || a->layer_idx >= a->n_layer ||
+        a->num_blocks <= 0 || static_cast<long long>(a->num_blocks) * a->n_layer * 2 >= (1LL << 31) - 1)
+        return fail(B2_ERR_SHAPE, "max_blocks_per_seq, n_layer, layer_idx or num_blocks out of range");
+    if (a->q_row_stride < a->n_head * a->head_dim || a->out_row_stride < a->n_head * a->head_dim)
+        return fail(B2_ERR_SHAPE, "row strides must cover n_head * head_dim");
+    if (!aligned16(a->q) || !aligned16(a->kv_pool) || !aligned16(a->out) || (a->q_bias && !aligned16(a->q_bias)) ||
+        a->q_row_stride % 8 != 0 || a->out_row_stride % 8 != 0)
+        return fail(B2_ERR_ALIGN, "q, q_bias, kv_pool and out must be 16-byte aligned, row strides multiples of 8");
+    CUtensorMap map;
+    int rc = encode_prefill_kv_map(a, &map);
+    if (rc != B2_OK) return rc;
+    PfParams pp;
+    pp.q = a->q;
+    pp.q_row_stride = a->q_row_stride;
+    pp.q_bias = a->q_bias;
+    pp.block_tables = a->block_tables;
+    pp.seq_lens_pre = a->seq_lens_pre;
+    pp.q_start = a->q_start;
+    pp.q_len = a->q_len;
+    pp.out = a->out;
+    pp.out_row_stride = a->out_row_stride;
+    pp.qg = a->n_head / a->n_kv_head;
+    pp.mbps = a->max_blocks_per_seq;
+    pp.layer_idx = a->layer_idx;
+    pp.n_layer = a->n_layer;
+    pp.num_blocks = a->num_blocks;
+    pp.oob_slab = a->num_blocks * a->n_layer * 2;
+    const float scale = a->scale != 0.0f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
+    pp.scale_log2 = scale * 1.4426950408889634f;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return a->dtype == B2_F16 ? launch_prefill_t<__half>(a, pp, map, s) : launch_prefill_t<__nv_bfloat16>(a, pp, map, s);
 }

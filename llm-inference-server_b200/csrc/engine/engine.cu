@@ -198,6 +198,7 @@ struct Engine {
     // [tokens | positions | seq_lens | last rows (max_batch) | tables (cap x mbps)],
     // row activations, and the per-sequence tail (last rows, logits, next tokens).
     int prefill_cap = 0;
+    bool prefill_tc = true;  // b2_engine_set_prefill_tensor_cores
     int32_t *d_pin = nullptr, *h_pin = nullptr, *d_pseq_post = nullptr, *d_pnext = nullptr, *h_pnext = nullptr;
     void *p_resid = nullptr, *p_x = nullptr, *p_qkv = nullptr, *p_attn = nullptr, *p_attn_out = nullptr,
          *p_ff = nullptr, *p_ff_out = nullptr, *p_last = nullptr, *p_logits = nullptr, *p_attn_ws = nullptr;
@@ -535,11 +536,18 @@ struct Engine {
         return b < cfg.max_batch ? b : cfg.max_batch;
     }
 
+    // Prefill attention on the tensor cores (b2_prefill_attention) for 16-bit
+    // models of head_dim 64 unless switched off; otherwise one decode-attention
+    // row per prompt token.
+    bool tc_prefill() const { return prefill_tc && dt != B2_F32 && head_dim == 64; }
+
     void setup_prefill() {
         if (prefill_cap > 0) return;
         const int cap = cfg.max_prefill_tokens > 0 ? cfg.max_prefill_tokens : 2048;
         const int B = cfg.max_batch, D = shape.d_model;
-        const size_t in_ints = 3 * static_cast<size_t>(cap) + B + static_cast<size_t>(cap) * mbps;
+        // [tok|pos|seq_len per row][last row|pre|start|rows per sequence][block table per sequence][per row]
+        const size_t in_ints = 3 * static_cast<size_t>(cap) + 4 * static_cast<size_t>(B) +
+                               static_cast<size_t>(B) * mbps + static_cast<size_t>(cap) * mbps;
         cuda_ok(cudaMalloc(&d_pin, in_ints * 4), "malloc prefill inputs");
         cuda_ok(cudaMallocHost(&h_pin, in_ints * 4), "pinned prefill inputs");
         std::memset(h_pin, 0, in_ints * 4);
@@ -570,7 +578,8 @@ struct Engine {
     // One pass over every remaining prompt token of the listed sequences: the
     // decode step's kernels with one row per token.  Row r of sequence s is
     // position p = seq_len(s) + t; kv_append writes its K/V at p and attention
-    // reads positions [0, p] -- causal prefill from the decode kernels.
+    // reads positions [0, p]: each sequence's rows as 128-row query tiles on the
+    // tensor cores (tc_prefill), or one decode-attention row per token.
     void prefill(const int32_t* ids, int n, int32_t* out) {
         if (tp > 1) throw Error(B2_ERR_UNSUPPORTED, "batched prefill is not available on head-sharded engines");
         if (n <= 0 || n > cfg.max_batch) throw Error(B2_ERR_SHAPE, "n must be in [1, max_batch]");
@@ -595,17 +604,30 @@ struct Engine {
         if (rows > prefill_cap) throw Error(B2_ERR_SHAPE, "more prompt tokens than max_prefill_tokens in one call");
         if (need > blocks->num_free()) throw Error(B2_ERR_POOL, "KV cache block pool exhausted");
         const int cap = prefill_cap, B = cfg.max_batch, D = shape.d_model, V = shape.vocab_size, L = shape.n_layer;
+        const size_t seq_off = 3 * static_cast<size_t>(cap);          // last, pre, start, rows: B each
+        const size_t sbt_off = seq_off + 4 * static_cast<size_t>(B);  // per-sequence block tables
+        const size_t bt_off = sbt_off + static_cast<size_t>(B) * mbps;
         int32_t* tok = h_pin;
         int32_t* pos = h_pin + cap;
         int32_t* sl = h_pin + 2 * cap;
-        int32_t* last = h_pin + 3 * cap;
-        int32_t* bt = h_pin + 3 * cap + B;
-        int r = 0;
+        int32_t* last = h_pin + seq_off;
+        int32_t* s_pre = last + B;
+        int32_t* s_start = last + 2 * B;
+        int32_t* s_rows = last + 3 * B;
+        int32_t* sbt = h_pin + sbt_off;
+        int32_t* bt = h_pin + bt_off;
+        int r = 0, max_t = 0;
         for (int i = 0; i < n; ++i) {
             Seq& q = *sv[static_cast<size_t>(i)];
             const int t = static_cast<int>(q.prompt.size()) - q.prompt_pos;
             while (static_cast<int>(q.table.ids.size()) * B2_BLOCK_TOKENS < q.seq_len + t)
                 q.table.ids.push_back(blocks->allocate());
+            s_pre[i] = q.seq_len;
+            s_start[i] = r;
+            s_rows[i] = t;
+            max_t = std::max(max_t, t);
+            int32_t* srow = sbt + static_cast<size_t>(i) * mbps;
+            for (size_t j = 0; j < q.table.ids.size(); ++j) srow[j] = q.table.ids[j];
             for (int k = 0; k < t; ++k, ++r) {
                 tok[r] = q.prompt[static_cast<size_t>(q.prompt_pos + k)];
                 pos[r] = q.seq_len + k;
@@ -615,13 +637,13 @@ struct Engine {
             }
             last[i] = r - 1;
         }
-        const size_t up = (3 * static_cast<size_t>(cap) + B + static_cast<size_t>(rows) * mbps) * 4;
+        const size_t up = (bt_off + static_cast<size_t>(rows) * mbps) * 4;
         cuda_ok(cudaMemcpyAsync(d_pin, h_pin, up, cudaMemcpyHostToDevice, stream), "upload prefill inputs");
         const int32_t* d_tok = d_pin;
         const int32_t* d_pos = d_pin + cap;
         const int32_t* d_sl = d_pin + 2 * cap;
-        const int32_t* d_last = d_pin + 3 * cap;
-        const int32_t* d_bt = d_pin + 3 * cap + B;
+        const int32_t* d_last = d_pin + seq_off;
+        const int32_t* d_bt = d_pin + bt_off;
         const float eps = shape.layer_norm_epsilon;
         b2_stream_t s = stream;
         const char* qkv = static_cast<const char*>(p_qkv);
@@ -651,13 +673,40 @@ struct Engine {
             ka.n_layer = 1;
             ka.num_blocks = num_blocks;
             b2_ok(b2_kv_append(&ka, s), "kv_append");
-            B2PagedAttnArgs aa = attn_args(rows, l);
-            aa.q = p_qkv;
-            aa.q_bias = w.qkv_b;
-            aa.block_tables = d_bt;
-            aa.seq_lens = d_pseq_post;
-            aa.out = p_attn;
-            b2_ok(b2_paged_attention(&aa, p_attn_ws, p_attn_ws_bytes, s), "paged_attention");
+            if (tc_prefill()) {
+                // causal attention of each sequence's new rows, 128-row query tiles on tcgen05
+                B2PrefillAttnArgs pa{};
+                pa.dtype = dt;
+                pa.q = p_qkv;
+                pa.q_row_stride = 3 * D;
+                pa.q_bias = w.qkv_b;
+                pa.kv_pool = layer_pool(l);
+                pa.block_tables = d_pin + sbt_off;
+                pa.seq_lens_pre = d_pin + seq_off + B;
+                pa.q_start = d_pin + seq_off + 2 * B;
+                pa.q_len = d_pin + seq_off + 3 * B;
+                pa.out = p_attn;
+                pa.out_row_stride = D;
+                pa.n_seqs = n;
+                pa.n_head = shape.n_head;
+                pa.n_kv_head = shape.n_head;
+                pa.head_dim = head_dim;
+                pa.max_blocks_per_seq = mbps;
+                pa.layer_idx = 0;
+                pa.n_layer = 1;
+                pa.num_blocks = num_blocks;
+                pa.max_q_len = max_t;
+                b2_ok(b2_prefill_attention(&pa, s), "prefill_attention");
+            } else {
+                // one decode row per prompt token: row r reads keys [0, position]
+                B2PagedAttnArgs aa = attn_args(rows, l);
+                aa.q = p_qkv;
+                aa.q_bias = w.qkv_b;
+                aa.block_tables = d_bt;
+                aa.seq_lens = d_pseq_post;
+                aa.out = p_attn;
+                b2_ok(b2_paged_attention(&aa, p_attn_ws, p_attn_ws_bytes, s), "paged_attention");
+            }
             gemm(rows, D, D, p_attn, w.proj_w, p_attn_out);
             b2_ok(b2_add_layernorm(dt, p_x, p_resid, p_attn_out, w.proj_b, p_resid, w.ln2_g, w.ln2_b, rows, D, eps, s),
                   "ln2");
@@ -1012,6 +1061,12 @@ int64_t b2_engine_free_blocks(const b2_engine* eng) { return eng ? eng->blocks->
 int b2_engine_set_use_cuda_graphs(b2_engine* eng, int32_t enabled) {
     if (!eng) return B2_ERR_NULL;
     eng->use_graphs = enabled != 0;
+    return B2_OK;
+}
+
+int b2_engine_set_prefill_tensor_cores(b2_engine* eng, int32_t enabled) {
+    if (!eng) return B2_ERR_NULL;
+    eng->prefill_tc = enabled != 0;
     return B2_OK;
 }
 

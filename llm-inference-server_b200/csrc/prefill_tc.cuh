@@ -1,0 +1,366 @@
+// prefill_tc.cuh -- causal prefill attention over the paged KV cache on the
+// 5th-generation tensor cores (tcgen05 + TMEM + TMA), head_dim 64.
+//
+// The reference has no prefill kernel: GpuEngineGenerator walks every prompt
+// token through Engine::decode_step at batch 1
+// (cpp-engine/src/gpu_engine_generator.cpp:28-42), so each prompt row reads
+// the whole key prefix again.  Here the new rows of a sequence are query
+// tiles: row i of sequence b (position seq_lens_pre[b] + i) attends the keys
+// at positions [0, seq_lens_pre[b] + i] -- the result the reference's decode
+// attention (gpu-engine/src/kernels/attention.cu:49-127, cpu_model.cpp:131-162)
+// gives that row, with every key tile read once per 128 query rows.
+//
+// One CTA per (128-row query tile, query head, sequence):
+//   Q tile [128 rows][64]             smem, SWIZZLE_128B K-major (threads, + bias)
+//   K, V tiles [128 keys][64]         8 paged blocks x one 16-row TMA box each
+//   S = Q . K^T      M=128 N=128 K=64  fp32 in TMEM columns [0, 128)
+//   O += P . V       M=128 N=64  K=128 fp32 in TMEM columns [128, 192)
+// P is written by the softmax threads as two 16-bit halves hi = T(p) and
+// lo = T(p - hi) and both are multiplied in (16 significant bits per weight).
+// Softmax in log2 units with a lazily moved reference maximum (moves only when
+// a tile's row maximum exceeds it by more than 8, so weights stay <= 2^8 and
+// O is rescaled only then).  Causality comes from positions: key k counts for
+// query row i iff k <= seq_lens_pre + i.  Key boxes past the last needed block
+// are fetched at an out-of-range slab (TMA fills zeros); rows of the last block
+// past the keys in use are zeroed before the PV product, so stale values there
+// (never written) cannot reach the output.
+//
+// Roles (192 threads): warp 0 lane 0 TMA producer (3-slot K/V ring), warp 1
+// TMEM owner and (lane 0) MMA issuer, warps 2-5 softmax / epilogue (warp w:
+// TMEM lanes = query rows 32 * (w % 4) ...).  Every wait is bounded; a wait
+// that gives up flags B2_DEVERR_TIMEOUT and the CTA winds down through the
+// common exit (its copies landed, its MMAs done, TMEM freed).
+#pragma once
+
+#include "b2_common.cuh"
+#include "tcgen05.cuh"
+
+namespace b2 {
+
+constexpr int kPfRows = 128;                    // query rows per CTA (MMA M)
+constexpr int kPfKeys = 128;                    // keys per tile: 8 paged blocks
+constexpr int kPfHeadDim = 64;                  // one 128-byte swizzle row per key / query
+constexpr int kPfTile = kPfKeys * kPfHeadDim * 2;  // one K or V tile: 16 KiB
+constexpr int kPfStages = 3;
+constexpr int kPfThreads = 192;
+constexpr uint32_t kPfTmemCols = 256;  // S [0, 128) and O [128, 192)
+
+struct PfParams {
+    const void* q;
+    int q_row_stride;
+    const void* q_bias;
+    const int* block_tables;
+    const int* seq_lens_pre;
+    const int* q_start;
+    const int* q_len;
+    void* out;
+    int out_row_stride;
+    int qg;  // query heads per kv head
+    int mbps, layer_idx, n_layer, num_blocks;
+    int oob_slab;  // a slab index past the pool: boxes there read zeros
+    float scale_log2;
+};
+
+// Shared-memory plan (bytes from the 1024-aligned base).
+struct PfLayout {
+    static constexpr int off_q = 0;                          // [128][64] K-major
+    static constexpr int off_p = off_q + kPfRows * 128;      // hi: 2 key atoms of [128][64]; then lo
+    static constexpr int off_kv = off_p + 4 * kPfRows * 128;  // [stage][K | V]
+    static constexpr int off_bars = off_kv + kPfStages * 2 * kPfTile;
+    static constexpr int n_bars = 2 * kPfStages + 4;  // kv_full, kv_empty, s_full, p_ready, o_done, done
+    static constexpr int off_tmem = off_bars + 8 * n_bars;
+    static constexpr int bytes = off_tmem + 16 + 1024;
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) tmem_st8(taddr + static_cast<uint32_t>(i), v + i);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_attn_tc_kernel(const PfParams p, const __grid_constant__ CUtensorMap kv_map) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem =
+        smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // swizzled tiles need 1024-B alignment
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int h = static_cast<int>(blockIdx.y);
+    const int b = static_cast<int>(blockIdx.z);
+    const int i0 = static_cast<int>(blockIdx.x) * kPfRows;
+
+    pdl_launch_dependents();
+    pdl_wait();  // q comes from the QKV product, the keys from the KV append before this launch
+    const int T_len = __ldg(p.q_len + b);
+    if (i0 >= T_len) return;  // CTA-uniform, before any barrier or TMEM use
+    const int pre = __ldg(p.seq_lens_pre + b);
+    const int nq = min(kPfRows, T_len - i0);  // query rows of this tile
+    int kv_end = pre + i0 + nq;              // keys [0, kv_end) are read
+    if (pre < 0 || kv_end > p.mbps * kBlockTokens) {
+        if (tid == 0) flag_error(B2_DEVERR_SEQ_LEN);
+        kv_end = max(1, min(kv_end, p.mbps * kBlockTokens));
+    }
+    const int ntiles = (kv_end + kPfKeys - 1) / kPfKeys;
+    const int hk = h / p.qg;
+    const size_t row0 = static_cast<size_t>(__ldg(p.q_start + b)) + i0;
+
+    unsigned char* qbuf = smem + PfLayout::off_q;
+    unsigned char* pbuf = smem + PfLayout::off_p;
+    unsigned char* kv = smem + PfLayout::off_kv;
+    uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + PfLayout::off_bars);
+    uint64_t* kv_empty = kv_full + kPfStages;
+    uint64_t* s_full = kv_empty + kPfStages;
+    uint64_t* p_ready = s_full + 1;
+    uint64_t* o_done = p_ready + 1;
+    uint64_t* done_bar = o_done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PfLayout::off_tmem);
+
+    if (tid == 0) {
+        for (int s = 0; s < kPfStages; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(p_ready, 1);
+        mbar_init(o_done, 1);
+        mbar_init(done_bar, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kPfTmemCols);
+        tmem_relinquish();
+    }
+    const int row = 32 * (warp & 3) + lane;  // query row of an epilogue thread (its TMEM lane)
+    if (warp >= 2) {
+        // Q row (+ bias, rounded to T as the reference's add_bias stores it), zeros past the tile
+        const T* qsrc = static_cast<const T*>(p.q) + (row0 + row) * static_cast<size_t>(p.q_row_stride) +
+                        static_cast<size_t>(h) * kPfHeadDim;
+        const T* bsrc = p.q_bias != nullptr ? static_cast<const T*>(p.q_bias) + h * kPfHeadDim : nullptr;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+            if (row < nq) {
+                raw = __ldg(reinterpret_cast<const uint4*>(qsrc) + c);
+                if (bsrc != nullptr) {
+                    float f[8], bf[8];
+                    unpack16<T>(raw, f);
+                    unpack16<T>(__ldg(reinterpret_cast<const uint4*>(bsrc) + c), bf);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = __fadd_rn(f[e], bf[e]);
+                    raw = pack16<T>(f);
+                }
+            }
+            *reinterpret_cast<uint4*>(qbuf + sw128_offset(row, c * 8, 2)) = raw;
+        }
+        fence_proxy_async_smem();  // the tensor core reads Q through the async proxy
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    int issued = 0;  // producer: ring fills issued
+    if (warp == 0) {
+        // ================================================= TMA producer
+        if (lane == 0) {
+            const int* bt = p.block_tables + static_cast<size_t>(b) * p.mbps;
+            const int nblk = (kv_end + kBlockTokens - 1) / kBlockTokens;
+            for (int t = 0; t < ntiles; ++t) {
+                const int st = t % kPfStages;
+                if (t >= kPfStages &&
+                    !mbar_wait_bounded(&kv_empty[st], (static_cast<uint32_t>(t / kPfStages) & 1u) ^ 1u)) {
+                    flag_error(B2_DEVERR_TIMEOUT);
+                    break;
+                }
+                mbar_arrive_expect_tx(&kv_full[st], 2 * kPfTile);  // every box counts, zero-filled ones too
+                unsigned char* kdst = kv + st * 2 * kPfTile;
+                for (int j = 0; j < kPfKeys / kBlockTokens; ++j) {
+                    const int kb = t * (kPfKeys / kBlockTokens) + j;
+                    int slab = p.oob_slab;
+                    if (kb < nblk) {
+                        int blk = __ldg(bt + kb);
+                        if (blk < 0 || blk >= p.num_blocks) {
+                            flag_error(B2_DEVERR_BLOCK_ID);
+                            blk = 0;
+                        }
+                        slab = (blk * p.n_layer + p.layer_idx) * 2;
+                    }
+                    tma_load_4d(kdst + j * 2048, &kv_map, 0, 0, hk, slab, &kv_full[st]);
+                    tma_load_4d(kdst + kPfTile + j * 2048, &kv_map, 0, 0, hk, slab == p.oob_slab ? slab : slab + 1,
+                                &kv_full[st]);
+                }
+                issued = t + 1;
+            }
+        }
+    } else if (warp == 1) {
+        // ================================================= MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t IDESC_S = umma_idesc<T>(kPfRows, kPfKeys, false, false);
+            constexpr uint32_t IDESC_O = umma_idesc<T>(kPfRows, kPfHeadDim, false, true);
+            const uint32_t qa = smem_addr(qbuf);
+            const uint32_t pa = smem_addr(pbuf);
+            for (int t = 0; t < ntiles; ++t) {
+                const int st = t % kPfStages;
+                if (!mbar_wait_bounded(&kv_full[st], static_cast<uint32_t>(t / kPfStages) & 1u)) {
+                    flag_error(B2_DEVERR_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ka = smem_addr(kv + st * 2 * kPfTile);
+                const uint32_t va = ka + kPfTile;
+#pragma unroll
+                for (int k = 0; k < kPfHeadDim / 16; ++k)
+                    umma_f16(tmem, sw128_desc(qa + 32 * k, 16, 1024), sw128_desc(ka + 32 * k, 16, 1024), IDESC_S, k > 0);
+                umma_commit(s_full);
+                if (!mbar_wait_bounded(p_ready, static_cast<uint32_t>(t) & 1u)) {
+                    flag_error(B2_DEVERR_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < kPfKeys / 16; ++kk) {
+                    const uint32_t po = static_cast<uint32_t>((kk >> 2) * kPfRows * 128 + (kk & 3) * 32);
+                    const uint64_t vd = sw128_desc(va + static_cast<uint32_t>(kk) * 2048u, kPfTile, 1024);
+                    umma_f16(tmem + 128u, sw128_desc(pa + po, 16, 1024), vd, IDESC_O, t > 0 || kk > 0);
+                    umma_f16(tmem + 128u, sw128_desc(pa + 2 * kPfRows * 128 + po, 16, 1024), vd, IDESC_O, true);
+                }
+                umma_commit(o_done);
+                umma_commit(&kv_empty[st]);
+            }
+        }
+    } else {
+        // ================================================= softmax / epilogue
+        const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        const uint32_t s_addr = tmem + lane_base;
+        const uint32_t o_addr = tmem + lane_base + 128u;
+        const bool valid = row < nq;
+        const int qpos = pre + i0 + row;
+        float m_ref = -INFINITY, l = 0.0f;
+        bool ok = true;
+        int t = 0;
+        for (; t < ntiles; ++t) {
+            ok = mbar_wait_bounded(s_full, static_cast<uint32_t>(t) & 1u);
+            if (named_sync_or(1, kPfThreads - 64, !ok)) {
+                if (!ok) flag_error(B2_DEVERR_TIMEOUT);
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int kbase = t * kPfKeys;
+            // pass 1: the row maximum over the keys this row may see
+            float mx = -INFINITY;
+            for (int c0 = 0; c0 < kPfKeys; c0 += 32) {
+                float v[32];
+                tmem_ld32(s_addr + static_cast<uint32_t>(c0), v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (valid && kbase + c0 + j <= qpos) mx = fmaxf(mx, v[j] * p.scale_log2);
+            }
+            // PV(t-1) must have finished before O is rescaled and P is overwritten
+            if (t > 0) ok = mbar_wait_bounded(o_done, static_cast<uint32_t>(t - 1) & 1u);
+            if (named_sync_or(2, kPfThreads - 64, !ok)) {
+                if (!ok) flag_error(B2_DEVERR_TIMEOUT);
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            // move the reference maximum (always on a row's first keys, which are in
+            // tile 0: key 0 is visible to every row); O rows are rescaled by all
+            // threads together when any row moved (tcgen05.ld/st are warp-wide)
+            const bool need = mx > m_ref + 8.0f;
+            float corr = 1.0f;
+            if (need) {
+                corr = exp2f(m_ref - mx);
+                l *= corr;
+                m_ref = mx;
+            }
+            if (named_sync_or(4, kPfThreads - 64, need) && t > 0) {
+#pragma unroll
+                for (int c0 = 0; c0 < kPfHeadDim; c0 += 32) {
+                    float o[32];
+                    tmem_ld32(o_addr + static_cast<uint32_t>(c0), o);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) o[j] *= corr;
+                    tmem_st32(o_addr + static_cast<uint32_t>(c0), o);
+                }
+                tmem_wait_st();
+            }
+            // pass 2: weights, split into two 16-bit halves, into P (K-major, 2 key atoms)
+            for (int c0 = 0; c0 < kPfKeys; c0 += 32) {
+                float v[32];
+                tmem_ld32(s_addr + static_cast<uint32_t>(c0), v);
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                    float hi[8], lo[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int kp = kbase + c0 + j + e;
+                        const float pw = (valid && kp <= qpos) ? exp2f(v[j + e] * p.scale_log2 - m_ref) : 0.0f;
+                        l += pw;
+                        hi[e] = Elem<T>::to_f(Elem<T>::from_f(pw));
+                        lo[e] = pw - hi[e];
+                    }
+                    const int key = c0 + j;  // 8 keys = one 16-byte chunk of the row
+                    const uint32_t off = static_cast<uint32_t>((key >> 6) * kPfRows * 128) + sw128_offset(row, key & 63, 2);
+                    *reinterpret_cast<uint4*>(pbuf + off) = pack16<T>(hi);
+                    *reinterpret_cast<uint4*>(pbuf + 2 * kPfRows * 128 + off) = pack16<T>(lo);
+                }
+            }
+            if (t == ntiles - 1 && kbase + row >= kv_end) {
+                // key row past the keys in use: zero its V (P is 0 there; V may be stale)
+                uint4* vrow = reinterpret_cast<uint4*>(kv + (t % kPfStages) * 2 * kPfTile + kPfTile + row * 128);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) vrow[c] = make_uint4(0u, 0u, 0u, 0u);
+            }
+            fence_proxy_async_smem();  // P and the zeroed V rows are read by the tensor core
+            tc_fence_before();
+            named_sync(3, kPfThreads - 64);
+            if (tid == 64) mbar_arrive(p_ready);
+        }
+        // ---- O / l for the tile's rows (every lane loads: tcgen05.ld is warp-wide)
+        bool fin = ok && mbar_wait_bounded(o_done, static_cast<uint32_t>(ntiles - 1) & 1u);
+        if (!named_sync_or(5, kPfThreads - 64, !fin)) {
+            tc_fence_after();
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            T* dst = static_cast<T*>(p.out) + (row0 + row) * static_cast<size_t>(p.out_row_stride) +
+                     static_cast<size_t>(h) * kPfHeadDim;
+#pragma unroll
+            for (int c0 = 0; c0 < kPfHeadDim; c0 += 32) {
+                float o[32];
+                tmem_ld32(o_addr + static_cast<uint32_t>(c0), o);
+                if (valid) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        float f[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = o[j + e] * inv;
+                        *reinterpret_cast<uint4*>(dst + c0 + j) = pack16<T>(f);
+                    }
+                }
+            }
+        } else if (ok) {
+            flag_error(B2_DEVERR_TIMEOUT);
+        }
+        tc_fence_before();
+    }
+
+    // ---- common exit: copies landed, MMAs done, TMEM freed
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < kPfStages && s < issued; ++s) {
+            const int last_use = (issued - 1 - s) / kPfStages;
+            if (!mbar_wait_bounded(&kv_full[s], static_cast<uint32_t>(last_use) & 1u)) flag_error(B2_DEVERR_TIMEOUT);
+        }
+    }
+    if (warp == 1 && lane == 0) {
+        umma_commit(done_bar);
+        if (!mbar_wait_bounded(done_bar, 0)) flag_error(B2_DEVERR_TIMEOUT);
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, kPfTmemCols);
+}
+
+}  // namespace b2

@@ -23,7 +23,8 @@ from . import F16, LIB_DIR, B2Error, load as load_decode
 ENGINE_SYMBOLS = (
     "b2_engine_create", "b2_engine_create_synthetic", "b2_engine_destroy", "b2_engine_add_sequence",
     "b2_engine_add_sequence_cached", "b2_engine_decode_step", "b2_engine_free_sequence",
-    "b2_engine_free_blocks", "b2_engine_set_use_cuda_graphs", "b2_engine_shape", "b2_engine_stream",
+    "b2_engine_free_blocks", "b2_engine_set_use_cuda_graphs", "b2_engine_set_prefill_tensor_cores",
+    "b2_engine_shape", "b2_engine_stream",
     "b2_engine_last_error", "b2_block_pool_create", "b2_block_pool_destroy", "b2_block_pool_allocate",
     "b2_block_pool_free", "b2_block_pool_num_free", "b2_engine_tp_handle", "b2_engine_tp_connect",
     "b2_engine_prefill",
@@ -79,6 +80,7 @@ def load() -> ctypes.CDLL:
     lib.b2_engine_free_blocks.argtypes = [_vp]
     lib.b2_engine_free_blocks.restype = ctypes.c_int64
     lib.b2_engine_set_use_cuda_graphs.argtypes = [_vp, _i32]
+    lib.b2_engine_set_prefill_tensor_cores.argtypes = [_vp, _i32]
     lib.b2_engine_shape.argtypes = [_vp, P(ModelShape)]
     lib.b2_engine_stream.argtypes = [_vp, P(_vp)]
     lib.b2_engine_last_error.restype = ctypes.c_char_p
@@ -191,6 +193,9 @@ class Engine:
 
     def set_use_cuda_graphs(self, enabled: bool) -> None:
         _check(self._lib.b2_engine_set_use_cuda_graphs(self._handle(), 1 if enabled else 0))
+
+    def set_prefill_tensor_cores(self, enabled: bool) -> None:
+        _check(self._lib.b2_engine_set_prefill_tensor_cores(self._handle(), 1 if enabled else 0))
 
     def tp_handle(self) -> bytes:
         """This head-sharded rank's IPC handles, to be shared with every rank."""
