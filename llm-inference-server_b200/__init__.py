@@ -52,7 +52,7 @@ class PagedAttnArgs(ctypes.Structure):
                 ("kv_pool", _vp), ("block_tables", _vp), ("seq_lens", _vp), ("out", _vp), ("batch", _c_int),
                 ("n_head", _c_int), ("n_kv_head", _c_int), ("head_dim", _c_int), ("max_blocks_per_seq", _c_int),
                 ("layer_idx", _c_int), ("n_layer", _c_int), ("num_blocks", _c_int), ("scale", _c_float),
-                ("flags", _c_int)]
+                ("flags", _c_int), ("max_ctas", _c_int)]
 
 
 class LinearArgs(ctypes.Structure):
@@ -154,10 +154,12 @@ def kv_append(kv_pool, k, v, kv_row_stride, block_tables, seq_lens, *, n_kv_head
 
 
 def attn_args(q, q_row_stride, kv_pool, block_tables, seq_lens, out, *, n_head, n_kv_head, head_dim,
-              max_blocks_per_seq, layer_idx, n_layer, num_blocks, scale=0.0, q_bias=None, flags=0) -> PagedAttnArgs:
+              max_blocks_per_seq, layer_idx, n_layer, num_blocks, scale=0.0, q_bias=None, flags=0,
+              max_ctas=0) -> PagedAttnArgs:
     return PagedAttnArgs(dtype_code(kv_pool.dtype), dtype_code(out.dtype), _ptr(q), q_row_stride, _ptr(q_bias),
                          _ptr(kv_pool), _ptr(block_tables), _ptr(seq_lens), _ptr(out), block_tables.shape[0], n_head,
-                         n_kv_head, head_dim, max_blocks_per_seq, layer_idx, n_layer, num_blocks, scale, flags)
+                         n_kv_head, head_dim, max_blocks_per_seq, layer_idx, n_layer, num_blocks, scale, flags,
+                         max_ctas)
 
 
 def attention_workspace(args: PagedAttnArgs):

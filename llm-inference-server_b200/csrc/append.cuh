@@ -29,6 +29,11 @@ template <typename T, int DH>
 __global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams p) {
     constexpr int E = Elem<T>::kPer16B;
     constexpr int GL = DH / E;
+    // The attention launched next may start now: with B2_ATTN_NEWEST_ROW_PENDING
+    // it streams every key row but the one written here, and waits for this
+    // kernel before reading that row (and with flags 0 before reading anything).
+    pdl_launch_dependents();
+    pdl_wait();  // k and v come from the kernel before this one
     const int chunks_per_row = p.n_kv_head * GL;  // per K (or V) row
     const long long total = static_cast<long long>(p.batch) * 2 * chunks_per_row;
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;

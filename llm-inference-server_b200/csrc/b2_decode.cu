@@ -163,6 +163,7 @@ int check_attn_args(const B2PagedAttnArgs* a) {
     if (a->q_row_stride < a->n_head * a->head_dim) return fail(B2_ERR_SHAPE, "q_row_stride < n_head*head_dim");
     if (a->flags != 0 && a->flags != B2_ATTN_INPUTS_READY && a->flags != B2_ATTN_NEWEST_ROW_PENDING)
         return fail(B2_ERR_SHAPE, "unknown flags");
+    if (a->max_ctas < 0) return fail(B2_ERR_SHAPE, "max_ctas < 0");
     if (!aligned16(a->q) || !aligned16(a->kv_pool) || !aligned16(a->out) || (a->q_bias && !aligned16(a->q_bias)) ||
         (static_cast<long long>(a->q_row_stride) * es) % 16 != 0)
         return fail(B2_ERR_ALIGN, "q, q_bias, kv_pool and out must be 16-byte aligned, q_row_stride*elem 16-byte multiple");
@@ -187,7 +188,7 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
         if (tc_smem_bytes(qg, stages) <= di.max_smem_optin) {
             pl->tensor_cores = true;
             pl->tc_stages = stages;
-            pl->grid = di.sms;
+            pl->grid = a->max_ctas > 0 ? std::min(di.sms, a->max_ctas) : di.sms;
             pl->threads = kTcThreads;
             pl->smem = tc_smem_bytes(qg, stages);
             pl->combine_threads = static_cast<int>(align_up(static_cast<size_t>(H) * GL, 32));
@@ -245,7 +246,7 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     off += (2 * best_s + 2 * kPieceRing + 1) * 8;
     pl->smem = off;
     pl->threads = p.ncons + 64;
-    pl->grid = di.sms * best_cps;
+    pl->grid = a->max_ctas > 0 ? std::min(di.sms * best_cps, a->max_ctas) : di.sms * best_cps;
     pl->combine_threads = static_cast<int>(align_up(static_cast<size_t>(H) * GL, 32));
 
     // One partial per (CTA, sequence) pair and token subgroup; cta + b < grid + batch.
