@@ -525,10 +525,9 @@ def run_engine(args, rank: int, world: int, dist) -> None:
     frac = achieved / (peak * world)
     steps_total = args.steps * r["waves"]
     es = EB.elem_bytes(w.dtype)
-    mbps = (w.n_ctx + 15) // 16
-    # embedding, per layer LN/append/attention/LN/GELU, final LN, argmax (+ epoch bump and a barrier per
-    # layer when head-sharded)
-    ours_per_step = 1 + 5 * w.n_layer + 2 + (1 + w.n_layer if w.head_sharded and world > 1 else 0)
+    # block-table update scatter, table gather, embedding, per layer LN/append/attention/LN/GELU, final LN,
+    # argmax (+ epoch bump and a barrier per layer when head-sharded)
+    ours_per_step = 2 + 1 + 5 * w.n_layer + 2 + (1 + w.n_layer if w.head_sharded and world > 1 else 0)
     line = {
         "metric": "GPT-2 decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_max / steps_total, 4),
@@ -547,10 +546,13 @@ def run_engine(args, rank: int, world: int, dist) -> None:
                      "roofline_tok_s": round(value / frac, 1)},
         "cpu_baseline": None,
         "e2e": {"value": round(value, 1), "unit": "tok/s",
-                "h2d_bytes_per_step": 4 * (3 * r["wave"] + r["wave"] * mbps),
+                # tokens, positions, seq_lens and table slots (4 int32 per sequence) + one 12-byte
+                # (slot, index, block) update per newly allocated block: one per sequence every 16 steps
+                "h2d_bytes_per_step": 16 * r["wave"] + (12 * r["wave"] + 15) // 16,
                 "d2h_bytes_per_step": 4 * r["wave"],
-                "path": "value is already end to end: b2_engine_decode_step (host block tables, one upload, graph "
-                        "replay, download of next tokens, stream sync) timed with CUDA events on the engine stream"},
+                "path": "value is already end to end: b2_engine_decode_step (device-resident block tables updated "
+                        "incrementally, one upload of the step inputs, graph replay, download of next tokens, "
+                        "stream sync) timed with CUDA events on the engine stream"},
         "clocks": clk.summary(),
         "gpu_launches": ours_per_step * steps_total,
         "elem_bytes": es,

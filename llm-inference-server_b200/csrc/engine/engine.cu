@@ -101,6 +101,25 @@ __global__ void gather_rows_kernel(uint4* dst, const uint4* src, const int32_t* 
     }
 }
 
+// Block tables live on the device, one row of max_blocks_per_seq entries per
+// sequence slot.  The host sends only what changed: (slot, index, block)
+// triples for newly allocated blocks, scattered here.
+__global__ void scatter_table_updates_kernel(int32_t* slot_tables, const int32_t* upd, int n, int mbps) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) slot_tables[static_cast<size_t>(upd[3 * i]) * mbps + upd[3 * i + 1]] = upd[3 * i + 2];
+}
+
+// The step's batch-ordered tables [bucket][mbps] from the slot rows: lane b
+// copies the entries of the blocks holding positions [0, seq_lens[b]] (the
+// only ones any kernel of the step reads).
+__global__ void gather_step_tables_kernel(int32_t* tables, const int32_t* slot_tables, const int32_t* slots,
+                                          const int32_t* seq_lens, int mbps) {
+    const int b = blockIdx.x;
+    const int n = min(mbps, seq_lens[b] / B2_BLOCK_TOKENS + 1);
+    const int32_t* src = slot_tables + static_cast<size_t>(slots[b]) * mbps;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) tables[static_cast<size_t>(b) * mbps + j] = src[j];
+}
+
 // ------------------------------------------------------------- the engine
 
 struct LayerW {
@@ -109,6 +128,7 @@ struct LayerW {
 
 struct Seq {
     BlockTable table;
+    int slot = -1;    // row of the device-resident block tables
     int seq_len = 0;  // positions already in the KV cache
     std::vector<int32_t> prompt;
     int prompt_pos = 0;
@@ -166,8 +186,17 @@ struct Engine {
     cublasHandle_t cublas = nullptr;
     void* cublas_ws = nullptr;
     // Per-step buffers at fixed addresses (CUDA graphs replay them).
+    // d_in: [tokens | positions | seq_lens | slots] (max_batch each) and the
+    // step's gathered block tables [max_batch][mbps].
     int32_t *d_in = nullptr, *d_seq_post = nullptr, *d_next = nullptr;
     int32_t *h_in = nullptr, *h_next = nullptr;  // pinned
+    // Device-resident block tables [num_blocks slots][mbps] (a live sequence
+    // holds at least one block, so num_blocks slots always suffice), the free
+    // slots, and the (slot, index, block) updates not yet on the device.
+    int32_t* d_slot_tables = nullptr;
+    int32_t *d_upd = nullptr, *h_upd = nullptr;  // update staging, kUpdChunk triples
+    std::vector<int> free_slots;
+    std::vector<int32_t> pending_upd;
     void *d_resid = nullptr, *d_x = nullptr, *d_qkv = nullptr, *d_attn = nullptr, *d_attn_out = nullptr,
          *d_ff = nullptr, *d_ff_out = nullptr, *d_logits = nullptr;
     void* attn_ws = nullptr;
@@ -204,10 +233,12 @@ struct Engine {
          *p_ff = nullptr, *p_ff_out = nullptr, *p_last = nullptr, *p_logits = nullptr, *p_attn_ws = nullptr;
     size_t p_attn_ws_bytes = 0;
 
+    static constexpr int kUpdChunk = 4096;  // table updates per upload
     int32_t* in_tokens() const { return d_in; }
     int32_t* in_positions() const { return d_in + cfg.max_batch; }
     int32_t* in_seq_lens() const { return d_in + 2 * cfg.max_batch; }
-    int32_t* in_tables() const { return d_in + 3 * cfg.max_batch; }
+    int32_t* in_slots() const { return d_in + 3 * cfg.max_batch; }
+    int32_t* in_tables() const { return d_in + 4 * cfg.max_batch; }
 
     ~Engine() {
         if (device >= 0) cudaSetDevice(device);
@@ -219,10 +250,11 @@ struct Engine {
                             d_attn, d_attn_out, d_ff, d_ff_out, d_logits, attn_ws, tp_weights, d_gath,
                             d_flags, d_epoch, d_peer_outs, d_peer_flags, d_pin, d_pseq_post, d_pnext,
                             p_resid, p_x, p_qkv, p_attn, p_attn_out, p_ff, p_ff_out, p_last, p_logits,
-                            p_attn_ws};
+                            p_attn_ws, d_slot_tables, d_upd};
         for (void* p : dev_ptrs)
             if (p) cudaFree(p);
         if (h_in) cudaFreeHost(h_in);
+        if (h_upd) cudaFreeHost(h_upd);
         if (h_next) cudaFreeHost(h_next);
         if (h_pin) cudaFreeHost(h_pin);
         if (h_pnext) cudaFreeHost(h_pnext);
@@ -369,11 +401,18 @@ struct Engine {
         cuda_ok(cudaMalloc(&pool, layer_bytes() * shape.n_layer), "malloc KV pool");
         cuda_ok(cudaMemsetAsync(pool, 0, layer_bytes() * shape.n_layer, stream), "memset KV pool");
         blocks = std::make_unique<BlockPool>(num_blocks);
-        const size_t in_ints = 3 * static_cast<size_t>(B) + static_cast<size_t>(B) * mbps;
+        const size_t in_ints = 4 * static_cast<size_t>(B) + static_cast<size_t>(B) * mbps;
         cuda_ok(cudaMalloc(&d_in, in_ints * 4), "malloc step inputs");
         cuda_ok(cudaMemsetAsync(d_in, 0, in_ints * 4, stream), "memset step inputs");
-        cuda_ok(cudaMallocHost(&h_in, in_ints * 4), "pinned step inputs");
-        std::memset(h_in, 0, in_ints * 4);
+        cuda_ok(cudaMallocHost(&h_in, 4 * static_cast<size_t>(B) * 4), "pinned step inputs");
+        std::memset(h_in, 0, 4 * static_cast<size_t>(B) * 4);
+        const size_t slot_ints = static_cast<size_t>(num_blocks) * mbps;
+        cuda_ok(cudaMalloc(&d_slot_tables, slot_ints * 4), "malloc block tables");
+        cuda_ok(cudaMemsetAsync(d_slot_tables, 0, slot_ints * 4, stream), "memset block tables");
+        cuda_ok(cudaMalloc(&d_upd, 3 * static_cast<size_t>(kUpdChunk) * 4), "malloc table updates");
+        cuda_ok(cudaMallocHost(&h_upd, 3 * static_cast<size_t>(kUpdChunk) * 4), "pinned table updates");
+        free_slots.resize(static_cast<size_t>(num_blocks));
+        for (int i = 0; i < num_blocks; ++i) free_slots[static_cast<size_t>(i)] = num_blocks - 1 - i;
         cuda_ok(cudaMalloc(&d_seq_post, B * 4), "malloc seq_lens_post");
         cuda_ok(cudaMalloc(&d_next, B * 4), "malloc next tokens");
         cuda_ok(cudaMallocHost(&h_next, B * 4), "pinned next tokens");
@@ -445,6 +484,10 @@ struct Engine {
         b2_stream_t s = stream;
         const char* qkv = static_cast<const char*>(d_qkv);
         if (tp > 1) b2_ok(b2_tp_epoch_bump(d_epoch, s), "tp_epoch_bump");  // a new step for the barriers
+        // this step's block tables, gathered from the device-resident slot rows
+        gather_step_tables_kernel<<<bucket, 64, 0, stream>>>(in_tables(), d_slot_tables, in_slots(), in_seq_lens(),
+                                                              mbps);
+        cuda_ok(cudaGetLastError(), "gather step tables");
         b2_ok(b2_embedding(dt, d_resid, wte, wpe, in_tokens(), in_positions(), bucket, D, V, shape.n_ctx, s), "embedding");
         const void* delta = nullptr;
         const void* delta_bias = nullptr;
@@ -620,8 +663,7 @@ struct Engine {
         for (int i = 0; i < n; ++i) {
             Seq& q = *sv[static_cast<size_t>(i)];
             const int t = static_cast<int>(q.prompt.size()) - q.prompt_pos;
-            while (static_cast<int>(q.table.ids.size()) * B2_BLOCK_TOKENS < q.seq_len + t)
-                q.table.ids.push_back(blocks->allocate());
+            while (static_cast<int>(q.table.ids.size()) * B2_BLOCK_TOKENS < q.seq_len + t) grow(q);
             s_pre[i] = q.seq_len;
             s_start[i] = r;
             s_rows[i] = t;
@@ -736,6 +778,57 @@ struct Engine {
         }
     }
 
+    // ---- sequences and their device-resident block tables
+
+    // Registers a sequence whose table already holds its first blocks: a slot,
+    // and one pending table update per block.
+    int32_t register_seq(Seq&& q) {
+        if (free_slots.empty()) throw Error(B2_ERR_POOL, "no free block-table slot");
+        q.slot = free_slots.back();
+        free_slots.pop_back();
+        for (size_t j = 0; j < q.table.ids.size(); ++j) note_block(q, static_cast<int>(j));
+        const int32_t id = next_id++;
+        seqs.emplace(id, std::move(q));
+        return id;
+    }
+
+    void note_block(const Seq& q, int j) {
+        pending_upd.push_back(q.slot);
+        pending_upd.push_back(j);
+        pending_upd.push_back(q.table.ids[static_cast<size_t>(j)]);
+    }
+
+    // One more block at the end of q's table (the caller checked the pool).
+    void grow(Seq& q) {
+        q.table.ids.push_back(blocks->allocate());
+        note_block(q, static_cast<int>(q.table.ids.size()) - 1);
+    }
+
+    void release_seq(int32_t id) {
+        auto it = seqs.find(id);
+        if (it == seqs.end()) return;
+        for (int blk : it->second.table.ids) blocks->free(blk);
+        free_slots.push_back(it->second.slot);
+        seqs.erase(it);
+    }
+
+    // Uploads the pending table updates and scatters them into the slot rows
+    // (stream-ordered before the step that needs them).
+    void flush_table_updates() {
+        const size_t n = pending_upd.size() / 3;
+        for (size_t done = 0; done < n; done += kUpdChunk) {
+            const int m = static_cast<int>(std::min<size_t>(kUpdChunk, n - done));
+            // the staging buffer is reused: the previous chunk's copy must have left it
+            cuda_ok(cudaStreamSynchronize(stream), "table update staging");
+            std::memcpy(h_upd, pending_upd.data() + 3 * done, static_cast<size_t>(m) * 12);
+            cuda_ok(cudaMemcpyAsync(d_upd, h_upd, static_cast<size_t>(m) * 12, cudaMemcpyHostToDevice, stream),
+                    "upload table updates");
+            scatter_table_updates_kernel<<<(m + 255) / 256, 256, 0, stream>>>(d_slot_tables, d_upd, m, mbps);
+            cuda_ok(cudaGetLastError(), "scatter table updates");
+        }
+        pending_upd.clear();
+    }
+
     void decode_step(const int32_t* ids, int batch, int32_t* out) {
         if (batch <= 0 || batch > cfg.max_batch) throw Error(B2_ERR_SHAPE, "batch must be in [1, max_batch]");
         if (tp > 1 && !tp_connected) throw Error(B2_ERR_SHAPE, "head-sharded engine is not connected (b2_engine_tp_connect)");
@@ -757,24 +850,25 @@ struct Engine {
         int32_t* tok = h_in;
         int32_t* pos = h_in + B;
         int32_t* sl = h_in + 2 * B;
-        int32_t* bt = h_in + 3 * B;
+        int32_t* slot = h_in + 3 * B;
         for (int i = 0; i < batch; ++i) {
             Seq& q = *sv[static_cast<size_t>(i)];
-            if (static_cast<int>(q.table.ids.size()) * B2_BLOCK_TOKENS <= q.seq_len) q.table.ids.push_back(blocks->allocate());
+            if (static_cast<int>(q.table.ids.size()) * B2_BLOCK_TOKENS <= q.seq_len) grow(q);
             tok[i] = q.prompt_pos < static_cast<int>(q.prompt.size()) ? q.prompt[static_cast<size_t>(q.prompt_pos)] : q.last_token;
             pos[i] = q.seq_len;
             sl[i] = q.seq_len;
-            int32_t* row = bt + static_cast<size_t>(i) * mbps;
-            for (size_t j = 0; j < q.table.ids.size(); ++j) row[j] = q.table.ids[j];
+            slot[i] = q.slot;
         }
         for (int i = batch; i < bucket; ++i) {  // pad lanes replay the last real lane
             tok[i] = tok[batch - 1];
             pos[i] = pos[batch - 1];
             sl[i] = sl[batch - 1];
-            std::memcpy(bt + static_cast<size_t>(i) * mbps, bt + static_cast<size_t>(batch - 1) * mbps, mbps * 4);
+            slot[i] = slot[batch - 1];
         }
-        const size_t up = (3 * static_cast<size_t>(B) + static_cast<size_t>(bucket) * mbps) * 4;
-        cuda_ok(cudaMemcpyAsync(d_in, h_in, up, cudaMemcpyHostToDevice, stream), "upload step inputs");
+        // the h_in copy of the previous step is complete: that step synchronised
+        flush_table_updates();
+        cuda_ok(cudaMemcpyAsync(d_in, h_in, 4 * static_cast<size_t>(B) * 4, cudaMemcpyHostToDevice, stream),
+                "upload step inputs");
         if (use_graphs)
             cuda_ok(cudaGraphLaunch(graph_for(bucket), stream), "cudaGraphLaunch");
         else
@@ -1000,8 +1094,7 @@ int32_t b2_engine_add_sequence(b2_engine* eng, const int32_t* prompt, int32_t pr
         b2::eng::Seq q;
         q.table.ids.push_back(blk);
         q.prompt.assign(prompt, prompt + prompt_len);
-        id = eng->next_id++;
-        eng->seqs.emplace(id, std::move(q));
+        id = eng->register_seq(std::move(q));
     });
     return rc == B2_OK ? id : rc;
 }
@@ -1018,8 +1111,7 @@ int32_t b2_engine_add_sequence_cached(b2_engine* eng, int32_t ctx_len, int32_t l
         for (int i = 0; i < nblk; ++i) q.table.ids.push_back(eng->blocks->allocate());
         q.seq_len = ctx_len;
         q.last_token = last_token;
-        id = eng->next_id++;
-        eng->seqs.emplace(id, std::move(q));
+        id = eng->register_seq(std::move(q));
     });
     return rc == B2_OK ? id : rc;
 }
@@ -1048,12 +1140,7 @@ int b2_engine_prefill(b2_engine* eng, const int32_t* seq_ids, int32_t n, int32_t
 
 int b2_engine_free_sequence(b2_engine* eng, int32_t seq_id) {
     if (!eng) return B2_ERR_NULL;
-    return guarded([&] {
-        auto it = eng->seqs.find(seq_id);
-        if (it == eng->seqs.end()) return;
-        for (int blk : it->second.table.ids) eng->blocks->free(blk);
-        eng->seqs.erase(it);
-    });
+    return guarded([&] { eng->release_seq(seq_id); });
 }
 
 int64_t b2_engine_free_blocks(const b2_engine* eng) { return eng ? eng->blocks->num_free() : 0; }
