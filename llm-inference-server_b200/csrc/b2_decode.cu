@@ -1081,8 +1081,8 @@ int launch_prefill_t(const B2PrefillAttnArgs* a, const PfParams& pp, const CUten
     const int rc = ensure_max_smem(kern, smem_set, dev, di.max_smem_optin);
     if (rc != B2_OK) return rc;
     if (PfLayout::bytes > di.max_smem_optin) return fail(B2_ERR_UNSUPPORTED, "prefill attention: shared memory");
-    const dim3 grid(static_cast<unsigned>((a->max_q_len + kPfRows - 1) / kPfRows), static_cast<unsigned>(a->n_head),
-                    static_cast<unsigned>(a->n_seqs));
+    const dim3 grid(static_cast<unsigned>(a->n_seqs), static_cast<unsigned>(a->n_head),
+                    static_cast<unsigned>((a->max_q_len + kPfRows - 1) / kPfRows));
     return launch_pdl(kern, grid, dim3(kPfThreads), PfLayout::bytes, stream, pp, map);
 }
 
@@ -1100,7 +1100,8 @@ extern "C" int b2_prefill_attention(const B2PrefillAttnArgs* a, b2_stream_t stre
     if (a->head_dim != kPfHeadDim) return fail(B2_ERR_UNSUPPORTED, "prefill attention: head_dim must be 64");
     if (a->n_kv_head <= 0 || a->n_head <= 0 || a->n_head % a->n_kv_head != 0)
         return fail(B2_ERR_SHAPE, "n_head must be a positive multiple of n_kv_head");
-    if (a->n_seqs > 65535 || a->n_head > 65535) return fail(B2_ERR_SHAPE, "n_seqs and n_head must be <= 65535");
+    if (a->n_head > 65535 || (a->max_q_len + kPfRows - 1) / kPfRows > 65535)
+        return fail(B2_ERR_SHAPE, "n_head and max_q_len / 128 must be <= 65535");
     if (a->max_blocks_per_seq <= 0 || a->n_layer <= 0 || a->layer_idx < 0 || a->layer_idx >= a->n_layer ||
         a->num_blocks <= 0 || static_cast<long long>(a->num_blocks) * a->n_layer * 2 >= (1LL << 31) - 1)
         return fail(B2_ERR_SHAPE, "max_blocks_per_seq, n_layer, layer_idx or num_blocks out of range");

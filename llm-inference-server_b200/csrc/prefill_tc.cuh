@@ -10,11 +10,13 @@
 // attention (gpu-engine/src/kernels/attention.cu:49-127, cpu_model.cpp:131-162)
 // gives that row, with every key tile read once per 128 query rows.
 //
-// One CTA per (128-row query tile, query head, sequence):
+// One CTA per (sequence, query head, 128-row query tile):
 //   Q tile [128 rows][64]             smem, SWIZZLE_128B K-major (threads, + bias)
 //   K, V tiles [128 keys][64]         8 paged blocks x one 16-row TMA box each
-//   S = Q . K^T      M=128 N=128 K=64  fp32 in TMEM columns [0, 128)
-//   O += P . V       M=128 N=64  K=128 fp32 in TMEM columns [128, 192)
+//   S = Q . K^T      M=128 N=128 K=64  fp32 in TMEM, two buffers (columns
+//                                      [0, 128) and [128, 256)): S(t + 1) is
+//                                      computed while the softmax reads S(t)
+//   O += P . V       M=128 N=64  K=128 fp32 in TMEM columns [256, 320)
 // P is written by the softmax threads as two 16-bit halves hi = T(p) and
 // lo = T(p - hi) and both are multiplied in (16 significant bits per weight).
 // Softmax in log2 units with a lazily moved reference maximum (moves only when
@@ -25,9 +27,12 @@
 // past the keys in use are zeroed before the PV product, so stale values there
 // (never written) cannot reach the output.
 //
-// Roles (192 threads): warp 0 lane 0 TMA producer (3-slot K/V ring), warp 1
-// TMEM owner and (lane 0) MMA issuer, warps 2-5 softmax / epilogue (warp w:
-// TMEM lanes = query rows 32 * (w % 4) ...).  Every wait is bounded; a wait
+// Roles (320 threads): warp 0 lane 0 TMA producer (3-slot K/V ring), warp 1
+// TMEM owner and (lane 0) MMA issuer, warps 2-9 softmax / epilogue: two
+// threads per query row (warps w and w + 4 read the same TMEM lanes
+// 32 * (w % 4) ...), each taking 64 of a tile's 128 keys, so every SM
+// sub-partition has two softmax warps to interleave; the two halves of a row
+// exchange their maxima (and at the end their sums) through shared memory.  Every wait is bounded; a wait
 // that gives up flags B2_DEVERR_TIMEOUT and the CTA winds down through the
 // common exit (its copies landed, its MMAs done, TMEM freed).
 #pragma once
@@ -42,8 +47,10 @@ constexpr int kPfKeys = 128;                    // keys per tile: 8 paged blocks
 constexpr int kPfHeadDim = 64;                  // one 128-byte swizzle row per key / query
 constexpr int kPfTile = kPfKeys * kPfHeadDim * 2;  // one K or V tile: 16 KiB
 constexpr int kPfStages = 3;
-constexpr int kPfThreads = 192;
-constexpr uint32_t kPfTmemCols = 256;  // S [0, 128) and O [128, 192)
+constexpr int kPfSoftmax = 256;  // two threads per query row, 64 key columns each
+constexpr int kPfThreads = 64 + kPfSoftmax;
+constexpr uint32_t kPfTmemCols = 512;  // S(t even) [0, 128), S(t odd) [128, 256), O [256, 320)
+constexpr uint32_t kPfOCol = 256;
 
 struct PfParams {
     const void* q;
@@ -66,11 +73,20 @@ struct PfLayout {
     static constexpr int off_q = 0;                          // [128][64] K-major
     static constexpr int off_p = off_q + kPfRows * 128;      // hi: 2 key atoms of [128][64]; then lo
     static constexpr int off_kv = off_p + 4 * kPfRows * 128;  // [stage][K | V]
-    static constexpr int off_bars = off_kv + kPfStages * 2 * kPfTile;
-    static constexpr int n_bars = 2 * kPfStages + 4;  // kv_full, kv_empty, s_full, p_ready, o_done, done
+    static constexpr int off_red = off_kv + kPfStages * 2 * kPfTile;  // [2 halves][128 rows] fp32
+    static constexpr int off_bars = off_red + 2 * kPfRows * 4;
+    static constexpr int n_bars = 2 * kPfStages + 5;  // kv_full, kv_empty, s_full[2], p_ready, o_done, done
     static constexpr int off_tmem = off_bars + 8 * n_bars;
     static constexpr int bytes = off_tmem + 16 + 1024;
 };
+
+// 2^x by the SFU (ex2.approx.ftz: relative error ~2^-22, far below the 16
+// bits the hi/lo split of a weight keeps; inputs here are <= 8).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 #pragma unroll
@@ -86,9 +102,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
+    // grid (sequence, head, query tile) with the tile index reversed in the
+    // slowest dimension: CTAs are dispatched in launch order, so the tiles with
+    // the most keys (the last ones) start first and the short ones fill the tail
+    const int b = static_cast<int>(blockIdx.x);
     const int h = static_cast<int>(blockIdx.y);
-    const int b = static_cast<int>(blockIdx.z);
-    const int i0 = static_cast<int>(blockIdx.x) * kPfRows;
+    const int i0 = static_cast<int>(gridDim.z - 1 - blockIdx.z) * kPfRows;
 
     pdl_launch_dependents();
     pdl_wait();  // q comes from the QKV product, the keys from the KV append before this launch
@@ -110,8 +129,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     unsigned char* kv = smem + PfLayout::off_kv;
     uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + PfLayout::off_bars);
     uint64_t* kv_empty = kv_full + kPfStages;
-    uint64_t* s_full = kv_empty + kPfStages;
-    uint64_t* p_ready = s_full + 1;
+    uint64_t* s_full = kv_empty + kPfStages;  // [2]: one per S buffer
+    uint64_t* p_ready = s_full + 2;
     uint64_t* o_done = p_ready + 1;
     uint64_t* done_bar = o_done + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PfLayout::off_tmem);
@@ -121,7 +140,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        mbar_init(s_full, 1);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
         mbar_init(p_ready, 1);
         mbar_init(o_done, 1);
         mbar_init(done_bar, 1);
@@ -131,14 +151,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tmem_alloc(tmem_slot, kPfTmemCols);
         tmem_relinquish();
     }
-    const int row = 32 * (warp & 3) + lane;  // query row of an epilogue thread (its TMEM lane)
+    // softmax threads: query row = their TMEM lane (warp w reads lanes 32 * (w % 4) ...),
+    // key columns [64 * half, 64 * half + 64) of each tile
+    const int row = 32 * (warp & 3) + lane;
+    const int half = (warp - 2) >> 2;
     if (warp >= 2) {
-        // Q row (+ bias, rounded to T as the reference's add_bias stores it), zeros past the tile
+        // Q row (+ bias, rounded to T as the reference's add_bias stores it), zeros past the tile;
+        // each of the row's two threads writes 4 of its 8 16-byte chunks
         const T* qsrc = static_cast<const T*>(p.q) + (row0 + row) * static_cast<size_t>(p.q_row_stride) +
                         static_cast<size_t>(h) * kPfHeadDim;
         const T* bsrc = p.q_bias != nullptr ? static_cast<const T*>(p.q_bias) + h * kPfHeadDim : nullptr;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int cc = 0; cc < 4; ++cc) {
+            const int c = 4 * half + cc;
             uint4 raw = make_uint4(0u, 0u, 0u, 0u);
             if (row < nq) {
                 raw = __ldg(reinterpret_cast<const uint4*>(qsrc) + c);
@@ -200,71 +225,86 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             constexpr uint32_t IDESC_O = umma_idesc<T>(kPfRows, kPfHeadDim, false, true);
             const uint32_t qa = smem_addr(qbuf);
             const uint32_t pa = smem_addr(pbuf);
-            for (int t = 0; t < ntiles; ++t) {
+            // S(t) = Q . K(t)^T into S buffer t % 2 as soon as K(t) lands; buffer t % 2
+            // last held S(t - 2), which the softmax had read before p_ready(t - 2)
+            auto issue_s = [&](int t) -> bool {
                 const int st = t % kPfStages;
-                if (!mbar_wait_bounded(&kv_full[st], static_cast<uint32_t>(t / kPfStages) & 1u)) {
-                    flag_error(B2_DEVERR_TIMEOUT);
-                    break;
-                }
+                if (!mbar_wait_bounded(&kv_full[st], static_cast<uint32_t>(t / kPfStages) & 1u)) return false;
                 tc_fence_after();
                 const uint32_t ka = smem_addr(kv + st * 2 * kPfTile);
-                const uint32_t va = ka + kPfTile;
 #pragma unroll
                 for (int k = 0; k < kPfHeadDim / 16; ++k)
-                    umma_f16(tmem, sw128_desc(qa + 32 * k, 16, 1024), sw128_desc(ka + 32 * k, 16, 1024), IDESC_S, k > 0);
-                umma_commit(s_full);
+                    umma_f16(tmem + static_cast<uint32_t>((t & 1) * kPfKeys), sw128_desc(qa + 32 * k, 16, 1024),
+                             sw128_desc(ka + 32 * k, 16, 1024), IDESC_S, k > 0);
+                umma_commit(&s_full[t & 1]);
+                return true;
+            };
+            bool ok = issue_s(0);
+            for (int t = 0; ok && t < ntiles; ++t) {
+                if (t + 1 < ntiles && !(ok = issue_s(t + 1))) break;  // overlaps the softmax of tile t
                 if (!mbar_wait_bounded(p_ready, static_cast<uint32_t>(t) & 1u)) {
-                    flag_error(B2_DEVERR_TIMEOUT);
+                    ok = false;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t va = smem_addr(kv + (t % kPfStages) * 2 * kPfTile) + kPfTile;
 #pragma unroll
                 for (int kk = 0; kk < kPfKeys / 16; ++kk) {
                     const uint32_t po = static_cast<uint32_t>((kk >> 2) * kPfRows * 128 + (kk & 3) * 32);
                     const uint64_t vd = sw128_desc(va + static_cast<uint32_t>(kk) * 2048u, kPfTile, 1024);
-                    umma_f16(tmem + 128u, sw128_desc(pa + po, 16, 1024), vd, IDESC_O, t > 0 || kk > 0);
-                    umma_f16(tmem + 128u, sw128_desc(pa + 2 * kPfRows * 128 + po, 16, 1024), vd, IDESC_O, true);
+                    umma_f16(tmem + kPfOCol, sw128_desc(pa + po, 16, 1024), vd, IDESC_O, t > 0 || kk > 0);
+                    umma_f16(tmem + kPfOCol, sw128_desc(pa + 2 * kPfRows * 128 + po, 16, 1024), vd, IDESC_O, true);
                 }
                 umma_commit(o_done);
-                umma_commit(&kv_empty[st]);
+                umma_commit(&kv_empty[t % kPfStages]);
             }
+            if (!ok) flag_error(B2_DEVERR_TIMEOUT);
         }
     } else {
         // ================================================= softmax / epilogue
+        constexpr int NS = kPfSoftmax;
         const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-        const uint32_t s_addr = tmem + lane_base;
-        const uint32_t o_addr = tmem + lane_base + 128u;
+        const uint32_t s_base = tmem + lane_base + static_cast<uint32_t>(64 * half);
+        const uint32_t o_addr = tmem + lane_base + kPfOCol + static_cast<uint32_t>(32 * half);
+        float* red = reinterpret_cast<float*>(smem + PfLayout::off_red);  // [half][row]
         const bool valid = row < nq;
         const int qpos = pre + i0 + row;
-        float m_ref = -INFINITY, l = 0.0f;
+        float m_ref = -INFINITY, l = 0.0f;  // l: this thread's share of the row sum
         bool ok = true;
-        int t = 0;
-        for (; t < ntiles; ++t) {
-            ok = mbar_wait_bounded(s_full, static_cast<uint32_t>(t) & 1u);
-            if (named_sync_or(1, kPfThreads - 64, !ok)) {
+        for (int t = 0; t < ntiles; ++t) {
+            ok = mbar_wait_bounded(&s_full[t & 1], static_cast<uint32_t>(t >> 1) & 1u);
+            if (named_sync_or(1, NS, !ok)) {
                 if (!ok) flag_error(B2_DEVERR_TIMEOUT);
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int kbase = t * kPfKeys;
-            // pass 1: the row maximum over the keys this row may see
-            float mx = -INFINITY;
-            for (int c0 = 0; c0 < kPfKeys; c0 += 32) {
+            const uint32_t s_addr = s_base + static_cast<uint32_t>((t & 1) * kPfKeys);
+            const int kbase = t * kPfKeys + 64 * half;  // position of this thread's first key
+            // pass 1: the maximum over this thread's visible keys, combined with the other half's
+            float mxs[8];  // independent partial maxima (no 64-long dependency chain)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mxs[e] = -INFINITY;
+#pragma unroll
+            for (int c0 = 0; c0 < 64; c0 += 32) {
                 float v[32];
                 tmem_ld32(s_addr + static_cast<uint32_t>(c0), v);
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                    if (valid && kbase + c0 + j <= qpos) mx = fmaxf(mx, v[j] * p.scale_log2);
+                    if (valid && kbase + c0 + j <= qpos) mxs[j & 7] = fmaxf(mxs[j & 7], v[j] * p.scale_log2);
             }
+            float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+            red[half * kPfRows + row] = mx;
             // PV(t-1) must have finished before O is rescaled and P is overwritten
             if (t > 0) ok = mbar_wait_bounded(o_done, static_cast<uint32_t>(t - 1) & 1u);
-            if (named_sync_or(2, kPfThreads - 64, !ok)) {
+            if (named_sync_or(2, NS, !ok)) {
                 if (!ok) flag_error(B2_DEVERR_TIMEOUT);
                 ok = false;
                 break;
             }
             tc_fence_after();
+            mx = fmaxf(mx, red[(half ^ 1) * kPfRows + row]);
             // move the reference maximum (always on a row's first keys, which are in
             // tile 0: key 0 is visible to every row); O rows are rescaled by all
             // threads together when any row moved (tcgen05.ld/st are warp-wide)
@@ -275,19 +315,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 l *= corr;
                 m_ref = mx;
             }
-            if (named_sync_or(4, kPfThreads - 64, need) && t > 0) {
+            if (named_sync_or(4, NS, need) && t > 0) {
+                float o[32];
+                tmem_ld32(o_addr, o);
 #pragma unroll
-                for (int c0 = 0; c0 < kPfHeadDim; c0 += 32) {
-                    float o[32];
-                    tmem_ld32(o_addr + static_cast<uint32_t>(c0), o);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) o[j] *= corr;
-                    tmem_st32(o_addr + static_cast<uint32_t>(c0), o);
-                }
+                for (int j = 0; j < 32; ++j) o[j] *= corr;
+                tmem_st32(o_addr, o);
                 tmem_wait_st();
             }
-            // pass 2: weights, split into two 16-bit halves, into P (K-major, 2 key atoms)
-            for (int c0 = 0; c0 < kPfKeys; c0 += 32) {
+            // pass 2: weights, split into two 16-bit halves, into P (K-major; this
+            // thread's 64 keys are exactly one 64-key atom of the tile)
+            unsigned char* p_hi = pbuf + half * kPfRows * 128;
+            unsigned char* p_lo = p_hi + 2 * kPfRows * 128;
+            float ls[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // partial sums
+#pragma unroll
+            for (int c0 = 0; c0 < 64; c0 += 32) {
                 float v[32];
                 tmem_ld32(s_addr + static_cast<uint32_t>(c0), v);
 #pragma unroll
@@ -296,18 +338,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const int kp = kbase + c0 + j + e;
-                        const float pw = (valid && kp <= qpos) ? exp2f(v[j + e] * p.scale_log2 - m_ref) : 0.0f;
-                        l += pw;
+                        const float pw = (valid && kp <= qpos) ? ex2_approx(v[j + e] * p.scale_log2 - m_ref) : 0.0f;
+                        ls[e] += pw;
                         hi[e] = Elem<T>::to_f(Elem<T>::from_f(pw));
                         lo[e] = pw - hi[e];
                     }
-                    const int key = c0 + j;  // 8 keys = one 16-byte chunk of the row
-                    const uint32_t off = static_cast<uint32_t>((key >> 6) * kPfRows * 128) + sw128_offset(row, key & 63, 2);
-                    *reinterpret_cast<uint4*>(pbuf + off) = pack16<T>(hi);
-                    *reinterpret_cast<uint4*>(pbuf + 2 * kPfRows * 128 + off) = pack16<T>(lo);
+                    const uint32_t off = sw128_offset(row, c0 + j, 2);
+                    *reinterpret_cast<uint4*>(p_hi + off) = pack16<T>(hi);
+                    *reinterpret_cast<uint4*>(p_lo + off) = pack16<T>(lo);
                 }
             }
-            if (t == ntiles - 1 && kbase + row >= kv_end) {
+            l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+            if (t == ntiles - 1 && half == 0 && t * kPfKeys + row >= kv_end) {
                 // key row past the keys in use: zero its V (P is 0 there; V may be stale)
                 uint4* vrow = reinterpret_cast<uint4*>(kv + (t % kPfStages) * 2 * kPfTile + kPfTile + row * 128);
 #pragma unroll
@@ -315,28 +357,28 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             fence_proxy_async_smem();  // P and the zeroed V rows are read by the tensor core
             tc_fence_before();
-            named_sync(3, kPfThreads - 64);
+            named_sync(3, NS);
             if (tid == 64) mbar_arrive(p_ready);
         }
-        // ---- O / l for the tile's rows (every lane loads: tcgen05.ld is warp-wide)
+        // ---- O / l for the tile's rows; each thread stores its 32 of the 64 dims
+        // (every lane loads: tcgen05.ld is warp-wide)
+        red[half * kPfRows + row] = l;
         bool fin = ok && mbar_wait_bounded(o_done, static_cast<uint32_t>(ntiles - 1) & 1u);
-        if (!named_sync_or(5, kPfThreads - 64, !fin)) {
+        if (!named_sync_or(5, NS, !fin)) {
             tc_fence_after();
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const float lt = l + red[(half ^ 1) * kPfRows + row];
+            const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
             T* dst = static_cast<T*>(p.out) + (row0 + row) * static_cast<size_t>(p.out_row_stride) +
-                     static_cast<size_t>(h) * kPfHeadDim;
+                     static_cast<size_t>(h) * kPfHeadDim + 32 * half;
+            float o[32];
+            tmem_ld32(o_addr, o);
+            if (valid) {
 #pragma unroll
-            for (int c0 = 0; c0 < kPfHeadDim; c0 += 32) {
-                float o[32];
-                tmem_ld32(o_addr + static_cast<uint32_t>(c0), o);
-                if (valid) {
+                for (int j = 0; j < 32; j += 8) {
+                    float f[8];
 #pragma unroll
-                    for (int j = 0; j < 32; j += 8) {
-                        float f[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) f[e] = o[j + e] * inv;
-                        *reinterpret_cast<uint4*>(dst + c0 + j) = pack16<T>(f);
-                    }
+                    for (int e = 0; e < 8; ++e) f[e] = o[j + e] * inv;
+                    *reinterpret_cast<uint4*>(dst + j) = pack16<T>(f);
                 }
             }
         } else if (ok) {
