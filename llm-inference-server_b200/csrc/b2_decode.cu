@@ -213,7 +213,7 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     for (int cps : {2, 1}) {
         const int smem_cap = cps == 1 ? di.max_smem_optin : di.smem_per_sm / cps - 1024;
         const int thread_cap = cps == 1 ? maxt : 256;
-        for (int k : {4, 2, 1}) {
+        for (int k : {4, 3, 2, 1}) {  // token subgroups: more consumer warps to hide latency
             const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * C, 32));
             if (ncons + 64 > thread_cap) continue;  // + producer warp + bookkeeping warp
             if (k > 1 && k * C > 512) continue;  // enough warps
