@@ -72,6 +72,11 @@ WORKLOADS = {
     "mha": Workload("mha", 64, 12, 12, 64, "f16", 128, 1024, False, 16, 65536, "paged_decode_microbench.md",
                     "paged-attention decode microbench: batch 64 per GPU, 12 heads, head_dim 64, fp16 K/V and q "
                     "N(0,1), context U[128,1024], block 16, random permutation of a 65536-block pool, scale 1/8"),
+    "mha-medium": Workload("mha-medium", 128, 16, 16, 64, "f16", 32, 1024, False, 16, 81920,
+                           "paged_decode_medium_heads.md",
+                           "paged-attention decode at the GPT-2 medium engine's shape: batch 128 per GPU, 16 heads, "
+                           "head_dim 64, fp16 K/V and q N(0,1), context U[32,1024], block 16, random permutation of "
+                           "an 81920-block pool, scale 1/8"),
     "gqa": Workload("gqa", 256, 32, 8, 128, "bf16", 512, 32768, True, 1, 140000, "paged_decode_tc_gqa.md",
                     "grouped-query paged-attention decode: batch 256 per GPU, 32 query / 8 kv heads, head_dim 128, "
                     "bf16 K/V and q N(0,1), context log-uniform [512,32768], block 16, random permutation of a "

@@ -580,7 +580,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
 #pragma unroll
                     for (int j = 0; j < TB; ++j)
                         if (j < cnt) mx = fmaxf(mx, s[j][g]);
-                    const float corr = exp2f(m_run[g] - mx);  // 0 on the first batch (m_run = -inf)
+                    const float corr = ex2_approx(m_run[g] - mx);  // 0 on the first batch (m_run = -inf)
                     m_run[g] = mx;
                     l_run[g] *= corr;
 #pragma unroll
@@ -592,7 +592,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                         const uint4 vraw = ld_shared16(V + ((t0 + j * ks) * C + c) * 16);
 #pragma unroll
                         for (int g = 0; g < QG; ++g) {
-                            const float pw = exp2f(s[j][g] - m_run[g]);
+                            const float pw = ex2_approx(s[j][g] - m_run[g]);
                             l_run[g] += pw;
                             axpy16<T>(pw, vraw, acc[g]);
                         }

@@ -310,6 +310,16 @@ __device__ __forceinline__ uint4 ld_shared16(const void* p) { return *reinterpre
 // consistent fence __threadfence() issues).
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// 2^x by the SFU in one instruction (ex2.approx.ftz: relative error ~2^-22;
+// -inf gives 0).  The softmax weights and rescale factors of the attention
+// kernels use it: the error is far below their 16-bit inputs' resolution and
+// the 2e-3 output bar.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Programmatic dependent launch.  launch_dependents lets the next kernel on
 // the stream start its prologue; pdl_wait blocks until the previous kernel
 // has completed and its writes are visible (a no-op when the launch had no

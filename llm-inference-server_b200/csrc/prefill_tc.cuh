@@ -80,14 +80,6 @@ struct PfLayout {
     static constexpr int bytes = off_tmem + 16 + 1024;
 };
 
-// 2^x by the SFU (ex2.approx.ftz: relative error ~2^-22, far below the 16
-// bits the hi/lo split of a weight keeps; inputs here are <= 8).
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 #pragma unroll
     for (int i = 0; i < 32; i += 8) tmem_st8(taddr + static_cast<uint32_t>(i), v + i);
