@@ -18,9 +18,9 @@
 //    async copies (cp.async.bulk, the TMA engine's untiled path) into a ring
 //    of shared-memory stages guarded by mbarriers; q rows travel the same way
 //    at a segment's first block.  Consumer warps never read K/V from global memory.
-//  * Math.  Consumer thread (ts, c) owns 16-byte chunk c of the token row
-//    (kv head c / GL, dims (c % GL) * E ...) and the tokens t = ts (mod k) of
-//    every block.  The GL lanes that share a head row form a group that
+//  * Math.  Consumer thread (ts, c) owns one or two consecutive 16-byte
+//    chunks of the token row (two for 16-bit types) and the tokens
+//    t = ts (mod k) of every block.  The lanes that share a head row form a group that
 //    reduces q.k with xor shuffles (16-bit operands go straight into fp32
 //    FMAs, see dot16) and keeps that head's online-softmax state (m, l) and
 //    its slice of the accumulator in registers, rescaling once per batch of
@@ -237,7 +237,7 @@ __device__ __forceinline__ unsigned count_piece(unsigned* counter) {
 // one entry per finished sequence piece.
 constexpr int kPieceRing = 8;
 
-template <typename T, int DH, int QG, int MAXT, typename OutT>
+template <typename T, int DH, int QG, int MAXT, typename OutT, int CPT>
 __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams p) {
     constexpr int E = Elem<T>::kPer16B;
     constexpr int GL = DH / E;  // lanes sharing one head row
@@ -483,26 +483,37 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     }
 
     // ===================================================== consumer threads
+    // Thread (ts, ct) of the CT = Hkv * GLT per token subgroup holds CPT
+    // consecutive 16-byte chunks of one head row.  Two (16-bit types, up to two
+    // query heads per kv head; more would spill) mean fewer shuffle levels and
+    // the softmax bookkeeping each lane of a head repeats spread over half as
+    // many lanes -- the planner picks them for the one-CTA-per-SM (wide head)
+    // shapes, where the consumers' instruction count limits the stream.
+    static_assert(CPT == 1 || (CPT == 2 && ES == 2 && QG <= 2), "chunks per consumer thread");
+    constexpr int GLT = GL / CPT;  // lanes sharing one head row
+    const int CT = Hkv * GLT;
     const int ks = p.ksplit;
-    const int ts = tid / C;
-    const int c = tid - ts * C;
+    const int ts = tid / CT;
+    const int ct = tid - ts * CT;
     const bool active = ts < ks;
-    const int hk = c / GL;
-    const int dg = c - hk * GL;
+    const int hk = ct / GLT;
+    const int dgt = ct - hk * GLT;
+    const int c0 = hk * GL + dgt * CPT;  // this thread's first chunk of the token row
     const int lane = tid & 31;
-    const unsigned gmask = (GL == 32) ? 0xffffffffu : (((1u << GL) - 1u) << (lane & ~(GL - 1)));
+    const unsigned gmask = (GLT == 32) ? 0xffffffffu : (((1u << GLT) - 1u) << (lane & ~(GLT - 1)));
 
-    uint4 qraw[QG];  // this thread's q chunks, in the storage dtype (bias added)
-    float acc[QG][E];
+    uint4 qraw[QG][CPT];  // this thread's q chunks, in the storage dtype (bias added)
+    float acc[QG][CPT * E];
     float m_run[QG];
     float l_run[QG];
 #pragma unroll
     for (int g = 0; g < QG; ++g) {
-        qraw[g] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) qraw[g][i] = make_uint4(0u, 0u, 0u, 0u);
         m_run[g] = -INFINITY;
         l_run[g] = 0.0f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[g][e] = 0.0f;
+        for (int e = 0; e < CPT * E; ++e) acc[g][e] = 0.0f;
     }
     const float scale_log2 = p.scale_log2;
 
@@ -529,21 +540,24 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 const unsigned char* qs = stage + 2 * p.slab_bytes;
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
-                    qraw[g] = ld_shared16(qs + ((hk * QG + g) * DH + dg * E) * ES);
-                    if (p.q_bias != nullptr) {
-                        // q + bias rounded to T, as the reference's separate
-                        // add_bias launch stores it (engine.cu:158).
-                        float f[E], bf[E];
-                        unpack16<T>(qraw[g], f);
-                        unpack16<T>(__ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.q_bias) +
-                                                                         (hk * QG + g) * DH + dg * E)),
-                                    bf);
 #pragma unroll
-                        for (int e = 0; e < E; ++e) f[e] = __fadd_rn(f[e], bf[e]);
-                        qraw[g] = pack16<T>(f);
+                    for (int i = 0; i < CPT; ++i) {
+                        const int dofs = (hk * QG + g) * DH + (dgt * CPT + i) * E;  // element offset in the q row
+                        qraw[g][i] = ld_shared16(qs + dofs * ES);
+                        if (p.q_bias != nullptr) {
+                            // q + bias rounded to T, as the reference's separate
+                            // add_bias launch stores it (engine.cu:158).
+                            float f[E], bf[E];
+                            unpack16<T>(qraw[g][i], f);
+                            unpack16<T>(__ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(p.q_bias) + dofs)),
+                                        bf);
+#pragma unroll
+                            for (int e = 0; e < E; ++e) f[e] = __fadd_rn(f[e], bf[e]);
+                            qraw[g][i] = pack16<T>(f);
+                        }
                     }
 #pragma unroll
-                    for (int e = 0; e < E; ++e) acc[g][e] = 0.0f;
+                    for (int e = 0; e < CPT * E; ++e) acc[g][e] = 0.0f;
                     m_run[g] = -INFINITY;
                     l_run[g] = 0.0f;
                 }
@@ -556,16 +570,24 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
 #pragma unroll
                 for (int j = 0; j < TB; ++j) {
                     if (j < cnt) {
-                        const uint4 kraw = ld_shared16(K + ((t0 + j * ks) * C + c) * 16);
+                        const unsigned char* krow = K + ((t0 + j * ks) * C + c0) * 16;
+                        uint4 kraw[CPT];
 #pragma unroll
-                        for (int g = 0; g < QG; ++g) s[j][g] = dot16<T>(qraw[g], kraw, 0.0f);
+                        for (int i = 0; i < CPT; ++i) kraw[i] = ld_shared16(krow + i * 16);
+#pragma unroll
+                        for (int g = 0; g < QG; ++g) {
+                            float d = dot16<T>(qraw[g][0], kraw[0], 0.0f);
+#pragma unroll
+                            for (int i = 1; i < CPT; ++i) d += dot16<T>(qraw[g][i], kraw[i], 0.0f);
+                            s[j][g] = d;
+                        }
                     } else {
 #pragma unroll
                         for (int g = 0; g < QG; ++g) s[j][g] = 0.0f;
                     }
                 }
 #pragma unroll
-                for (int off = GL / 2; off > 0; off >>= 1)
+                for (int off = GLT / 2; off > 0; off >>= 1)
 #pragma unroll
                     for (int j = 0; j < TB; ++j)
 #pragma unroll
@@ -584,17 +606,21 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                     m_run[g] = mx;
                     l_run[g] *= corr;
 #pragma unroll
-                    for (int e = 0; e < E; ++e) acc[g][e] *= corr;
+                    for (int e = 0; e < CPT * E; ++e) acc[g][e] *= corr;
                 }
 #pragma unroll
                 for (int j = 0; j < TB; ++j) {
                     if (j < cnt) {
-                        const uint4 vraw = ld_shared16(V + ((t0 + j * ks) * C + c) * 16);
+                        const unsigned char* vrow = V + ((t0 + j * ks) * C + c0) * 16;
+                        uint4 vraw[CPT];
+#pragma unroll
+                        for (int i = 0; i < CPT; ++i) vraw[i] = ld_shared16(vrow + i * 16);
 #pragma unroll
                         for (int g = 0; g < QG; ++g) {
                             const float pw = ex2_approx(s[j][g] - m_run[g]);
                             l_run[g] += pw;
-                            axpy16<T>(pw, vraw, acc[g]);
+#pragma unroll
+                            for (int i = 0; i < CPT; ++i) axpy16<T>(pw, vraw[i], acc[g] + i * E);
                         }
                     }
                 }
@@ -613,12 +639,12 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
                     const int h = hk * QG + g;
-                    float* dst = p.part_acc + (slot * H + h) * DH + dg * E;
+                    float* dst = p.part_acc + (slot * H + h) * DH + dgt * CPT * E;
 #pragma unroll
-                    for (int e = 0; e < E; e += 4)
+                    for (int e = 0; e < CPT * E; e += 4)
                         __stcg(reinterpret_cast<float4*>(dst + e),
                                make_float4(acc[g][e], acc[g][e + 1], acc[g][e + 2], acc[g][e + 3]));
-                    if (dg == 0) __stcg(p.part_ml + slot * H + h, make_float2(m_run[g], l_run[g]));
+                    if (dgt == 0) __stcg(p.part_ml + slot * H + h, make_float2(m_run[g], l_run[g]));
                 }
             }
             // Hand the piece to the bookkeeping warp (ring slot npieces % R):

@@ -107,6 +107,7 @@ struct AttnPlan {
     int combine_threads = 0;
     bool tensor_cores = false;  // paged_decode_tc_kernel instead of paged_decode_kernel
     int tc_stages = 0;
+    int cpt = 1;  // paged_decode_kernel: 16-byte chunks per consumer thread
     AttnParams prm{};
     // workspace: [piece counters][seq_info][(m, l) partials][acc partials]
     size_t ws_cnt = 0, ws_info = 0, ws_ml = 0, ws_acc = 0, ws_total = 0;
@@ -209,31 +210,38 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     // Two CTAs per SM when each still gets a double-buffered ring: one CTA's
     // prologue and tail then overlap the other's streaming.  The 128-register
     // cap limits a co-resident pair to 256 threads each.
-    int best_k = 0, best_s = 0, best_cps = 0;
+    int best_k = 0, best_s = 0, best_cps = 0, best_cpt = 1;
     for (int cps : {2, 1}) {
+        // one CTA per SM (wide heads): two chunks per consumer thread (16-bit,
+        // up to two query heads per kv head); consumer threads per subgroup CT
+        const int cpt = (cps == 1 && es == 2 && H / a->n_kv_head <= 2) ? 2 : 1;
+        const int CT = C / cpt;
         const int smem_cap = cps == 1 ? di.max_smem_optin : di.smem_per_sm / cps - 1024;
         const int thread_cap = cps == 1 ? maxt : 256;
-        for (int k : {4, 3, 2, 1}) {  // token subgroups: more consumer warps to hide latency
-            const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * C, 32));
+        for (int k : {8, 6, 4, 3, 2, 1}) {  // token subgroups: more consumer warps to hide latency
+            const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * CT, 32));
             if (ncons + 64 > thread_cap) continue;  // + producer warp + bookkeeping warp
-            if (k > 1 && k * C > 512) continue;  // enough warps
+            if (k > 1 && k * CT > 512) continue;  // enough warps
             int s = (smem_cap - kMiscBytes - 512) / stage;  // 512: barriers + alignment padding
             if (s > 8) s = 8;
             if (s < 2) continue;
             best_k = k;
             best_s = s;
             best_cps = cps;
+            best_cpt = cpt;
             break;
         }
         if (best_k != 0) break;
     }
     if (best_k == 0) return fail(B2_ERR_UNSUPPORTED, "head shape does not fit the decode kernel's shared memory");
-    if (a->batch > 16 * (static_cast<int>(align_up(static_cast<size_t>(best_k) * C, 32)) + 32))
+    const int CT = C / best_cpt;
+    pl->cpt = best_cpt;
+    if (a->batch > 16 * (static_cast<int>(align_up(static_cast<size_t>(best_k) * CT, 32)) + 32))
         return fail(B2_ERR_UNSUPPORTED, "batch too large for one launch");
 
     AttnParams& p = pl->prm;
     p.ksplit = best_k;
-    p.ncons = static_cast<int>(align_up(static_cast<size_t>(best_k) * C, 32));
+    p.ncons = static_cast<int>(align_up(static_cast<size_t>(best_k) * CT, 32));
     p.stages = best_s;
     p.stage_bytes = stage;
     p.slab_bytes = slab;
@@ -343,10 +351,10 @@ int launch_tc(const AttnPlan& pl, const TcParams& tp, const CUtensorMap& map, in
     return fail(B2_ERR_UNSUPPORTED, "no tensor-core kernel for this head shape");
 }
 
-template <typename T, int DH, int QG, typename OutT>
-int launch_attn_o(const AttnPlan& pl, cudaStream_t stream) {
+template <typename T, int DH, int QG, typename OutT, int CPT>
+int launch_attn_c(const AttnPlan& pl, cudaStream_t stream) {
     constexpr int MAXT = kAttnMaxThreads;
-    auto kern = paged_decode_kernel<T, DH, QG, MAXT, OutT>;
+    auto kern = paged_decode_kernel<T, DH, QG, MAXT, OutT, CPT>;
     static std::atomic<uint64_t> smem_set{0};  // one flag word per instantiation
     int dev = -1;
     const DeviceInfo di = device_info(&dev);
@@ -354,6 +362,14 @@ int launch_attn_o(const AttnPlan& pl, cudaStream_t stream) {
     if (rc != B2_OK) return rc;
     return launch_pdl(kern, dim3(static_cast<unsigned>(pl.grid)), dim3(static_cast<unsigned>(pl.threads)), pl.smem,
                       stream, pl.prm);
+}
+
+template <typename T, int DH, int QG, typename OutT>
+int launch_attn_o(const AttnPlan& pl, cudaStream_t stream) {
+    if constexpr (sizeof(T) == 2 && QG <= 2) {
+        if (pl.cpt == 2) return launch_attn_c<T, DH, QG, OutT, 2>(pl, stream);
+    }
+    return launch_attn_c<T, DH, QG, OutT, 1>(pl, stream);
 }
 
 // out_dtype is F32, or the input dtype (checked by check_attn_args).
