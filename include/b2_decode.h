@@ -183,6 +183,37 @@ B2_API int b2_paged_attention(const B2PagedAttnArgs* args, void* workspace, size
                               b2_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * One synchronous decode-attention call from host buffers.
+ * Replaces the host side of one decode step around the attention launch in
+ * Engine::decode_step (gpu-engine/src/engine.cu:343-368): upload the step's
+ * inputs with cudaMemcpyAsync, launch, download the output, synchronise.
+ *
+ * Copies io->q, io->block_tables and io->seq_lens (each optional: NULL skips
+ * that upload) into args->q, args->block_tables and args->seq_lens, runs
+ * b2_paged_attention on `stream`, copies args->out into io->out (optional),
+ * and waits for the stream.  Uploads whose host AND device ranges are both
+ * back to back (q, then block tables, then seq_lens at the same offsets in one
+ * host and one device allocation) go as one copy.  Host buffers should be
+ * pinned (page-locked); pageable memory works but copies synchronously.
+ * When io->out is page-locked memory mapped into the device's address space
+ * (cudaHostAlloc / cudaHostRegister memory on a unified-addressing system)
+ * and 16-byte aligned, the kernel stores the output into it directly (the
+ * PCIe writes overlap the kernel) and args->out is not written.
+ * Byte counts: q ((batch-1)*q_row_stride + n_head*head_dim) elements of
+ * dtype; block tables batch*max_blocks_per_seq int32; seq_lens batch int32;
+ * out batch*n_head*head_dim elements of out_dtype.
+ * ---------------------------------------------------------------------- */
+typedef struct B2AttnHostIO {
+    const void* q;
+    const int32_t* block_tables;
+    const int32_t* seq_lens;
+    void* out;
+} B2AttnHostIO;
+
+B2_API int b2_paged_attention_host(const B2PagedAttnArgs* args, const B2AttnHostIO* io, void* workspace,
+                                   size_t workspace_bytes, b2_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Paged decode attention whose output is all-gathered in its epilogue.
  * No counterpart in the reference (its engine is single-GPU).  For
  * head-sharded decode: a rank computes attention for its own heads and stores

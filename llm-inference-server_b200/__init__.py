@@ -33,7 +33,7 @@ DECODE_SYMBOLS = (
     "b2_paged_attention_workspace_bytes", "b2_paged_attention",
     "b2_add_layernorm", "b2_bias_gelu", "b2_add_bias", "b2_add_one", "b2_embedding", "b2_argmax",
     "b2_paged_attention_noalloc", "b2_argmax_rows", "b2_paged_attention_gather", "b2_tp_barrier",
-    "b2_tp_epoch_bump", "b2_linear", "b2_prefill_attention",
+    "b2_tp_epoch_bump", "b2_linear", "b2_prefill_attention", "b2_paged_attention_host",
 )
 
 _c_int, _c_float, _vp = ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
@@ -53,6 +53,10 @@ class PagedAttnArgs(ctypes.Structure):
                 ("n_head", _c_int), ("n_kv_head", _c_int), ("head_dim", _c_int), ("max_blocks_per_seq", _c_int),
                 ("layer_idx", _c_int), ("n_layer", _c_int), ("num_blocks", _c_int), ("scale", _c_float),
                 ("flags", _c_int), ("max_ctas", _c_int)]
+
+
+class AttnHostIO(ctypes.Structure):
+    _fields_ = [("q", _vp), ("block_tables", _vp), ("seq_lens", _vp), ("out", _vp)]
 
 
 class LinearArgs(ctypes.Structure):
@@ -98,6 +102,8 @@ def load() -> ctypes.CDLL:
     lib.b2_paged_attention_workspace_bytes.argtypes = [ctypes.POINTER(PagedAttnArgs)]
     lib.b2_paged_attention_workspace_bytes.restype = ctypes.c_size_t
     lib.b2_paged_attention.argtypes = [ctypes.POINTER(PagedAttnArgs), _vp, ctypes.c_size_t, _vp]
+    lib.b2_paged_attention_host.argtypes = [ctypes.POINTER(PagedAttnArgs), ctypes.POINTER(AttnHostIO), _vp,
+                                            ctypes.c_size_t, _vp]
     lib.b2_add_layernorm.argtypes = [_c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp]
     lib.b2_bias_gelu.argtypes = [_c_int, _vp, _vp, _vp, _c_int, _c_int, _vp]
     lib.b2_add_bias.argtypes = [_c_int, _vp, _vp, _vp, _c_int, _c_int, _vp]
@@ -176,6 +182,17 @@ def attention_workspace(args: PagedAttnArgs):
 def paged_attention(args: PagedAttnArgs, workspace, stream=None) -> None:
     """kernels::launch_paged_attention (kernels.h:67-87) with the C-ABI's argument struct."""
     _check(load().b2_paged_attention(ctypes.byref(args), workspace.data_ptr(), workspace.numel(), _stream(stream)))
+
+
+def paged_attention_host(args: PagedAttnArgs, workspace, *, q=None, block_tables=None, seq_lens=None, out=None,
+                         stream=None) -> None:
+    """One synchronous attention call from host buffers (pinned torch CPU
+    tensors or None): upload q / block_tables / seq_lens into the device
+    arrays args names, launch, download args.out into `out`, wait -- the host
+    side of Engine::decode_step (engine.cu:343-368) around one attention."""
+    io = AttnHostIO(_ptr(q), _ptr(block_tables), _ptr(seq_lens), _ptr(out))
+    _check(load().b2_paged_attention_host(ctypes.byref(args), ctypes.byref(io), workspace.data_ptr(),
+                                          workspace.numel(), _stream(stream)))
 
 
 def add_layernorm(out, residual_out, x, residual_in, gamma, beta, eps, bias=None, stream=None):

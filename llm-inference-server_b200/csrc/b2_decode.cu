@@ -624,6 +624,75 @@ int b2_paged_attention_gather(const B2PagedAttnArgs* a, void* ws, size_t ws_byte
     return b2::paged_attention_impl(a, ws, ws_bytes, gather, stream);
 }
 
+int b2_paged_attention_host(const B2PagedAttnArgs* a, const B2AttnHostIO* io, void* ws, size_t ws_bytes,
+                            b2_stream_t stream) {
+    using namespace b2;
+    if (io == nullptr) return fail(B2_ERR_NULL, "io is NULL");
+    int rc = check_attn_args(a);
+    if (rc != B2_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    struct Up {
+        char* dst;
+        const char* src;
+        size_t bytes;
+    } up[3];
+    int n = 0;
+    if (a->batch > 0) {
+        const size_t es = static_cast<size_t>(dtype_size(a->dtype));
+        const size_t qn = static_cast<size_t>(a->batch - 1) * a->q_row_stride + static_cast<size_t>(a->n_head) * a->head_dim;
+        if (io->q) up[n++] = {static_cast<char*>(const_cast<void*>(a->q)), static_cast<const char*>(io->q), qn * es};
+        if (io->block_tables)
+            up[n++] = {reinterpret_cast<char*>(const_cast<int32_t*>(a->block_tables)),
+                       reinterpret_cast<const char*>(io->block_tables),
+                       static_cast<size_t>(a->batch) * a->max_blocks_per_seq * sizeof(int32_t)};
+        if (io->seq_lens)
+            up[n++] = {reinterpret_cast<char*>(const_cast<int32_t*>(a->seq_lens)),
+                       reinterpret_cast<const char*>(io->seq_lens), static_cast<size_t>(a->batch) * sizeof(int32_t)};
+    }
+    // One copy per run of uploads that are contiguous on both sides.
+    for (int i = 0; i < n;) {
+        Up c = up[i++];
+        while (i < n && up[i].dst == c.dst + c.bytes && up[i].src == c.src + c.bytes) c.bytes += up[i++].bytes;
+        const cudaError_t e = cudaMemcpyAsync(c.dst, c.src, c.bytes, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(static_cast<int>(e), cudaGetErrorString(e));
+        }
+    }
+    // Output straight into the caller's buffer when it is page-locked host
+    // memory mapped into the device's address space: the stores cross PCIe
+    // while the kernel runs instead of in a copy after it.
+    void* mapped_out = nullptr;
+    if (io->out) {
+        cudaPointerAttributes pa;
+        if (cudaPointerGetAttributes(&pa, io->out) == cudaSuccess && pa.type == cudaMemoryTypeHost)
+            mapped_out = pa.devicePointer;
+        cudaGetLastError();
+    }
+    if (mapped_out != nullptr && aligned16(mapped_out)) {
+        B2PagedAttnArgs direct = *a;
+        direct.out = mapped_out;
+        rc = paged_attention_impl(&direct, ws, ws_bytes, nullptr, s);
+        if (rc != B2_OK) return rc;
+        const cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return fail(static_cast<int>(e), cudaGetErrorString(e));
+        return B2_OK;
+    }
+    rc = paged_attention_impl(a, ws, ws_bytes, nullptr, s);
+    if (rc != B2_OK) return rc;
+    if (io->out && a->batch > 0) {
+        const size_t out_bytes = static_cast<size_t>(a->batch) * a->n_head * a->head_dim * dtype_size(a->out_dtype);
+        const cudaError_t e = cudaMemcpyAsync(io->out, a->out, out_bytes, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(static_cast<int>(e), cudaGetErrorString(e));
+        }
+    }
+    const cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), cudaGetErrorString(e));
+    return B2_OK;
+}
+
 int b2_tp_barrier(uint32_t* local_flags, uint32_t* const* peer_flags, int32_t rank, int32_t n, const uint32_t* epoch,
                   int32_t slot, b2_stream_t stream) {
     if (!local_flags || !peer_flags || !epoch) return fail(B2_ERR_NULL, "local_flags, peer_flags and epoch are required");

@@ -147,6 +147,66 @@ def test_paged_attention_native_output_and_bias(b2, cuda, dt):
     assert np.all(np.abs(got - ref) <= bound)
 
 
+@pytest.mark.parametrize("dt,Dh,H,Hkv,packed", [(O.F16, 64, 12, 12, True), (O.F16, 64, 12, 12, False),
+                                                 (O.BF16, 128, 32, 8, True), (O.F32, 64, 8, 4, False)])
+def test_paged_attention_host_buffers(b2, cuda, dt, Dh, H, Hkv, packed):
+    """b2_paged_attention_host: uploads from pinned host memory (one copy when
+    q | block tables | seq_lens are back to back on both sides), launch,
+    output to the host (stored by the kernel into pinned memory, or copied into
+    pageable memory), sync -- two calls with different inputs through the same
+    device buffers, each against the oracle."""
+    torch = _torch()
+    rng = np.random.Generator(np.random.PCG64(11 + Dh + H))
+    L, layer, B = 2, 1, 9
+    ctx_a = rng.integers(1, 700, size=B).tolist()
+    ctx_b = rng.integers(1, 700, size=B).tolist()
+    ctx_b[0] = 0
+    pool, _, mbps, nb = make_paged(rng, dt, [max(a, b) for a, b in zip(ctx_a, ctx_b)], Hkv, Dh, L)
+    q_stride = 3 * H * Dh  # q inside a fused QKV row: the upload covers (B-1) strides + one row
+    es = 4 if dt == O.F32 else 2
+    qn = (B - 1) * q_stride + H * Dh
+    q_bytes, bt_bytes = qn * es, B * mbps * 4
+    pd = to_dev(dt, pool)
+    if packed:
+        d_in = torch.empty(q_bytes + bt_bytes + 4 * B, dtype=torch.uint8, device="cuda")
+        qd, btd, sld = d_in[:q_bytes], d_in[q_bytes:q_bytes + bt_bytes], d_in[q_bytes + bt_bytes:]
+    else:
+        qd = torch.empty(q_bytes, dtype=torch.uint8, device="cuda")
+        btd = torch.empty(bt_bytes, dtype=torch.uint8, device="cuda")
+        sld = torch.empty(4 * B, dtype=torch.uint8, device="cuda")
+    out = torch.empty(B, H, Dh, dtype=torch.float32, device="cuda")
+    args = b2.attn_args(qd, q_stride, pd, btd.view(torch.int32).view(B, mbps), sld.view(torch.int32), out,
+                        n_head=H, n_kv_head=Hkv, head_dim=Dh, max_blocks_per_seq=mbps, layer_idx=layer, n_layer=L,
+                        num_blocks=nb)
+    ws = b2.attention_workspace(args)
+    perm = rng.permutation(nb).astype(np.int32)
+    for ctx in (ctx_a, ctx_b):
+        bt = np.full((B, mbps), -1, np.int32)
+        o = 0
+        for i, c in enumerate(ctx):
+            n = (c + 15) // 16
+            bt[i, :n] = perm[o:o + n]
+            o += n
+        q = O.round_to(dt, rng.standard_normal(qn, dtype=np.float32))
+        host = torch.from_numpy(np.concatenate([np.ascontiguousarray(q).view(np.uint8), bt.view(np.uint8).reshape(-1),
+                                                np.asarray(ctx, np.int32).view(np.uint8)])).pin_memory()
+        # pinned (mapped) output: the kernel stores into it; pageable: copied from args.out
+        hout = torch.empty(B, H, Dh, dtype=torch.float32)
+        if packed:
+            hout = hout.pin_memory()
+        b2.paged_attention_host(args, ws, q=host[:q_bytes], block_tables=host[q_bytes:q_bytes + bt_bytes],
+                                seq_lens=host[q_bytes + bt_bytes:], out=hout)
+        got = hout.numpy()  # the call has synchronised: no further sync before reading
+        q_full = np.zeros(B * q_stride, q.dtype)
+        q_full[:qn] = q
+        ref = O.paged_attention(dt, q_full, q_stride, pool, np.where(bt < 0, 0, bt), ctx, n_head=H, n_kv_head=Hkv,
+                                head_dim=Dh, max_blocks_per_seq=mbps, layer_idx=layer, n_layer=L, nthreads=8)
+        tol = 1e-5 if dt == O.F32 else 2e-3
+        assert np.isfinite(got).all()
+        assert float(np.max(np.abs(got - ref))) <= tol
+    assert b2.device_errors() == 0
+
+
 def test_paged_attention_repeat_launches_are_identical(b2, cuda):
     """The merge counters are left at zero, so a reused workspace gives the same bits."""
     rng = np.random.Generator(np.random.PCG64(3))
