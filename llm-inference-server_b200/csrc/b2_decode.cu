@@ -495,17 +495,14 @@ int b2_kv_append(const B2KvAppendArgs* a, b2_stream_t stream) {
     const long long total = static_cast<long long>(a->batch) * 2 * a->n_kv_head * (a->head_dim / E);
     const int grid = static_cast<int>((total + 255) / 256);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (a->dtype == B2_F32) {
-        if (a->head_dim == 64) kv_append_kernel<float, 64><<<grid, 256, 0, s>>>(p);
-        else kv_append_kernel<float, 128><<<grid, 256, 0, s>>>(p);
-    } else if (a->dtype == B2_F16) {
-        if (a->head_dim == 64) kv_append_kernel<__half, 64><<<grid, 256, 0, s>>>(p);
-        else kv_append_kernel<__half, 128><<<grid, 256, 0, s>>>(p);
-    } else {
-        if (a->head_dim == 64) kv_append_kernel<__nv_bfloat16, 64><<<grid, 256, 0, s>>>(p);
-        else kv_append_kernel<__nv_bfloat16, 128><<<grid, 256, 0, s>>>(p);
-    }
-    return launch_status();
+    if (a->dtype == B2_F32)
+        return a->head_dim == 64 ? launch_pdl(kv_append_kernel<float, 64>, grid, 256, 0, s, p)
+                                 : launch_pdl(kv_append_kernel<float, 128>, grid, 256, 0, s, p);
+    if (a->dtype == B2_F16)
+        return a->head_dim == 64 ? launch_pdl(kv_append_kernel<__half, 64>, grid, 256, 0, s, p)
+                                 : launch_pdl(kv_append_kernel<__half, 128>, grid, 256, 0, s, p);
+    return a->head_dim == 64 ? launch_pdl(kv_append_kernel<__nv_bfloat16, 64>, grid, 256, 0, s, p)
+                             : launch_pdl(kv_append_kernel<__nv_bfloat16, 128>, grid, 256, 0, s, p);
 }
 
 // ------------------------------------------------------- paged attention
@@ -778,12 +775,11 @@ int b2_add_layernorm(int32_t dtype, void* out, void* residual_out, const void* x
     if (nch > 4 * 1024) return fail(B2_ERR_UNSUPPORTED, "d_model too large for the one-CTA-per-row kernel");
     const int threads = static_cast<int>(align_up(static_cast<size_t>((nch + per_thread - 1) / per_thread), 32));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define B2_LN_LAUNCH(T, N)                                                                                         \
-    add_layernorm_kernel<T, N><<<batch, threads, 0, s>>>(static_cast<T*>(out), static_cast<T*>(residual_out),    \
-                                                         static_cast<const T*>(x), static_cast<const T*>(bias),     \
-                                                         static_cast<const T*>(residual_in),                        \
-                                                         static_cast<const T*>(gamma), static_cast<const T*>(beta), \
-                                                         d_model, eps)
+#define B2_LN_LAUNCH(T, N)                                                                                   \
+    return launch_pdl(add_layernorm_kernel<T, N>, batch, threads, 0, s, static_cast<T*>(out),                \
+                      static_cast<T*>(residual_out), static_cast<const T*>(x), static_cast<const T*>(bias), \
+                      static_cast<const T*>(residual_in), static_cast<const T*>(gamma),                     \
+                      static_cast<const T*>(beta), static_cast<int>(d_model), eps)
 #define B2_LN_DISPATCH(T)                      \
     if (per_thread == 1) B2_LN_LAUNCH(T, 1);      \
     else if (per_thread == 2) B2_LN_LAUNCH(T, 2); \
@@ -818,16 +814,13 @@ int b2_bias_gelu(int32_t dtype, void* out, const void* x, const void* bias, int3
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int g = row_grid(n);
     if (dtype == B2_F32)
-        bias_gelu_kernel<float><<<g, 256, 0, s>>>(static_cast<float*>(out), static_cast<const float*>(x),
-                                                  static_cast<const float*>(bias), n, rc_chunks);
-    else if (dtype == B2_F16)
-        bias_gelu_kernel<__half><<<g, 256, 0, s>>>(static_cast<__half*>(out), static_cast<const __half*>(x),
-                                                   static_cast<const __half*>(bias), n, rc_chunks);
-    else
-        bias_gelu_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out),
-                                                          static_cast<const __nv_bfloat16*>(x),
-                                                          static_cast<const __nv_bfloat16*>(bias), n, rc_chunks);
-    return launch_status();
+        return launch_pdl(bias_gelu_kernel<float>, g, 256, 0, s, static_cast<float*>(out),
+                          static_cast<const float*>(x), static_cast<const float*>(bias), n, rc_chunks);
+    if (dtype == B2_F16)
+        return launch_pdl(bias_gelu_kernel<__half>, g, 256, 0, s, static_cast<__half*>(out),
+                          static_cast<const __half*>(x), static_cast<const __half*>(bias), n, rc_chunks);
+    return launch_pdl(bias_gelu_kernel<__nv_bfloat16>, g, 256, 0, s, static_cast<__nv_bfloat16*>(out),
+                      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(bias), n, rc_chunks);
 }
 
 int b2_add_bias(int32_t dtype, void* out, const void* x, const void* bias, int32_t batch, int32_t dim,

@@ -49,6 +49,19 @@ __global__ void __launch_bounds__(1024) add_layernorm_kernel(T* out, T* residual
     __shared__ double red[33];
     const int nch = d / E;
     const size_t base = static_cast<size_t>(blockIdx.x) * d;
+    // gamma and beta are weights (nothing on the stream writes them): fetched
+    // before waiting for the kernel that produced x and residual_in.
+    uint4 graw[NCH], braw[NCH];
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+        const int c = threadIdx.x + i * static_cast<int>(blockDim.x);
+        if (c < nch) {
+            graw[i] = __ldg(reinterpret_cast<const uint4*>(gamma) + c);
+            braw[i] = __ldg(reinterpret_cast<const uint4*>(beta) + c);
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();
     float v[NCH][E];
     double sum = 0.0;
 #pragma unroll
@@ -103,8 +116,8 @@ __global__ void __launch_bounds__(1024) add_layernorm_kernel(T* out, T* residual
         const int c = threadIdx.x + i * static_cast<int>(blockDim.x);
         if (c < nch) {
             float gf[E], bf[E], y[E];
-            unpack16<T>(__ldg(reinterpret_cast<const uint4*>(gamma) + c), gf);
-            unpack16<T>(__ldg(reinterpret_cast<const uint4*>(beta) + c), bf);
+            unpack16<T>(graw[i], gf);
+            unpack16<T>(braw[i], bf);
 #pragma unroll
             for (int e = 0; e < E; ++e) {
                 const float nrm = static_cast<float>(__dmul_rn(static_cast<double>(v[i][e]) - mean,
@@ -130,12 +143,17 @@ template <typename T>
 __global__ void __launch_bounds__(256) bias_gelu_kernel(T* out, const T* x, const T* bias, long long nchunks,
                                                         int row_chunks) {
     constexpr int E = Elem<T>::kPer16B;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < nchunks;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int c = static_cast<int>(i % row_chunks);
+    const long long i0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    // The first chunk's bias (a weight) is fetched before waiting for the
+    // kernel that produced x.
+    uint4 b0 = make_uint4(0u, 0u, 0u, 0u);
+    if (i0 < nchunks) b0 = __ldg(reinterpret_cast<const uint4*>(bias) + static_cast<int>(i0 % row_chunks));
+    pdl_launch_dependents();
+    pdl_wait();
+    for (long long i = i0; i < nchunks; i += static_cast<long long>(gridDim.x) * blockDim.x) {
         float f[E], bf[E];
         unpack16<T>(__ldg(reinterpret_cast<const uint4*>(x) + i), f);
-        unpack16<T>(__ldg(reinterpret_cast<const uint4*>(bias) + c), bf);
+        unpack16<T>(i == i0 ? b0 : __ldg(reinterpret_cast<const uint4*>(bias) + static_cast<int>(i % row_chunks)), bf);
 #pragma unroll
         for (int e = 0; e < E; ++e) f[e] = gelu_tanh_ref(__fadd_rn(f[e], bf[e]));
         reinterpret_cast<uint4*>(out)[i] = pack16<T>(f);
