@@ -16,9 +16,16 @@
 //   S = Q . K^T      M=128 N=128 K=64  fp32 in TMEM, two buffers (columns
 //                                      [0, 128) and [128, 256)): S(t + 1) is
 //                                      computed while the softmax reads S(t)
-//   O += P . V       M=128 N=64  K=128 fp32 in TMEM columns [256, 320)
+//   O += P . V       M=128 N=64  K=128 fp32 in TMEM columns [256, 320), P
+//                                      read from TMEM (the A operand of the MMA)
 // P is written by the softmax threads as two 16-bit halves hi = T(p) and
 // lo = T(p - hi) and both are multiplied in (16 significant bits per weight).
+// P(t) overwrites S(t) in its own TMEM buffer: each thread has read its 64 S
+// columns into registers and writes the packed hi words into the first 32 of
+// them and the lo words into the next 32.  So P is double-buffered with S, the
+// softmax of tile t + 1 runs while the tensor core multiplies P(t) . V(t), and
+// S(t + 2) overwrites P(t) only after that product (MMAs issued by one thread
+// execute in order).
 // Softmax in log2 units with a lazily moved reference maximum (moves only when
 // a tile's row maximum exceeds it by more than 8, so weights stay <= 2^8 and
 // O is rescaled only then).  Causality comes from positions: key k counts for
@@ -27,7 +34,7 @@
 // past the keys in use are zeroed before the PV product, so stale values there
 // (never written) cannot reach the output.
 //
-// Roles (320 threads): warp 0 lane 0 TMA producer (3-slot K/V ring), warp 1
+// Roles (320 threads): warp 0 lane 0 TMA producer (4-slot K/V ring), warp 1
 // TMEM owner and (lane 0) MMA issuer, warps 2-9 softmax / epilogue: two
 // threads per query row (warps w and w + 4 read the same TMEM lanes
 // 32 * (w % 4) ...), each taking 64 of a tile's 128 keys, so every SM
@@ -46,10 +53,10 @@ constexpr int kPfRows = 128;                    // query rows per CTA (MMA M)
 constexpr int kPfKeys = 128;                    // keys per tile: 8 paged blocks
 constexpr int kPfHeadDim = 64;                  // one 128-byte swizzle row per key / query
 constexpr int kPfTile = kPfKeys * kPfHeadDim * 2;  // one K or V tile: 16 KiB
-constexpr int kPfStages = 3;
+constexpr int kPfStages = 4;
 constexpr int kPfSoftmax = 256;  // two threads per query row, 64 key columns each
 constexpr int kPfThreads = 64 + kPfSoftmax;
-constexpr uint32_t kPfTmemCols = 512;  // S(t even) [0, 128), S(t odd) [128, 256), O [256, 320)
+constexpr uint32_t kPfTmemCols = 512;  // S/P(t even) [0, 128), S/P(t odd) [128, 256), O [256, 320)
 constexpr uint32_t kPfOCol = 256;
 
 struct PfParams {
@@ -71,8 +78,7 @@ struct PfParams {
 // Shared-memory plan (bytes from the 1024-aligned base).
 struct PfLayout {
     static constexpr int off_q = 0;                          // [128][64] K-major
-    static constexpr int off_p = off_q + kPfRows * 128;      // hi: 2 key atoms of [128][64]; then lo
-    static constexpr int off_kv = off_p + 4 * kPfRows * 128;  // [stage][K | V]
+    static constexpr int off_kv = off_q + kPfRows * 128;     // [stage][K | V]
     static constexpr int off_red = off_kv + kPfStages * 2 * kPfTile;  // [2 halves][128 rows] fp32
     static constexpr int off_bars = off_red + 2 * kPfRows * 4;
     static constexpr int n_bars = 2 * kPfStages + 5;  // kv_full, kv_empty, s_full[2], p_ready, o_done, done
@@ -83,6 +89,49 @@ struct PfLayout {
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 #pragma unroll
     for (int i = 0; i < 32; i += 8) tmem_st8(taddr + static_cast<uint32_t>(i), v + i);
+}
+
+// Two 16-bit values in one 32-bit word (first in the low half) and back.
+__device__ __forceinline__ uint32_t pf_pack2(__half, float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pf_pack2(__nv_bfloat16, float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 pf_unpack2(__half, uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+__device__ __forceinline__ float2 pf_unpack2(__nv_bfloat16, uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+
+// Pass 2 of one thread's 64 keys of a tile: p = 2^(s * v - m_ref) (0 for masked
+// keys when MASK), accumulated into ls, and written over the thread's S columns
+// as hi = T(p) (first 32 columns) and lo = T(p - hi) (next 32).
+template <typename T, bool MASK>
+__device__ __forceinline__ void pf_weights(const float* v, float scale_log2, float m_ref, int kbase, int qpos,
+                                           bool valid, uint32_t s_addr, float* ls) {
+#pragma unroll
+    for (int j = 0; j < 64; j += 8) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float pw[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int c = j + 2 * q + e;
+                pw[e] = (!MASK || (valid && kbase + c <= qpos)) ? ex2_approx(fmaf(v[c], scale_log2, -m_ref)) : 0.0f;
+                ls[(2 * q + e) & 7] += pw[e];
+            }
+            hw[q] = pf_pack2(T(), pw[0], pw[1]);
+            const float2 h = pf_unpack2(T(), hw[q]);
+            lw[q] = pf_pack2(T(), pw[0] - h.x, pw[1] - h.y);
+        }
+        tmem_st4u(s_addr + static_cast<uint32_t>(j / 2), make_uint4(hw[0], hw[1], hw[2], hw[3]));
+        tmem_st4u(s_addr + 32u + static_cast<uint32_t>(j / 2), make_uint4(lw[0], lw[1], lw[2], lw[3]));
+    }
 }
 
 template <typename T>
@@ -117,7 +166,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const size_t row0 = static_cast<size_t>(__ldg(p.q_start + b)) + i0;
 
     unsigned char* qbuf = smem + PfLayout::off_q;
-    unsigned char* pbuf = smem + PfLayout::off_p;
     unsigned char* kv = smem + PfLayout::off_kv;
     uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + PfLayout::off_bars);
     uint64_t* kv_empty = kv_full + kPfStages;
@@ -216,9 +264,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             constexpr uint32_t IDESC_S = umma_idesc<T>(kPfRows, kPfKeys, false, false);
             constexpr uint32_t IDESC_O = umma_idesc<T>(kPfRows, kPfHeadDim, false, true);
             const uint32_t qa = smem_addr(qbuf);
-            const uint32_t pa = smem_addr(pbuf);
             // S(t) = Q . K(t)^T into S buffer t % 2 as soon as K(t) lands; buffer t % 2
-            // last held S(t - 2), which the softmax had read before p_ready(t - 2)
+            // last held P(t - 2), which PV(t - 2), issued before it, has consumed
             auto issue_s = [&](int t) -> bool {
                 const int st = t % kPfStages;
                 if (!mbar_wait_bounded(&kv_full[st], static_cast<uint32_t>(t / kPfStages) & 1u)) return false;
@@ -240,12 +287,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t va = smem_addr(kv + (t % kPfStages) * 2 * kPfTile) + kPfTile;
+                const uint32_t pt = tmem + static_cast<uint32_t>((t & 1) * kPfKeys);
 #pragma unroll
                 for (int kk = 0; kk < kPfKeys / 16; ++kk) {
-                    const uint32_t po = static_cast<uint32_t>((kk >> 2) * kPfRows * 128 + (kk & 3) * 32);
+                    // keys [16 kk, 16 kk + 16): written by half kk / 4, hi words then lo words
+                    const uint32_t pa = pt + static_cast<uint32_t>((kk >> 2) * 64 + (kk & 3) * 8);
                     const uint64_t vd = sw128_desc(va + static_cast<uint32_t>(kk) * 2048u, kPfTile, 1024);
-                    umma_f16(tmem + kPfOCol, sw128_desc(pa + po, 16, 1024), vd, IDESC_O, t > 0 || kk > 0);
-                    umma_f16(tmem + kPfOCol, sw128_desc(pa + 2 * kPfRows * 128 + po, 16, 1024), vd, IDESC_O, true);
+                    umma_f16_ts(tmem + kPfOCol, pa, vd, IDESC_O, t > 0 || kk > 0);
+                    umma_f16_ts(tmem + kPfOCol, pa + 32u, vd, IDESC_O, true);
                 }
                 umma_commit(o_done);
                 umma_commit(&kv_empty[t % kPfStages]);
@@ -273,29 +322,32 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tc_fence_after();
             const uint32_t s_addr = s_base + static_cast<uint32_t>((t & 1) * kPfKeys);
             const int kbase = t * kPfKeys + 64 * half;  // position of this thread's first key
-            // pass 1: the maximum over this thread's visible keys, combined with the other half's
+            float v[64];  // this thread's 64 scores of the tile, kept for both passes
+            tmem_ld32(s_addr, v);
+            tmem_ld32(s_addr + 32u, v + 32);
+            // A tile whose last key precedes the tile's first query position is
+            // visible to every row (CTA-uniform): no causal mask.  Rows past nq
+            // then see S = 0 (their Q rows are zero) and are never stored.
+            const bool open = (t + 1) * kPfKeys - 1 <= pre + i0;
+            // pass 1: the maximum over this thread's visible keys, combined with the
+            // other half's; scaled once (x -> x * s is monotonic for s > 0, so
+            // max(v) * s == max(v * s) exactly)
             float mxs[8];  // independent partial maxima (no 64-long dependency chain)
 #pragma unroll
             for (int e = 0; e < 8; ++e) mxs[e] = -INFINITY;
+            if (open) {
 #pragma unroll
-            for (int c0 = 0; c0 < 64; c0 += 32) {
-                float v[32];
-                tmem_ld32(s_addr + static_cast<uint32_t>(c0), v);
+                for (int j = 0; j < 64; ++j) mxs[j & 7] = fmaxf(mxs[j & 7], v[j]);
+            } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (valid && kbase + c0 + j <= qpos) mxs[j & 7] = fmaxf(mxs[j & 7], v[j] * p.scale_log2);
+                for (int j = 0; j < 64; ++j)
+                    if (valid && kbase + j <= qpos) mxs[j & 7] = fmaxf(mxs[j & 7], v[j]);
             }
             float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]))) *
+                       p.scale_log2;
             red[half * kPfRows + row] = mx;
-            // PV(t-1) must have finished before O is rescaled and P is overwritten
-            if (t > 0) ok = mbar_wait_bounded(o_done, static_cast<uint32_t>(t - 1) & 1u);
-            if (named_sync_or(2, NS, !ok)) {
-                if (!ok) flag_error(B2_DEVERR_TIMEOUT);
-                ok = false;
-                break;
-            }
-            tc_fence_after();
+            named_sync(2, NS);
             mx = fmaxf(mx, red[(half ^ 1) * kPfRows + row]);
             // move the reference maximum (always on a row's first keys, which are in
             // tile 0: key 0 is visible to every row); O rows are rescaled by all
@@ -308,6 +360,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 m_ref = mx;
             }
             if (named_sync_or(4, NS, need) && t > 0) {
+                // PV(t - 1) must have finished before O is rescaled.  PV(t - 2) has
+                // (S(t) was issued after it), so o_done is at most one phase behind.
+                ok = mbar_wait_bounded(o_done, static_cast<uint32_t>(t - 1) & 1u);
+                if (named_sync_or(6, NS, !ok)) {
+                    if (!ok) flag_error(B2_DEVERR_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
                 float o[32];
                 tmem_ld32(o_addr, o);
 #pragma unroll
@@ -315,31 +376,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 tmem_st32(o_addr, o);
                 tmem_wait_st();
             }
-            // pass 2: weights, split into two 16-bit halves, into P (K-major; this
-            // thread's 64 keys are exactly one 64-key atom of the tile)
-            unsigned char* p_hi = pbuf + half * kPfRows * 128;
-            unsigned char* p_lo = p_hi + 2 * kPfRows * 128;
+            // pass 2: weights, split into two 16-bit halves, over this thread's S
+            // columns: hi words into the first 32, lo words into the next 32
             float ls[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // partial sums
-#pragma unroll
-            for (int c0 = 0; c0 < 64; c0 += 32) {
-                float v[32];
-                tmem_ld32(s_addr + static_cast<uint32_t>(c0), v);
-#pragma unroll
-                for (int j = 0; j < 32; j += 8) {
-                    float hi[8], lo[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int kp = kbase + c0 + j + e;
-                        const float pw = (valid && kp <= qpos) ? ex2_approx(v[j + e] * p.scale_log2 - m_ref) : 0.0f;
-                        ls[e] += pw;
-                        hi[e] = Elem<T>::to_f(Elem<T>::from_f(pw));
-                        lo[e] = pw - hi[e];
-                    }
-                    const uint32_t off = sw128_offset(row, c0 + j, 2);
-                    *reinterpret_cast<uint4*>(p_hi + off) = pack16<T>(hi);
-                    *reinterpret_cast<uint4*>(p_lo + off) = pack16<T>(lo);
-                }
-            }
+            if (open)
+                pf_weights<T, false>(v, p.scale_log2, m_ref, kbase, qpos, valid, s_addr, ls);
+            else
+                pf_weights<T, true>(v, p.scale_log2, m_ref, kbase, qpos, valid, s_addr, ls);
+            tmem_wait_st();
             l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
             if (t == ntiles - 1 && half == 0 && t * kPfKeys + row >= kv_end) {
                 // key row past the keys in use: zero its V (P is 0 there; V may be stale)
@@ -347,7 +391,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 8; ++c) vrow[c] = make_uint4(0u, 0u, 0u, 0u);
             }
-            fence_proxy_async_smem();  // P and the zeroed V rows are read by the tensor core
+            fence_proxy_async_smem();  // the zeroed V rows are read by the tensor core
             tc_fence_before();
             named_sync(3, NS);
             if (tid == 64) mbar_arrive(p_ready);
@@ -355,7 +399,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // ---- O / l for the tile's rows; each thread stores its 32 of the 64 dims
         // (every lane loads: tcgen05.ld is warp-wide)
         red[half * kPfRows + row] = l;
-        bool fin = ok && mbar_wait_bounded(o_done, static_cast<uint32_t>(ntiles - 1) & 1u);
+        // PV(ntiles - 1) done; PV(ntiles - 2) first, so o_done is never two phases behind
+        bool fin = ok;
+        if (fin && ntiles >= 2) fin = mbar_wait_bounded(o_done, static_cast<uint32_t>(ntiles - 2) & 1u);
+        if (fin) fin = mbar_wait_bounded(o_done, static_cast<uint32_t>(ntiles - 1) & 1u);
         if (!named_sync_or(5, NS, !fin)) {
             tc_fence_after();
             const float lt = l + red[(half ^ 1) * kPfRows + row];

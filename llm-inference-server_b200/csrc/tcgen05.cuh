@@ -38,6 +38,19 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]: A K-major in tensor memory, row m in lane m,
+// two 16-bit elements per 32-bit column (the lower-addressed element in the low
+// half, as in memory); one K=16 step reads 8 columns from a_tmem.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+
 // Arrives on `bar` once every MMA this thread issued before it has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
@@ -110,6 +123,12 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const float* v) {
         "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
         "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
         : "memory");
+}
+// 4 consecutive 32-bit TMEM columns from raw words (packed 16-bit pairs).
+__device__ __forceinline__ void tmem_st4u(uint32_t taddr, uint4 w) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(w.x), "r"(w.y),
+                 "r"(w.z), "r"(w.w)
+                 : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
