@@ -52,6 +52,11 @@ CASES = [
     ("bf16-cached-prefix", O.BF16, 6, 6, [(37, 50), (200, 256), (5, 300), (1000, 130)], 2, 1, True),
     ("f16-gpt2-medium-heads", O.F16, 16, 16, [(0, 512), (0, 33), (16, 100)], 1, 0, True),
     ("bf16-gqa4", O.BF16, 8, 2, [(0, 200), (64, 64), (3, 7)], 1, 0, False),
+    # 480 (sequence, head, query tile) CTAs, ragged lengths and cached prefixes:
+    # more than three waves of one CTA per SM
+    ("f16-many-items-per-cta", O.F16, 16, 16,
+     [(0, 512), (0, 300), (50, 256), (0, 140), (200, 384), (0, 64), (0, 512), (30, 129), (0, 400), (0, 200),
+      (90, 96), (0, 256)], 2, 1, True),
 ]
 
 
