@@ -155,8 +155,10 @@ typedef struct B2PagedAttnArgs {
     int32_t num_blocks; /* pool capacity in blocks (bounds check) */
     float scale;        /* 0 selects 1/sqrt(head_dim) */
     int32_t flags;      /* 0, B2_ATTN_INPUTS_READY or B2_ATTN_NEWEST_ROW_PENDING */
-    int32_t max_ctas;   /* 0: the whole GPU (one or two CTAs per SM); n > 0: at most n CTAs,
-                           leaving SMs to kernels running concurrently on other streams */
+    int32_t max_ctas;   /* 0: the whole GPU (one or two CTAs per SM; at two per SM with
+                           B2_ATTN_INPUTS_READY, SMs / 16 slots stay free for the next
+                           launch's first CTAs); n > 0: at most n CTAs, leaving SMs to
+                           kernels running concurrently on other streams */
 } B2PagedAttnArgs;
 
 /* flags: what the kernel may read before the kernel launched just before it
