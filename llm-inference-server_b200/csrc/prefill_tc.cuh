@@ -10,22 +10,26 @@
 // attention (gpu-engine/src/kernels/attention.cu:49-127, cpu_model.cpp:131-162)
 // gives that row, with every key tile read once per 128 query rows.
 //
-// One CTA per (sequence, query head, 128-row query tile):
+// One CTA per (sequence, query head, 128-row query tile), two CTAs per SM
+// (256 TMEM columns, ~82 KB of shared memory and <= 102 registers a thread
+// each): a tile's chain -- K/V lands, S, softmax, P . V -- is serial within a
+// CTA, so the second CTA's chain and its set-up fill the gaps (one CTA per SM
+// with S double-buffered in TMEM ran 37 us where this runs 27 us at 8 x 512
+// rows x 16 heads):
 //   Q tile [128 rows][64]             smem, SWIZZLE_128B K-major (threads, + bias)
-//   K, V tiles [128 keys][64]         8 paged blocks x one 16-row TMA box each
-//   S = Q . K^T      M=128 N=128 K=64  fp32 in TMEM, two buffers (columns
-//                                      [0, 128) and [128, 256)): S(t + 1) is
-//                                      computed while the softmax reads S(t)
-//   O += P . V       M=128 N=64  K=128 fp32 in TMEM columns [256, 320), P
-//                                      read from TMEM (the A operand of the MMA)
+//   K, V tiles [128 keys][64]         8 paged blocks x one 16-row TMA box each,
+//                                      2-slot ring
+//   S = Q . K^T      M=128 N=128 K=64  fp32 in TMEM columns [0, 128)
+//   O += P . V       M=128 N=64  K=128 fp32 in TMEM columns [128, 192), P read
+//                                      from TMEM (the A operand of the MMA)
 // P is written by the softmax threads as two 16-bit halves hi = T(p) and
 // lo = T(p - hi) and both are multiplied in (16 significant bits per weight).
-// P(t) overwrites S(t) in its own TMEM buffer: each thread has read its 64 S
-// columns into registers and writes the packed hi words into the first 32 of
-// them and the lo words into the next 32.  So P is double-buffered with S, the
-// softmax of tile t + 1 runs while the tensor core multiplies P(t) . V(t), and
-// S(t + 2) overwrites P(t) only after that product (MMAs issued by one thread
-// execute in order).
+// P(t) overwrites S(t): each thread handles its 64 S columns as two chunks of
+// 32, reading a chunk's scores before writing its packed hi words into the
+// chunk's first 16 columns and its lo words into the next 16.  S(t + 1) is
+// issued after P(t) . V(t) (one thread's MMAs execute in order, so the product
+// has read P before S overwrites it), and the softmax, which waits for S(t + 1),
+// thereby also knows P(t) . V(t) has finished when it rescales O.
 // Softmax in log2 units with a lazily moved reference maximum (moves only when
 // a tile's row maximum exceeds it by more than 8, so weights stay <= 2^8 and
 // O is rescaled only then).  Causality comes from positions: key k counts for
@@ -34,12 +38,11 @@
 // past the keys in use are zeroed before the PV product, so stale values there
 // (never written) cannot reach the output.
 //
-// Roles (320 threads): warp 0 lane 0 TMA producer (4-slot K/V ring), warp 1
-// TMEM owner and (lane 0) MMA issuer, warps 2-9 softmax / epilogue: two
-// threads per query row (warps w and w + 4 read the same TMEM lanes
-// 32 * (w % 4) ...), each taking 64 of a tile's 128 keys, so every SM
-// sub-partition has two softmax warps to interleave; the two halves of a row
-// exchange their maxima (and at the end their sums) through shared memory.  Every wait is bounded; a wait
+// Roles (320 threads): warp 0 lane 0 TMA producer, warp 1 TMEM owner and
+// (lane 0) MMA issuer, warps 2-9 softmax / epilogue: two threads per query row
+// (warps w and w + 4 read the same TMEM lanes 32 * (w % 4) ...), each taking 64
+// of a tile's 128 keys; the two halves of a row exchange their maxima (and at
+// the end their sums) through shared memory.  Every wait is bounded; a wait
 // that gives up flags B2_DEVERR_TIMEOUT and the CTA winds down through the
 // common exit (its copies landed, its MMAs done, TMEM freed).
 #pragma once
@@ -53,11 +56,11 @@ constexpr int kPfRows = 128;                    // query rows per CTA (MMA M)
 constexpr int kPfKeys = 128;                    // keys per tile: 8 paged blocks
 constexpr int kPfHeadDim = 64;                  // one 128-byte swizzle row per key / query
 constexpr int kPfTile = kPfKeys * kPfHeadDim * 2;  // one K or V tile: 16 KiB
-constexpr int kPfStages = 4;
+constexpr int kPfStages = 2;
 constexpr int kPfSoftmax = 256;  // two threads per query row, 64 key columns each
 constexpr int kPfThreads = 64 + kPfSoftmax;
-constexpr uint32_t kPfTmemCols = 512;  // S/P(t even) [0, 128), S/P(t odd) [128, 256), O [256, 320)
-constexpr uint32_t kPfOCol = 256;
+constexpr uint32_t kPfTmemCols = 256;  // S/P [0, 128), O [128, 192): two CTAs share an SM's 512
+constexpr uint32_t kPfOCol = 128;
 
 struct PfParams {
     const void* q;
@@ -81,7 +84,7 @@ struct PfLayout {
     static constexpr int off_kv = off_q + kPfRows * 128;     // [stage][K | V]
     static constexpr int off_red = off_kv + kPfStages * 2 * kPfTile;  // [2 halves][128 rows] fp32
     static constexpr int off_bars = off_red + 2 * kPfRows * 4;
-    static constexpr int n_bars = 2 * kPfStages + 5;  // kv_full, kv_empty, s_full[2], p_ready, o_done, done
+    static constexpr int n_bars = 2 * kPfStages + 4;  // kv_full, kv_empty, s_full, p_ready, o_done, done
     static constexpr int off_tmem = off_bars + 8 * n_bars;
     static constexpr int bytes = off_tmem + 16 + 1024;
 };
@@ -107,14 +110,14 @@ __device__ __forceinline__ float2 pf_unpack2(__nv_bfloat16, uint32_t w) {
     return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 
-// Pass 2 of one thread's 64 keys of a tile: p = 2^(s * v - m_ref) (0 for masked
-// keys when MASK), accumulated into ls, and written over the thread's S columns
-// as hi = T(p) (first 32 columns) and lo = T(p - hi) (next 32).
-template <typename T, bool MASK>
+// Pass 2 of NK of one thread's keys: p = 2^(s * v - m_ref) (0 for masked keys
+// when MASK), accumulated into ls, and written over those keys' S columns as
+// hi = T(p) (first NK / 2 columns) and lo = T(p - hi) (next NK / 2).
+template <typename T, bool MASK, int NK>
 __device__ __forceinline__ void pf_weights(const float* v, float scale_log2, float m_ref, int kbase, int qpos,
                                            bool valid, uint32_t s_addr, float* ls) {
 #pragma unroll
-    for (int j = 0; j < 64; j += 8) {
+    for (int j = 0; j < NK; j += 8) {
         uint32_t hw[4], lw[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -130,12 +133,12 @@ __device__ __forceinline__ void pf_weights(const float* v, float scale_log2, flo
             lw[q] = pf_pack2(T(), pw[0] - h.x, pw[1] - h.y);
         }
         tmem_st4u(s_addr + static_cast<uint32_t>(j / 2), make_uint4(hw[0], hw[1], hw[2], hw[3]));
-        tmem_st4u(s_addr + 32u + static_cast<uint32_t>(j / 2), make_uint4(lw[0], lw[1], lw[2], lw[3]));
+        tmem_st4u(s_addr + static_cast<uint32_t>(NK / 2 + j / 2), make_uint4(lw[0], lw[1], lw[2], lw[3]));
     }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kPfThreads, 1)
+__global__ void __launch_bounds__(kPfThreads, 2)
     prefill_attn_tc_kernel(const PfParams p, const __grid_constant__ CUtensorMap kv_map) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem =
@@ -169,8 +172,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     unsigned char* kv = smem + PfLayout::off_kv;
     uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + PfLayout::off_bars);
     uint64_t* kv_empty = kv_full + kPfStages;
-    uint64_t* s_full = kv_empty + kPfStages;  // [2]: one per S buffer
-    uint64_t* p_ready = s_full + 2;
+    uint64_t* s_full = kv_empty + kPfStages;
+    uint64_t* p_ready = s_full + 1;
     uint64_t* o_done = p_ready + 1;
     uint64_t* done_bar = o_done + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PfLayout::off_tmem);
@@ -180,8 +183,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        mbar_init(&s_full[0], 1);
-        mbar_init(&s_full[1], 1);
+        mbar_init(s_full, 1);
         mbar_init(p_ready, 1);
         mbar_init(o_done, 1);
         mbar_init(done_bar, 1);
@@ -264,8 +266,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             constexpr uint32_t IDESC_S = umma_idesc<T>(kPfRows, kPfKeys, false, false);
             constexpr uint32_t IDESC_O = umma_idesc<T>(kPfRows, kPfHeadDim, false, true);
             const uint32_t qa = smem_addr(qbuf);
-            // S(t) = Q . K(t)^T into S buffer t % 2 as soon as K(t) lands; buffer t % 2
-            // last held P(t - 2), which PV(t - 2), issued before it, has consumed
+            // S(t) = Q . K(t)^T into the S/P columns once K(t) has landed; they held P(t - 1),
+            // which PV(t - 1), issued before it, has read (one thread's MMAs run in order)
             auto issue_s = [&](int t) -> bool {
                 const int st = t % kPfStages;
                 if (!mbar_wait_bounded(&kv_full[st], static_cast<uint32_t>(t / kPfStages) & 1u)) return false;
@@ -273,31 +275,30 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const uint32_t ka = smem_addr(kv + st * 2 * kPfTile);
 #pragma unroll
                 for (int k = 0; k < kPfHeadDim / 16; ++k)
-                    umma_f16(tmem + static_cast<uint32_t>((t & 1) * kPfKeys), sw128_desc(qa + 32 * k, 16, 1024),
-                             sw128_desc(ka + 32 * k, 16, 1024), IDESC_S, k > 0);
-                umma_commit(&s_full[t & 1]);
+                    umma_f16(tmem, sw128_desc(qa + 32 * k, 16, 1024), sw128_desc(ka + 32 * k, 16, 1024), IDESC_S,
+                             k > 0);
+                umma_commit(s_full);
                 return true;
             };
             bool ok = issue_s(0);
             for (int t = 0; ok && t < ntiles; ++t) {
-                if (t + 1 < ntiles && !(ok = issue_s(t + 1))) break;  // overlaps the softmax of tile t
                 if (!mbar_wait_bounded(p_ready, static_cast<uint32_t>(t) & 1u)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t va = smem_addr(kv + (t % kPfStages) * 2 * kPfTile) + kPfTile;
-                const uint32_t pt = tmem + static_cast<uint32_t>((t & 1) * kPfKeys);
 #pragma unroll
                 for (int kk = 0; kk < kPfKeys / 16; ++kk) {
-                    // keys [16 kk, 16 kk + 16): written by half kk / 4, hi words then lo words
-                    const uint32_t pa = pt + static_cast<uint32_t>((kk >> 2) * 64 + (kk & 3) * 8);
+                    // keys [16 kk, 16 kk + 16): in the 32-key chunk kk / 2, hi words then lo words
+                    const uint32_t pa = tmem + static_cast<uint32_t>((kk >> 1) * 32 + (kk & 1) * 8);
                     const uint64_t vd = sw128_desc(va + static_cast<uint32_t>(kk) * 2048u, kPfTile, 1024);
                     umma_f16_ts(tmem + kPfOCol, pa, vd, IDESC_O, t > 0 || kk > 0);
-                    umma_f16_ts(tmem + kPfOCol, pa + 32u, vd, IDESC_O, true);
+                    umma_f16_ts(tmem + kPfOCol, pa + 16u, vd, IDESC_O, true);
                 }
                 umma_commit(o_done);
                 umma_commit(&kv_empty[t % kPfStages]);
+                if (t + 1 < ntiles && !(ok = issue_s(t + 1))) break;
             }
             if (!ok) flag_error(B2_DEVERR_TIMEOUT);
         }
@@ -313,18 +314,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         float m_ref = -INFINITY, l = 0.0f;  // l: this thread's share of the row sum
         bool ok = true;
         for (int t = 0; t < ntiles; ++t) {
-            ok = mbar_wait_bounded(&s_full[t & 1], static_cast<uint32_t>(t >> 1) & 1u);
+            ok = mbar_wait_bounded(s_full, static_cast<uint32_t>(t) & 1u);
             if (named_sync_or(1, NS, !ok)) {
                 if (!ok) flag_error(B2_DEVERR_TIMEOUT);
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t s_addr = s_base + static_cast<uint32_t>((t & 1) * kPfKeys);
+            const uint32_t s_addr = s_base;
             const int kbase = t * kPfKeys + 64 * half;  // position of this thread's first key
-            float v[64];  // this thread's 64 scores of the tile, kept for both passes
-            tmem_ld32(s_addr, v);
-            tmem_ld32(s_addr + 32u, v + 32);
+            float v[32];  // 32 of this thread's 64 scores of the tile at a time
             // A tile whose last key precedes the tile's first query position is
             // visible to every row (CTA-uniform): no causal mask.  Rows past nq
             // then see S = 0 (their Q rows are zero) and are never stored.
@@ -335,13 +334,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             float mxs[8];  // independent partial maxima (no 64-long dependency chain)
 #pragma unroll
             for (int e = 0; e < 8; ++e) mxs[e] = -INFINITY;
-            if (open) {
 #pragma unroll
-                for (int j = 0; j < 64; ++j) mxs[j & 7] = fmaxf(mxs[j & 7], v[j]);
-            } else {
+            for (int ch = 0; ch < 2; ++ch) {
+                tmem_ld32(s_addr + static_cast<uint32_t>(32 * ch), v);
+                if (open) {
 #pragma unroll
-                for (int j = 0; j < 64; ++j)
-                    if (valid && kbase + j <= qpos) mxs[j & 7] = fmaxf(mxs[j & 7], v[j]);
+                    for (int j = 0; j < 32; ++j) mxs[j & 7] = fmaxf(mxs[j & 7], v[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (valid && kbase + 32 * ch + j <= qpos) mxs[j & 7] = fmaxf(mxs[j & 7], v[j]);
+                }
             }
             float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
                              fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]))) *
@@ -360,15 +363,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 m_ref = mx;
             }
             if (named_sync_or(4, NS, need) && t > 0) {
-                // PV(t - 1) must have finished before O is rescaled.  PV(t - 2) has
-                // (S(t) was issued after it), so o_done is at most one phase behind.
-                ok = mbar_wait_bounded(o_done, static_cast<uint32_t>(t - 1) & 1u);
-                if (named_sync_or(6, NS, !ok)) {
-                    if (!ok) flag_error(B2_DEVERR_TIMEOUT);
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+                // PV(t - 1) has finished: S(t), whose completion the softmax waited
+                // for, was issued after it
                 float o[32];
                 tmem_ld32(o_addr, o);
 #pragma unroll
@@ -376,13 +372,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 tmem_st32(o_addr, o);
                 tmem_wait_st();
             }
-            // pass 2: weights, split into two 16-bit halves, over this thread's S
-            // columns: hi words into the first 32, lo words into the next 32
+            // pass 2: weights, split into two 16-bit halves, over this thread's S columns,
+            // 32 keys at a time (each chunk's scores are re-read before its P overwrites them)
             float ls[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // partial sums
-            if (open)
-                pf_weights<T, false>(v, p.scale_log2, m_ref, kbase, qpos, valid, s_addr, ls);
-            else
-                pf_weights<T, true>(v, p.scale_log2, m_ref, kbase, qpos, valid, s_addr, ls);
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch) {
+                const uint32_t ca = s_addr + static_cast<uint32_t>(32 * ch);
+                tmem_ld32(ca, v);
+                if (open)
+                    pf_weights<T, false, 32>(v, p.scale_log2, m_ref, kbase + 32 * ch, qpos, valid, ca, ls);
+                else
+                    pf_weights<T, true, 32>(v, p.scale_log2, m_ref, kbase + 32 * ch, qpos, valid, ca, ls);
+            }
             tmem_wait_st();
             l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
             if (t == ntiles - 1 && half == 0 && t * kPfKeys + row >= kv_end) {
@@ -399,10 +400,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // ---- O / l for the tile's rows; each thread stores its 32 of the 64 dims
         // (every lane loads: tcgen05.ld is warp-wide)
         red[half * kPfRows + row] = l;
-        // PV(ntiles - 1) done; PV(ntiles - 2) first, so o_done is never two phases behind
-        bool fin = ok;
-        if (fin && ntiles >= 2) fin = mbar_wait_bounded(o_done, static_cast<uint32_t>(ntiles - 2) & 1u);
-        if (fin) fin = mbar_wait_bounded(o_done, static_cast<uint32_t>(ntiles - 1) & 1u);
+        // PV(ntiles - 1) done (PV(ntiles - 2) is: S(ntiles - 1) was issued after it)
+        const bool fin = ok && mbar_wait_bounded(o_done, static_cast<uint32_t>(ntiles - 1) & 1u);
         if (!named_sync_or(5, NS, !fin)) {
             tc_fence_after();
             const float lt = l + red[(half ^ 1) * kPfRows + row];
