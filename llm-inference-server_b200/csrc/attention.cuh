@@ -81,7 +81,8 @@ struct AttnParams {
     int ncons;         // consumer threads, multiple of 32
     int stages;
     int stage_bytes;
-    int slab_bytes;  // 16 * n_kv_head * head_dim * sizeof(T)
+    int stage_rows;  // key rows a stage holds at most: 16 (a block) or 8
+    int slab_bytes;  // stage_rows * n_kv_head * head_dim * sizeof(T): K (then V) capacity of a stage
     int q_bytes;     // n_head * head_dim * sizeof(T)
     int off_meta;    // within a stage
     int off_misc, off_bars;
@@ -378,50 +379,54 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                         }
                     }
                     const int cnt = min(32, j1 - jc);
-                    for (int x = 0; x < cnt; ++x) {
+                    for (int x = 0; x < cnt && !failed; ++x) {
                         const int blk = __shfl_sync(0xffffffffu, blk_l, x);
-                        int ok = 1;
-                        if (lane == 0) {
-                            const int st = n % S;
-                            const uint32_t ph = static_cast<uint32_t>(n / S) & 1u;
-                            if (!mbar_wait_bounded(&empty[st], ph ^ 1u)) {
-                                ok = 0;
-                            } else {
-                                const int j = jc + x;
-                                if (!newest_ok && j == (cs - 1) / kBlockTokens) {
-                                    pdl_wait();  // this block holds the sequence's newest row
-                                    newest_ok = true;
-                                }
-                                const int r_lo = max(t_lo - j * kBlockTokens, 0);
-                                const int r_hi = min(t_hi - j * kBlockTokens, kBlockTokens);
-                                const int nrows = r_hi - r_lo;
-                                const int first = (j == j0) ? 1 : 0;
-                                const int lastf = (j == j1 - 1) ? 2 : 0;
-                                // the stage that ends at this CTA's last row ends its work
-                                const int finalf = (Ps + j * kBlockTokens + r_hi == e_unit) ? 4 : 0;
-                                unsigned char* stage = smem + static_cast<size_t>(st) * p.stage_bytes;
-                                *reinterpret_cast<int4*>(stage + p.off_meta) =
-                                    make_int4(bs, nrows | ((first | lastf | finalf) << 8), i0, nseg);
-                                const uint32_t kv_bytes = static_cast<uint32_t>(nrows * row_bytes);
-                                mbar_arrive_expect_tx(&full[st], 2u * kv_bytes + (first ? p.q_bytes : 0));
-                                const char* src = pool + (static_cast<size_t>(blk) * block_elems + layer_off +
-                                                          static_cast<size_t>(r_lo) * row_elems) * ES;
-                                bulk_g2s(stage, src, kv_bytes, &full[st]);
-                                bulk_g2s(stage + p.slab_bytes, src + slab_elems * ES, kv_bytes, &full[st]);
-                                if (first) {
-                                    const char* qsrc = static_cast<const char*>(p.q) +
-                                                       static_cast<size_t>(bs) * p.q_row_stride * ES;
-                                    bulk_g2s(stage + 2 * p.slab_bytes, qsrc, static_cast<uint32_t>(p.q_bytes),
-                                             &full[st]);
+                        const int j = jc + x;
+                        const int r_lo = max(t_lo - j * kBlockTokens, 0);
+                        const int r_hi = min(t_hi - j * kBlockTokens, kBlockTokens);
+                        // the block's rows [r_lo, r_hi) in stages of at most stage_rows rows
+                        for (int rs = r_lo; rs < r_hi; rs += p.stage_rows) {
+                            const int re = min(rs + p.stage_rows, r_hi);
+                            int ok = 1;
+                            if (lane == 0) {
+                                const int st = n % S;
+                                const uint32_t ph = static_cast<uint32_t>(n / S) & 1u;
+                                if (!mbar_wait_bounded(&empty[st], ph ^ 1u)) {
+                                    ok = 0;
+                                } else {
+                                    if (!newest_ok && j == (cs - 1) / kBlockTokens) {
+                                        pdl_wait();  // this block holds the sequence's newest row
+                                        newest_ok = true;
+                                    }
+                                    const int nrows = re - rs;
+                                    const int first = (j == j0 && rs == r_lo) ? 1 : 0;
+                                    const int lastf = (j == j1 - 1 && re == r_hi) ? 2 : 0;
+                                    // the stage that ends at this CTA's last row ends its work
+                                    const int finalf = (Ps + j * kBlockTokens + re == e_unit) ? 4 : 0;
+                                    unsigned char* stage = smem + static_cast<size_t>(st) * p.stage_bytes;
+                                    *reinterpret_cast<int4*>(stage + p.off_meta) =
+                                        make_int4(bs, nrows | ((first | lastf | finalf) << 8), i0, nseg);
+                                    const uint32_t kv_bytes = static_cast<uint32_t>(nrows * row_bytes);
+                                    mbar_arrive_expect_tx(&full[st], 2u * kv_bytes + (first ? p.q_bytes : 0));
+                                    const char* src = pool + (static_cast<size_t>(blk) * block_elems + layer_off +
+                                                              static_cast<size_t>(rs) * row_elems) * ES;
+                                    bulk_g2s(stage, src, kv_bytes, &full[st]);
+                                    bulk_g2s(stage + p.slab_bytes, src + slab_elems * ES, kv_bytes, &full[st]);
+                                    if (first) {
+                                        const char* qsrc = static_cast<const char*>(p.q) +
+                                                           static_cast<size_t>(bs) * p.q_row_stride * ES;
+                                        bulk_g2s(stage + 2 * p.slab_bytes, qsrc, static_cast<uint32_t>(p.q_bytes),
+                                                 &full[st]);
+                                    }
                                 }
                             }
+                            ok = __shfl_sync(0xffffffffu, ok, 0);
+                            if (!ok) {
+                                failed = true;
+                                break;
+                            }
+                            ++n;
                         }
-                        ok = __shfl_sync(0xffffffffu, ok, 0);
-                        if (!ok) {
-                            failed = true;
-                            break;
-                        }
-                        ++n;
                     }
                 }
                 u = Ps + t_hi;

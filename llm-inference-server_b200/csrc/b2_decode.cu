@@ -203,22 +203,36 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
             return B2_OK;
         }
     }
-    const int slab = B2_BLOCK_TOKENS * a->n_kv_head * a->head_dim * es;
     const int qbytes = H * a->head_dim * es;
-    const int off_meta = 2 * slab + qbytes;
-    const int stage = static_cast<int>(align_up(off_meta + 16, 128));
-    // Two CTAs per SM when each still gets a double-buffered ring: one CTA's
-    // prologue and tail then overlap the other's streaming.  The 128-register
-    // cap limits a co-resident pair to 256 threads each.
-    int best_k = 0, best_s = 0, best_cps = 0, best_cpt = 1;
-    for (int cps : {2, 1}) {
-        // one CTA per SM (wide heads): two chunks per consumer thread (16-bit,
-        // up to two query heads per kv head); consumer threads per subgroup CT
-        const int cpt = (cps == 1 && es == 2 && H / a->n_kv_head <= 2) ? 2 : 1;
-        const int CT = C / cpt;
-        const int smem_cap = cps == 1 ? di.max_smem_optin : di.smem_per_sm / cps - 1024;
-        const int thread_cap = cps == 1 ? maxt : 256;
+    // Plans, in order of preference:
+    //  1. two CTAs per SM, a stage per paged block (16 rows), one chunk per consumer
+    //     thread -- each CTA still gets a double-buffered ring, and one CTA's
+    //     prologue and tail overlap the other's streaming;
+    //  2. where a block does not fit that, two CTAs per SM with stages of 8 rows and
+    //     two chunks per thread, if that leaves at least two token subgroups (GPT-2
+    //     medium's 16 heads x 64: 48.7 -> 46.4 us per launch; with 25 heads only one
+    //     subgroup fits and it is slower than plan 3);
+    //  3. one CTA per SM, a stage per block, two chunks per thread (16-bit, up to two
+    //     query heads per kv head): fewer shuffle levels and less repeated softmax
+    //     bookkeeping, which the wide-head shapes' instruction count needs.
+    // The 128-register cap limits a co-resident pair to 256 threads each.
+    struct Cand {
+        int cps, rows, cpt, min_k;
+    };
+    const bool cpt2_ok = es == 2 && H / a->n_kv_head <= 2;
+    const Cand cands[3] = {{2, B2_BLOCK_TOKENS, 1, 1}, {2, B2_BLOCK_TOKENS / 2, 2, 2}, {1, B2_BLOCK_TOKENS, cpt2_ok ? 2 : 1, 1}};
+    int best_k = 0, best_s = 0, best_cps = 0, best_cpt = 1, best_rows = 0;
+    int slab = 0, off_meta = 0, stage = 0;
+    for (const Cand& cd : cands) {
+        if (cd.cpt == 2 && !cpt2_ok) continue;
+        slab = cd.rows * a->n_kv_head * a->head_dim * es;
+        off_meta = 2 * slab + qbytes;
+        stage = static_cast<int>(align_up(off_meta + 16, 128));
+        const int CT = C / cd.cpt;  // consumer threads per token subgroup
+        const int smem_cap = cd.cps == 1 ? di.max_smem_optin : di.smem_per_sm / cd.cps - 1024;
+        const int thread_cap = cd.cps == 1 ? maxt : 256;
         for (int k : {8, 6, 4, 3, 2, 1}) {  // token subgroups: more consumer warps to hide latency
+            if (k < cd.min_k) break;
             const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * CT, 32));
             if (ncons + 64 > thread_cap) continue;  // + producer warp + bookkeeping warp
             if (k > 1 && k * CT > 512) continue;  // enough warps
@@ -227,8 +241,9 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
             if (s < 2) continue;
             best_k = k;
             best_s = s;
-            best_cps = cps;
-            best_cpt = cpt;
+            best_cps = cd.cps;
+            best_cpt = cd.cpt;
+            best_rows = cd.rows;
             break;
         }
         if (best_k != 0) break;
@@ -244,6 +259,7 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     p.ncons = static_cast<int>(align_up(static_cast<size_t>(best_k) * CT, 32));
     p.stages = best_s;
     p.stage_bytes = stage;
+    p.stage_rows = best_rows;
     p.slab_bytes = slab;
     p.q_bytes = qbytes;
     p.off_meta = off_meta;
