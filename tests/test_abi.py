@@ -62,6 +62,17 @@ def test_paged_attention_host_checks(b2, kw, code):
     assert lib.b2_last_error_string().decode() != ""
 
 
+def test_paged_attention_host_checks_before_any_copy(b2):
+    # The host-buffer entry point validates everything before its first copy.
+    lib = b2.load()
+    assert lib.b2_paged_attention_host(ctypes.byref(_attn_args(b2)), None, None, 0, None) == -1  # io NULL
+    io = b2.AttnHostIO(None, None, None, None)
+    for kw, code in ((dict(dtype=7), -2), (dict(q=17), -4), (dict(head_dim=96), -6), (dict(q=None), -1)):
+        args = _attn_args(b2, **kw)
+        assert lib.b2_paged_attention_host(ctypes.byref(args), ctypes.byref(io), None, 0, None) == code
+        assert lib.b2_last_error_string().decode() != ""
+
+
 def test_paged_attention_empty_batch_is_a_no_op(b2):
     args = _attn_args(b2, batch=0, q=None, kv_pool=None)
     assert b2.load().b2_paged_attention(ctypes.byref(args), None, 0, None) == 0
