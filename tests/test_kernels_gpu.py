@@ -439,16 +439,17 @@ def test_reference_kernel_kats(b2, cuda, golden):
     assert toks.cpu().numpy().tolist() == a["expected"]
 
 
+@pytest.mark.parametrize("H", [12, 16])  # 16 heads x 64: the 8-row-stage plan (GPT-2 medium's)
 @pytest.mark.parametrize("dt", [O.F16, O.BF16])
-def test_attention_early_start_after_kv_append(b2, cuda, dt):
+def test_attention_early_start_after_kv_append(b2, cuda, dt, H):
     """kv_append writes each sequence's newest row, then attention runs right
     behind it with B2_ATTN_NEWEST_ROW_PENDING (it may start before kv_append
     finishes and must still read the new rows); and with B2_ATTN_INPUTS_READY
     on inputs written long before.  Both against the oracle over the appended
     pool, several rounds."""
     torch = _torch()
-    rng = np.random.Generator(np.random.PCG64(77))
-    H, Dh, L, layer = 12, 64, 2, 1
+    rng = np.random.Generator(np.random.PCG64(77 + H))
+    Dh, L, layer = 64, 2, 1
     ctx_pre = rng.integers(0, 700, size=48).astype(np.int32)
     pool, bt, mbps, nb = make_paged(rng, dt, (ctx_pre + 1).tolist(), H, Dh, L)
     B = len(ctx_pre)
