@@ -243,12 +243,31 @@ B2_API int b2_paged_attention_gather(const B2PagedAttnArgs* args, void* workspac
  * after a system-scope fence, so the rank's earlier stores to peers are
  * visible first) and then waits until its own local_flags[slot * n + p]
  * reach *epoch for every p.  The wait is bounded (2 s); a timeout sets
- * B2_DEVERR_TIMEOUT and returns.  flag arrays start zeroed; epochs only grow. */
+ * B2_DEVERR_TIMEOUT and returns.  While the device's error word holds
+ * B2_DEVERR_TIMEOUT (a barrier earlier in the step gave up), later barriers
+ * publish their flags but do not wait, so a step whose peer stopped fails in
+ * one limit, not one per layer.  flag arrays start zeroed; epochs only grow. */
 B2_API int b2_tp_barrier(uint32_t* local_flags, uint32_t* const* peer_flags, int32_t rank, int32_t n,
                          const uint32_t* epoch, int32_t slot, b2_stream_t stream);
 
+/* b2_tp_barrier with the wait bounded by limit_ns (0 < limit_ns <= 60 s)
+ * instead of 2 s.  No reference counterpart. */
+B2_API int b2_tp_barrier_timed(uint32_t* local_flags, uint32_t* const* peer_flags, int32_t rank, int32_t n,
+                               const uint32_t* epoch, int32_t slot, uint64_t limit_ns, b2_stream_t stream);
+
 /* *epoch += 1 (one thread): the start of a new step for b2_tp_barrier. */
 B2_API int b2_tp_epoch_bump(uint32_t* epoch, b2_stream_t stream);
+
+/* Device address of the current device's error word (the one
+ * b2_device_errors reads), for callers that read it without a device-wide
+ * synchronisation: a stream-ordered copy of it next to a step's results.
+ * No reference counterpart (its kernels report nothing). */
+B2_API int b2_device_error_word(uint32_t** out);
+
+/* Sets `bits` in the current device's error word from a one-thread kernel on
+ * `stream`, for tests of error propagation: no kernel has to fail for a
+ * caller's error path to run.  No reference counterpart. */
+B2_API int b2_raise_device_error(uint32_t bits, b2_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Paged decode attention without any device allocation.
@@ -265,12 +284,16 @@ B2_API int b2_tp_epoch_bump(uint32_t* epoch, b2_stream_t stream);
  * B2_ERR_WORKSPACE before anything is launched.
  *
  * The first call on a device looks up the array's device address for that
- * device (cudaGetSymbolAddress); make that first call before any stream
- * capture.  All calls share the one array; it starts zeroed (module load) and
- * every completed call leaves its piece counters at zero, so it never needs
- * clearing -- but calls whose kernels overlap on the GPU (different streams,
- * no ordering between them) race on it: order them on one stream, or use
- * b2_paged_attention with a workspace per stream.
+ * device (cudaGetSymbolAddress; a failed lookup is retried by the next call);
+ * make that first call before any stream capture.  The address is kept for
+ * the life of the process, so this entry point does not support
+ * cudaDeviceReset.  All calls share the one array, which keeps what the last
+ * call left in it: each call first clears the array's piece-counter region
+ * with cudaMemsetAsync on `stream` (a call that gave up on a bounded wait,
+ * B2_DEVERR_TIMEOUT, may leave counts behind), then launches.  Calls whose
+ * work overlaps on the GPU (different streams, no ordering between them) race
+ * on the array: order them on one stream, or use b2_paged_attention with a
+ * workspace per stream.
  * ---------------------------------------------------------------------- */
 #define B2_NOALLOC_SCRATCH_BYTES (4u << 20) /* 4 MiB */
 

@@ -41,6 +41,8 @@ typedef struct B2EngineConfig {
     int32_t tp_rank;         /* head-sharded engines: this rank (0 .. tp_size-1) */
     int32_t tp_size;         /* 0 or 1: one engine holds every head; 2..8: head-sharded */
     int32_t max_prefill_tokens; /* prompt tokens one b2_engine_prefill call may carry; 0 = 2048 */
+    int32_t tp_allgather;    /* head-sharded engines: 0 = peer stores fused into the attention
+                                epilogue + flag barrier; 1 = ncclAllGather after attention */
 } B2EngineConfig;
 
 /* gpu-engine/include/engine/model.h:7-18 (GPT2Config). */
@@ -127,6 +129,17 @@ B2_API const char* b2_engine_last_error(void);
 
 #define B2_ERR_POOL (-8) /* the KV block pool ran out during decode_step */
 #define B2_ERR_IO (-9)   /* a weight file is missing, short or inconsistent */
+/* A kernel of the step set a device-side error bit (B2_DEVERR_*, named in
+ * b2_engine_last_error): a bounded wait gave up (e.g. a head-sharded peer
+ * that never reached the barrier), or a block id, seq_len or token was out of
+ * range and clamped.  decode_step / prefill copy the device's error word next
+ * to the step's tokens and check it after the step's synchronisation; on a
+ * nonzero word they clear it and return this code, with no sequence advanced
+ * (the step's tokens are invalid).  The word is shared by everything on the
+ * device that uses libb2decode, so a bit set by another caller's kernel fails
+ * this engine's next step too.  The reference throws std::runtime_error on
+ * CUDA errors (gpu-engine/src/engine.cu:40-44) and has no device-side checks. */
+#define B2_ERR_KERNEL (-10)
 
 /* Head-sharded decode (no reference counterpart; the reference engine is
  * single-GPU).  tp_size engines, one per GPU (each created with its
@@ -145,6 +158,18 @@ B2_API const char* b2_engine_last_error(void);
 #define B2_TP_HANDLE_BYTES 128 /* two cudaIpcMemHandle_t: gathered buffer, barrier flags */
 B2_API int b2_engine_tp_handle(const b2_engine* eng, void* out);
 B2_API int b2_engine_tp_connect(b2_engine* eng, const void* handles);
+
+/* The NCCL variant (cfg.tp_allgather = 1), the all-gather the reference's
+ * multi-GPU plan would use: each layer's attention writes this rank's heads
+ * locally, one ncclAllGather (captured in the step's CUDA graph) collects every
+ * rank's slice and a small kernel lays the rows out for the output projection.
+ * Set-up: one rank calls b2_engine_tp_nccl_id (B2_TP_NCCL_ID_BYTES), every
+ * rank receives that blob (any host transport) and calls
+ * b2_engine_tp_connect_nccl.  Destroying the engine destroys its graphs, then
+ * its communicator. */
+#define B2_TP_NCCL_ID_BYTES 128
+B2_API int b2_engine_tp_nccl_id(void* out);
+B2_API int b2_engine_tp_connect_nccl(b2_engine* eng, const void* id);
 
 /* The engine's paged-block allocator, exposed so its behaviour can be checked
  * against the reference's BlockPool (gpu-engine/src/kv_cache_pool.cpp:6-28):

@@ -33,6 +33,7 @@ struct EngineConfig {
     int tp_rank = 0;  // head-sharded engines (include/b2_engine.h)
     int tp_size = 1;
     int max_prefill_tokens = 0;  // 0: 2048
+    int tp_allgather = 0;        // head-sharded: 0 fused peer stores, 1 ncclAllGather
 };
 
 class Engine {
@@ -47,7 +48,7 @@ public:
         eng_ = nullptr;
         const B2EngineConfig c{cfg.max_batch, cfg.max_seq_len, cfg.kv_block_budget, cfg.dtype,
                                cfg.use_cuda_graphs ? 1 : 0, cfg.device, cfg.tp_rank, cfg.tp_size,
-                               cfg.max_prefill_tokens};
+                               cfg.max_prefill_tokens, cfg.tp_allgather};
         return b2_engine_create(weights_dir.c_str(), &c, &eng_) == B2_OK;
     }
 

@@ -34,6 +34,7 @@ DECODE_SYMBOLS = (
     "b2_add_layernorm", "b2_bias_gelu", "b2_add_bias", "b2_add_one", "b2_embedding", "b2_argmax",
     "b2_paged_attention_noalloc", "b2_argmax_rows", "b2_paged_attention_gather", "b2_tp_barrier",
     "b2_tp_epoch_bump", "b2_linear", "b2_prefill_attention", "b2_paged_attention_host",
+    "b2_tp_barrier_timed", "b2_device_error_word", "b2_raise_device_error",
 )
 
 _c_int, _c_float, _vp = ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
@@ -113,6 +114,12 @@ def load() -> ctypes.CDLL:
     lib.b2_argmax_rows.argtypes = [_c_int, _vp, _vp, ctypes.c_int64, _c_int, _c_int, _vp]
     lib.b2_linear.argtypes = [ctypes.POINTER(LinearArgs), _vp]
     lib.b2_prefill_attention.argtypes = [ctypes.POINTER(PrefillAttnArgs), _vp]
+    lib.b2_paged_attention_noalloc.argtypes = [ctypes.POINTER(PagedAttnArgs), _vp]
+    lib.b2_tp_barrier.argtypes = [_vp, _vp, _c_int, _c_int, _vp, _c_int, _vp]
+    lib.b2_tp_barrier_timed.argtypes = [_vp, _vp, _c_int, _c_int, _vp, _c_int, ctypes.c_uint64, _vp]
+    lib.b2_tp_epoch_bump.argtypes = [_vp, _vp]
+    lib.b2_device_error_word.argtypes = [ctypes.POINTER(ctypes.c_void_p)]
+    lib.b2_raise_device_error.argtypes = [ctypes.c_uint32, _vp]
     _lib = lib
     return lib
 

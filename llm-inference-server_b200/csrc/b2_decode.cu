@@ -713,11 +713,35 @@ int b2_paged_attention_host(const B2PagedAttnArgs* a, const B2AttnHostIO* io, vo
     return B2_OK;
 }
 
-int b2_tp_barrier(uint32_t* local_flags, uint32_t* const* peer_flags, int32_t rank, int32_t n, const uint32_t* epoch,
-                  int32_t slot, b2_stream_t stream) {
+int b2_tp_barrier_timed(uint32_t* local_flags, uint32_t* const* peer_flags, int32_t rank, int32_t n,
+                        const uint32_t* epoch, int32_t slot, uint64_t limit_ns, b2_stream_t stream) {
     if (!local_flags || !peer_flags || !epoch) return fail(B2_ERR_NULL, "local_flags, peer_flags and epoch are required");
     if (n < 1 || n > B2_MAX_GATHER || rank < 0 || rank >= n || slot < 0) return fail(B2_ERR_SHAPE, "bad rank / n / slot");
-    tp_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(local_flags, peer_flags, rank, n, epoch, slot);
+    if (limit_ns == 0 || limit_ns > 60000000000ull) return fail(B2_ERR_SHAPE, "limit_ns must be in (0, 60 s]");
+    tp_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(local_flags, peer_flags, rank, n, epoch, slot,
+                                                                        limit_ns);
+    return launch_status();
+}
+
+int b2_tp_barrier(uint32_t* local_flags, uint32_t* const* peer_flags, int32_t rank, int32_t n, const uint32_t* epoch,
+                  int32_t slot, b2_stream_t stream) {
+    return b2_tp_barrier_timed(local_flags, peer_flags, rank, n, epoch, slot, kTpWaitLimitNs, stream);
+}
+
+int b2_device_error_word(uint32_t** out) {
+    if (out == nullptr) return fail(B2_ERR_NULL, "out is NULL");
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_device_errors);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(static_cast<int>(e), cudaGetErrorString(e));
+    }
+    *out = static_cast<uint32_t*>(p);
+    return B2_OK;
+}
+
+int b2_raise_device_error(uint32_t bits, b2_stream_t stream) {
+    raise_device_error_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(bits);
     return launch_status();
 }
 
@@ -741,12 +765,39 @@ int b2_tp_epoch_bump(uint32_t* epoch, b2_stream_t stream) {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[B2_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-struct NoAllocScratch {
-    std::once_flag once;
-    void* ptr = nullptr;
-    cudaError_t err = cudaSuccess;
-};
-NoAllocScratch g_noalloc_devices[64];
+constexpr int kMaxDevices = 64;
+// Per device: the array's device address once a lookup has succeeded.  A
+// failed lookup is not remembered, so the next call tries again.  The cached
+// address belongs to the device's primary context: after cudaDeviceReset a
+// later call would use a stale address, so this entry point does not support
+// a reset (the header says so).
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(void** out) {
+    int dev = -1;
+    const cudaError_t ge = cudaGetDevice(&dev);
+    if (ge != cudaSuccess) {
+        cudaGetLastError();
+        return fail(static_cast<int>(ge), (std::string("cudaGetDevice failed: ") + cudaGetErrorString(ge)).c_str());
+    }
+    if (dev < 0 || dev >= kMaxDevices)
+        return fail(B2_ERR_DEVICE, "b2_paged_attention_noalloc supports device ordinals 0..63 only");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        // First call on this device (it is current here): its address of the array.
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            g_last_error = std::string("cudaGetSymbolAddress for the built-in scratch failed: ") + cudaGetErrorString(e);
+            return e != cudaSuccess ? static_cast<int>(e) : B2_ERR_DEVICE;
+        }
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return B2_OK;
+}
 }  // namespace
 
 extern "C" int b2_paged_attention_noalloc(const B2PagedAttnArgs* a, b2_stream_t stream) {
@@ -764,16 +815,20 @@ extern "C" int b2_paged_attention_noalloc(const B2PagedAttnArgs* a, b2_stream_t 
                       pl.ws_total, static_cast<unsigned>(B2_NOALLOC_SCRATCH_BYTES));
         return fail(B2_ERR_WORKSPACE, msg);
     }
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(B2_ERR_DEVICE, "no current CUDA device");
-    // First call on this device: its address of the array (the device is current here).
-    NoAllocScratch& s = g_noalloc_devices[dev];
-    std::call_once(s.once, [&s]() { s.err = cudaGetSymbolAddress(&s.ptr, g_noalloc_scratch); });
-    if (s.err != cudaSuccess || s.ptr == nullptr) {
-        g_last_error = std::string("cudaGetSymbolAddress for the built-in scratch failed: ") + cudaGetErrorString(s.err);
-        return s.err != cudaSuccess ? static_cast<int>(s.err) : B2_ERR_DEVICE;
+    void* scratch = nullptr;
+    rc = noalloc_scratch(&scratch);
+    if (rc != B2_OK) return rc;
+    // The array keeps whatever the last call left in it.  A completed call
+    // leaves its piece counters at zero, but one that gave up on a bounded
+    // wait (B2_DEVERR_TIMEOUT) may not, and a stale count would make a later
+    // call merge a sequence too early or never.  So every call clears the
+    // counter region first, on its own stream (no allocation).
+    const cudaError_t me = cudaMemsetAsync(scratch, 0, pl.ws_cnt, static_cast<cudaStream_t>(stream));
+    if (me != cudaSuccess) {
+        cudaGetLastError();
+        return fail(static_cast<int>(me), cudaGetErrorString(me));
     }
-    return b2_paged_attention(a, s.ptr, B2_NOALLOC_SCRATCH_BYTES, stream);
+    return b2_paged_attention(a, scratch, B2_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 extern "C" {

@@ -22,6 +22,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -56,6 +57,9 @@ void cuda_ok(cudaError_t e, const char* what) {
 }
 void cublas_ok(cublasStatus_t s, const char* what) {
     if (s != CUBLAS_STATUS_SUCCESS) throw Error(B2_ERR_DEVICE, std::string(what) + ": cuBLAS status " + std::to_string(s));
+}
+void nccl_ok(ncclResult_t r, const char* what) {
+    if (r != ncclSuccess) throw Error(B2_ERR_DEVICE, std::string(what) + ": " + ncclGetErrorString(r));
 }
 void b2_ok(int rc, const char* what) {
     if (rc != B2_OK) throw Error(rc, std::string(what) + ": " + b2_last_error_string());
@@ -118,6 +122,27 @@ __global__ void gather_step_tables_kernel(int32_t* tables, const int32_t* slot_t
     const int n = min(mbps, seq_lens[b] / B2_BLOCK_TOKENS + 1);
     const int32_t* src = slot_tables + static_cast<size_t>(slots[b]) * mbps;
     for (int j = threadIdx.x; j < n; j += blockDim.x) tables[static_cast<size_t>(b) * mbps + j] = src[j];
+}
+
+// Head-sharded engines with the NCCL all-gather: ncclAllGather leaves the
+// ranks' slices one after another, [rank][row][qd chunks]; the output
+// projection wants each row's slices side by side, [row][rank * qd chunks].
+__global__ void interleave_slices_kernel(uint4* dst, const uint4* src, int rows, int ranks, int qchunks) {
+    const long long total = static_cast<long long>(rows) * ranks * qchunks;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % qchunks);
+        const long long rr = i / qchunks;
+        const int r = static_cast<int>(rr % ranks);
+        const int row = static_cast<int>(rr / ranks);
+        dst[i] = src[(static_cast<long long>(r) * rows + row) * qchunks + c];
+    }
+}
+
+// The step's last launch: the device error word (the one b2_device_errors
+// reads) next to the step's tokens, so one download brings both back.
+__global__ void copy_error_word_kernel(int32_t* dst, const uint32_t* word) {
+    if (threadIdx.x == 0) *dst = static_cast<int32_t>(*word);
 }
 
 // ------------------------------------------------------------- the engine
@@ -188,8 +213,10 @@ struct Engine {
     // Per-step buffers at fixed addresses (CUDA graphs replay them).
     // d_in: [tokens | positions | seq_lens | slots] (max_batch each) and the
     // step's gathered block tables [max_batch][mbps].
+    // d_next / h_next: [max_batch] next tokens, then the device error word.
     int32_t *d_in = nullptr, *d_seq_post = nullptr, *d_next = nullptr;
     int32_t *h_in = nullptr, *h_next = nullptr;  // pinned
+    uint32_t* d_err_word = nullptr;               // libb2decode's device error word
     // Device-resident block tables [num_blocks slots][mbps] (a live sequence
     // holds at least one block, so num_blocks slots always suffice), the free
     // slots, and the (slot, index, block) updates not yet on the device.
@@ -223,6 +250,14 @@ struct Engine {
     uint32_t** d_peer_flags = nullptr;
     std::vector<void*> peer_mapped;  // IPC-opened peer bases, closed at destruction
     bool tp_connected = false;
+    // cfg.tp_allgather == 1: attention writes this rank's slice to d_attn_loc
+    // [max_batch][hl * head_dim], ncclAllGather collects every rank's slice
+    // into d_gath's first half ([rank][row][...]) and a small kernel
+    // interleaves them into the second half ([row][rank * hl * head_dim]),
+    // which the output projection reads.  No peer stores, no flag barrier.
+    bool tp_nccl = false;
+    ncclComm_t nccl = nullptr;
+    void* d_attn_loc = nullptr;
     // Batched prefill (allocated at the first b2_engine_prefill): per-row inputs
     // [tokens | positions | seq_lens | last rows (max_batch) | tables (cap x mbps)],
     // row activations, and the per-sequence tail (last rows, logits, next tokens).
@@ -242,7 +277,11 @@ struct Engine {
 
     ~Engine() {
         if (device >= 0) cudaSetDevice(device);
-        for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+        for (auto& g : graphs) cudaGraphExecDestroy(g.second);  // graphs holding NCCL calls go first
+        if (nccl) {
+            cudaStreamSynchronize(stream);
+            ncclCommDestroy(nccl);
+        }
         if (cublas) cublasDestroy(cublas);
         if (stream) cudaStreamDestroy(stream);
         for (void* p : peer_mapped) cudaIpcCloseMemHandle(p);
@@ -250,7 +289,7 @@ struct Engine {
                             d_attn, d_attn_out, d_ff, d_ff_out, d_logits, attn_ws, tp_weights, d_gath,
                             d_flags, d_epoch, d_peer_outs, d_peer_flags, d_pin, d_pseq_post, d_pnext,
                             p_resid, p_x, p_qkv, p_attn, p_attn_out, p_ff, p_ff_out, p_last, p_logits,
-                            p_attn_ws, d_slot_tables, d_upd};
+                            p_attn_ws, d_slot_tables, d_upd, d_attn_loc};
         for (void* p : dev_ptrs)
             if (p) cudaFree(p);
         if (h_in) cudaFreeHost(h_in);
@@ -316,6 +355,8 @@ struct Engine {
         if (tp > B2_MAX_GATHER || tp_rank < 0 || tp_rank >= tp)
             throw Error(B2_ERR_SHAPE, "tp_size must be 1..8 and tp_rank in [0, tp_size)");
         hl = (s.n_head + tp - 1) / tp;
+        if (cfg.tp_allgather != 0 && cfg.tp_allgather != 1) throw Error(B2_ERR_SHAPE, "tp_allgather must be 0 or 1");
+        tp_nccl = tp > 1 && cfg.tp_allgather == 1;
     }
 
     // Vocabulary rounded up to a multiple of 8: wte (the tied lm_head) gets
@@ -414,8 +455,9 @@ struct Engine {
         free_slots.resize(static_cast<size_t>(num_blocks));
         for (int i = 0; i < num_blocks; ++i) free_slots[static_cast<size_t>(i)] = num_blocks - 1 - i;
         cuda_ok(cudaMalloc(&d_seq_post, B * 4), "malloc seq_lens_post");
-        cuda_ok(cudaMalloc(&d_next, B * 4), "malloc next tokens");
-        cuda_ok(cudaMallocHost(&h_next, B * 4), "pinned next tokens");
+        cuda_ok(cudaMalloc(&d_next, (B + 1) * 4), "malloc next tokens");
+        cuda_ok(cudaMallocHost(&h_next, (B + 1) * 4), "pinned next tokens");
+        b2_ok(b2_device_error_word(&d_err_word), "device error word");
         auto act = [&](void** p, size_t cols, const char* what) { cuda_ok(cudaMalloc(p, static_cast<size_t>(B) * cols * es), what); };
         act(&d_resid, D, "malloc residual");
         act(&d_x, D, "malloc ln out");
@@ -431,6 +473,7 @@ struct Engine {
             cuda_ok(cudaMemsetAsync(d_epoch, 0, 4, stream), "memset epoch");
             cuda_ok(cudaMalloc(&d_peer_outs, 2 * tp * sizeof(void*)), "malloc peer table");
             cuda_ok(cudaMalloc(&d_peer_flags, tp * sizeof(void*)), "malloc peer table");
+            if (tp_nccl) act(&d_attn_loc, static_cast<size_t>(hl) * head_dim, "malloc local attention slice");
         }
         act(&d_attn, D, "malloc attention out");
         act(&d_attn_out, D, "malloc proj out");
@@ -483,7 +526,7 @@ struct Engine {
         const float eps = shape.layer_norm_epsilon;
         b2_stream_t s = stream;
         const char* qkv = static_cast<const char*>(d_qkv);
-        if (tp > 1) b2_ok(b2_tp_epoch_bump(d_epoch, s), "tp_epoch_bump");  // a new step for the barriers
+        if (tp > 1 && !tp_nccl) b2_ok(b2_tp_epoch_bump(d_epoch, s), "tp_epoch_bump");  // a new step for the barriers
         // this step's block tables, gathered from the device-resident slot rows
         gather_step_tables_kernel<<<bucket, 64, 0, stream>>>(in_tables(), d_slot_tables, in_slots(), in_seq_lens(),
                                                               mbps);
@@ -523,7 +566,23 @@ struct Engine {
             // Past layer 0, seq_lens_post, the block tables, q and every key row
             // but the newest were complete before kv_append started.
             if (l > 0) aa.flags = B2_ATTN_NEWEST_ROW_PENDING;
-            if (tp > 1) {
+            if (tp_nccl) {
+                // this rank's heads, then ncclAllGather of every rank's slice and
+                // the interleave into [row][rank slices] for the projection
+                aa.out = d_attn_loc;
+                b2_ok(b2_paged_attention(&aa, attn_ws, attn_ws_bytes, s), "paged_attention");
+                const ncclDataType_t nt = dt == B2_F32 ? ncclFloat32 : (dt == B2_F16 ? ncclFloat16 : ncclBfloat16);
+                nccl_ok(ncclAllGather(d_attn_loc, d_gath, static_cast<size_t>(bucket) * QD, nt, nccl, stream),
+                        "ncclAllGather");
+                const int qchunks = QD * es / 16;
+                void* inter = static_cast<char*>(d_gath) + gath_half_bytes();
+                const long long total = static_cast<long long>(bucket) * tp * qchunks;
+                interleave_slices_kernel<<<static_cast<int>(std::min<long long>((total + 255) / 256, 148 * 8)), 256, 0,
+                                           stream>>>(static_cast<uint4*>(inter), static_cast<const uint4*>(d_gath),
+                                                     bucket, tp, qchunks);
+                cuda_ok(cudaGetLastError(), "interleave gathered slices");
+                gemm(bucket, tp * QD, D, inter, proj_w_pad[static_cast<size_t>(l)], d_attn_out);
+            } else if (tp > 1) {
                 // all-gather in the attention epilogue, then meet the peers
                 const int par = l & 1;  // gathered-buffer half of this layer
                 B2OutputGather g{d_peer_outs + par * tp, tp, static_cast<int64_t>(tp) * QD,
@@ -548,6 +607,27 @@ struct Engine {
         // never read by the argmax)
         gemm(bucket, D, vocab_padded(), d_x, wte, d_logits, vocab_padded());
         b2_ok(b2_argmax_rows(dt, d_next, d_logits, vocab_padded(), bucket, V, s), "argmax");
+        copy_error_word_kernel<<<1, 32, 0, stream>>>(d_next + cfg.max_batch, d_err_word);
+        cuda_ok(cudaGetLastError(), "copy error word");
+    }
+
+    // After a step's synchronisation: a nonzero device error word (a bounded
+    // wait that gave up, a clamped block id, seq_len or token) means the
+    // step's results are invalid.  The word is per device and shared by every
+    // user of libb2decode on it; it is cleared here and the step fails.
+    void check_device_errors(uint32_t bits) {
+        if (bits == 0) return;
+        cuda_ok(cudaMemsetAsync(d_err_word, 0, 4, stream), "clear device error word");
+        cuda_ok(cudaStreamSynchronize(stream), "clear device error word");
+        std::string what;
+        if (bits & B2_DEVERR_BLOCK_ID) what += " block id out of range;";
+        if (bits & B2_DEVERR_SEQ_LEN) what += " seq_len beyond the block table;";
+        if (bits & B2_DEVERR_TIMEOUT) what += " a bounded wait gave up;";
+        if (bits & B2_DEVERR_TOKEN) what += " token id or position out of range;";
+        char hex[16];
+        std::snprintf(hex, sizeof(hex), "0x%x", bits);
+        throw Error(B2_ERR_KERNEL, std::string("device-side error bits ") + hex + ":" + what +
+                                       " the step's tokens are invalid and no sequence advanced");
     }
 
     cudaGraphExec_t graph_for(int bucket) {
@@ -595,8 +675,8 @@ struct Engine {
         cuda_ok(cudaMallocHost(&h_pin, in_ints * 4), "pinned prefill inputs");
         std::memset(h_pin, 0, in_ints * 4);
         cuda_ok(cudaMalloc(&d_pseq_post, static_cast<size_t>(cap) * 4), "malloc prefill seq_lens_post");
-        cuda_ok(cudaMalloc(&d_pnext, static_cast<size_t>(B) * 4), "malloc prefill next tokens");
-        cuda_ok(cudaMallocHost(&h_pnext, static_cast<size_t>(B) * 4), "pinned prefill next tokens");
+        cuda_ok(cudaMalloc(&d_pnext, static_cast<size_t>(B + 1) * 4), "malloc prefill next tokens");
+        cuda_ok(cudaMallocHost(&h_pnext, static_cast<size_t>(B + 1) * 4), "pinned prefill next tokens");
         auto act = [&](void** p, size_t rows, size_t cols, const char* what) {
             cuda_ok(cudaMalloc(p, rows * cols * es), what);
         };
@@ -765,9 +845,13 @@ struct Engine {
         cuda_ok(cudaGetLastError(), "gather last rows");
         gemm(n, D, vocab_padded(), p_last, wte, p_logits, vocab_padded());
         b2_ok(b2_argmax_rows(dt, d_pnext, p_logits, vocab_padded(), n, V, s), "argmax");
+        copy_error_word_kernel<<<1, 32, 0, stream>>>(d_pnext + B, d_err_word);
+        cuda_ok(cudaGetLastError(), "copy error word");
         cuda_ok(cudaMemcpyAsync(h_pnext, d_pnext, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, stream),
                 "download next tokens");
+        cuda_ok(cudaMemcpyAsync(h_pnext + B, d_pnext + B, 4, cudaMemcpyDeviceToHost, stream), "download error word");
         cuda_ok(cudaStreamSynchronize(stream), "prefill");
+        check_device_errors(static_cast<uint32_t>(h_pnext[B]));
         for (int i = 0; i < n; ++i) {
             Seq& q = *sv[static_cast<size_t>(i)];
             const int t = static_cast<int>(q.prompt.size()) - q.prompt_pos;
@@ -873,9 +957,16 @@ struct Engine {
             cuda_ok(cudaGraphLaunch(graph_for(bucket), stream), "cudaGraphLaunch");
         else
             run_step_kernels(bucket);
-        cuda_ok(cudaMemcpyAsync(h_next, d_next, static_cast<size_t>(batch) * 4, cudaMemcpyDeviceToHost, stream),
-                "download next tokens");
+        if (batch < B) {
+            cuda_ok(cudaMemcpyAsync(h_next, d_next, static_cast<size_t>(batch) * 4, cudaMemcpyDeviceToHost, stream),
+                    "download next tokens");
+            cuda_ok(cudaMemcpyAsync(h_next + B, d_next + B, 4, cudaMemcpyDeviceToHost, stream), "download error word");
+        } else {
+            cuda_ok(cudaMemcpyAsync(h_next, d_next, static_cast<size_t>(B + 1) * 4, cudaMemcpyDeviceToHost, stream),
+                    "download next tokens");
+        }
         cuda_ok(cudaStreamSynchronize(stream), "decode step");
+        check_device_errors(static_cast<uint32_t>(h_next[B]));
         for (int i = 0; i < batch; ++i) {
             Seq& q = *sv[static_cast<size_t>(i)];
             if (q.prompt_pos < static_cast<int>(q.prompt.size())) ++q.prompt_pos;
@@ -1185,7 +1276,7 @@ int b2_engine_tp_handle(const b2_engine* eng, void* out) {
 int b2_engine_tp_connect(b2_engine* eng, const void* handles) {
     if (!eng || !handles) return B2_ERR_NULL;
     return guarded([&] {
-        if (eng->tp <= 1) throw Error(B2_ERR_SHAPE, "not a head-sharded engine");
+        if (eng->tp <= 1 || eng->tp_nccl) throw Error(B2_ERR_SHAPE, "not a head-sharded engine with tp_allgather = 0");
         if (eng->tp_connected) throw Error(B2_ERR_SHAPE, "already connected");
         b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
         std::vector<void*> outs(2 * static_cast<size_t>(eng->tp)), flags(static_cast<size_t>(eng->tp));
@@ -1214,6 +1305,29 @@ int b2_engine_tp_connect(b2_engine* eng, const void* handles) {
         b2::eng::cuda_ok(cudaMemcpy(eng->d_peer_flags, flags.data(), flags.size() * sizeof(void*),
                                     cudaMemcpyHostToDevice),
                          "upload peer table");
+        eng->tp_connected = true;
+    });
+}
+
+int b2_engine_tp_nccl_id(void* out) {
+    if (!out) return B2_ERR_NULL;
+    static_assert(sizeof(ncclUniqueId) == B2_TP_NCCL_ID_BYTES, "NCCL id size");
+    return guarded([&] {
+        ncclUniqueId id;
+        b2::eng::nccl_ok(ncclGetUniqueId(&id), "ncclGetUniqueId");
+        std::memcpy(out, &id, sizeof(id));
+    });
+}
+
+int b2_engine_tp_connect_nccl(b2_engine* eng, const void* id) {
+    if (!eng || !id) return B2_ERR_NULL;
+    return guarded([&] {
+        if (!eng->tp_nccl) throw Error(B2_ERR_SHAPE, "not a head-sharded engine with tp_allgather = 1");
+        if (eng->tp_connected) throw Error(B2_ERR_SHAPE, "already connected");
+        b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
+        ncclUniqueId uid;
+        std::memcpy(&uid, id, sizeof(uid));
+        b2::eng::nccl_ok(ncclCommInitRank(&eng->nccl, eng->tp, uid, eng->tp_rank), "ncclCommInitRank");
         eng->tp_connected = true;
     });
 }

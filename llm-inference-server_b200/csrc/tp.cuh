@@ -13,10 +13,10 @@
 
 namespace b2 {
 
-constexpr uint64_t kTpWaitLimitNs = 2000000000ull;  // 2 s: a peer that does not arrive is an error
+constexpr uint64_t kTpWaitLimitNs = 2000000000ull;  // default 2 s: a peer that does not arrive is an error
 
 __global__ void __launch_bounds__(32) tp_barrier_kernel(uint32_t* local_flags, uint32_t* const* peer_flags, int rank,
-                                                        int n, const uint32_t* epoch_ptr, int slot) {
+                                                        int n, const uint32_t* epoch_ptr, int slot, uint64_t limit_ns) {
     const int t = threadIdx.x;
     const uint32_t epoch = *epoch_ptr;
     // Every store this GPU issued before (the attention epilogue's stores into
@@ -28,7 +28,10 @@ __global__ void __launch_bounds__(32) tp_barrier_kernel(uint32_t* local_flags, u
         uint32_t* f = peer_flags[t] + static_cast<size_t>(slot) * n + rank;
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
     }
-    if (t < n) {
+    // A barrier of this device already gave up (a peer that stopped, seen by
+    // an earlier layer of the step): the step is failed, so do not wait again.
+    const bool given_up = (*reinterpret_cast<volatile unsigned int*>(&g_device_errors) & B2_DEVERR_TIMEOUT) != 0u;
+    if (t < n && !given_up) {
         const uint32_t* mine = local_flags + static_cast<size_t>(slot) * n + t;
         const uint64_t t0 = global_timer_ns();
         bool ok = true;
@@ -36,7 +39,7 @@ __global__ void __launch_bounds__(32) tp_barrier_kernel(uint32_t* local_flags, u
             uint32_t v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
             if (static_cast<int>(v - epoch) >= 0) break;  // reached (wrap-safe)
-            if ((it & 63u) == 63u && global_timer_ns() - t0 > kTpWaitLimitNs) {
+            if ((it & 63u) == 63u && global_timer_ns() - t0 > limit_ns) {
                 ok = false;
                 break;
             }
@@ -49,6 +52,12 @@ __global__ void __launch_bounds__(32) tp_barrier_kernel(uint32_t* local_flags, u
 
 __global__ void tp_epoch_bump_kernel(uint32_t* epoch) {
     if (threadIdx.x == 0) *epoch += 1u;
+}
+
+// Sets bits in the device error word from the host's side of a test: error
+// propagation is exercised without making any kernel fail.
+__global__ void raise_device_error_kernel(unsigned int bits) {
+    if (threadIdx.x == 0) flag_error(bits);
 }
 
 }  // namespace b2

@@ -27,12 +27,13 @@ ENGINE_SYMBOLS = (
     "b2_engine_shape", "b2_engine_stream",
     "b2_engine_last_error", "b2_block_pool_create", "b2_block_pool_destroy", "b2_block_pool_allocate",
     "b2_block_pool_free", "b2_block_pool_num_free", "b2_engine_tp_handle", "b2_engine_tp_connect",
-    "b2_engine_prefill",
+    "b2_engine_prefill", "b2_engine_tp_nccl_id", "b2_engine_tp_connect_nccl",
 )
 
 TP_HANDLE_BYTES = 128
+TP_NCCL_ID_BYTES = 128
 
-ERR_POOL, ERR_IO = -8, -9
+ERR_POOL, ERR_IO, ERR_KERNEL = -8, -9, -10
 
 _i32, _vp = ctypes.c_int32, ctypes.c_void_p
 
@@ -41,7 +42,7 @@ class EngineConfig(ctypes.Structure):
     """gpu-engine/include/engine/engine_api.h:9-13 plus dtype, graphs and device."""
     _fields_ = [("max_batch", _i32), ("max_seq_len", _i32), ("kv_block_budget", _i32), ("dtype", _i32),
                 ("use_cuda_graphs", _i32), ("device", _i32), ("tp_rank", _i32), ("tp_size", _i32),
-                ("max_prefill_tokens", _i32)]
+                ("max_prefill_tokens", _i32), ("tp_allgather", _i32)]
 
 
 class ModelShape(ctypes.Structure):
@@ -94,6 +95,8 @@ def load() -> ctypes.CDLL:
     lib.b2_engine_tp_handle.argtypes = [_vp, ctypes.c_char_p]
     lib.b2_engine_tp_connect.argtypes = [_vp, ctypes.c_char_p]
     lib.b2_engine_prefill.argtypes = [_vp, P(_i32), _i32, P(_i32)]
+    lib.b2_engine_tp_nccl_id.argtypes = [ctypes.c_char_p]
+    lib.b2_engine_tp_connect_nccl.argtypes = [_vp, ctypes.c_char_p]
     _lib = lib
     return lib
 
@@ -122,11 +125,12 @@ class Config:
     tp_rank: int = 0   # head-sharded engines: this rank
     tp_size: int = 1   # > 1: heads split over tp_size GPUs (see include/b2_engine.h)
     max_prefill_tokens: int = 0  # prompt tokens per prefill call; 0 = 2048
+    tp_allgather: int = 0  # head-sharded: 0 peer stores fused into attention, 1 ncclAllGather
 
     def to_c(self) -> EngineConfig:
         return EngineConfig(self.max_batch, self.max_seq_len, self.kv_block_budget, self.dtype,
                             1 if self.use_cuda_graphs else 0, self.device, self.tp_rank, self.tp_size,
-                            self.max_prefill_tokens)
+                            self.max_prefill_tokens, self.tp_allgather)
 
 
 class Engine:
@@ -202,6 +206,19 @@ class Engine:
         buf = ctypes.create_string_buffer(TP_HANDLE_BYTES)
         _check(self._lib.b2_engine_tp_handle(self._handle(), buf))
         return buf.raw
+
+    @staticmethod
+    def tp_nccl_id() -> bytes:
+        """A new NCCL unique id (one rank makes it, every rank connects with it)."""
+        buf = ctypes.create_string_buffer(TP_NCCL_ID_BYTES)
+        _check(load().b2_engine_tp_nccl_id(buf))
+        return buf.raw
+
+    def tp_connect_nccl(self, nccl_id: bytes) -> None:
+        """Joins the NCCL communicator of the head-sharded ranks (tp_allgather = 1)."""
+        if len(nccl_id) != TP_NCCL_ID_BYTES:
+            raise ValueError("the NCCL id is TP_NCCL_ID_BYTES bytes")
+        _check(self._lib.b2_engine_tp_connect_nccl(self._handle(), nccl_id))
 
     def tp_connect(self, handles: Sequence[bytes]) -> None:
         """Maps every rank's buffers (handles in rank order, this rank's included)."""

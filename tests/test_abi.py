@@ -113,3 +113,10 @@ def test_row_kernel_host_checks(b2):
     assert lib.b2_argmax(1, None, 16, 2, 100, None) == -1
     for fn in (lib.b2_bias_gelu, lib.b2_add_bias):
         assert fn(1, 16, 16, 16, 0, 768, None) == 0  # empty batch
+
+
+def test_barrier_limit_is_checked_on_the_host(b2):
+    lib = b2.load()
+    assert lib.b2_tp_barrier_timed(16, 32, 0, 2, 48, 0, 0, None) == -3  # zero limit: B2_ERR_SHAPE, no launch
+    assert lib.b2_tp_barrier_timed(16, 32, 0, 2, 48, 0, 61 * 10**9, None) == -3
+    assert lib.b2_tp_barrier_timed(16, 32, 2, 2, 48, 0, 10**6, None) == -3  # rank out of range

@@ -12,7 +12,13 @@ import traceback
 from pathlib import Path
 
 
-def run(rank: int, world: int, model_dir: str, prompts, n_new: int, dtype: int, to_parent, from_parent) -> None:
+def run(rank: int, world: int, model_dir: str, prompts, n_new: int, dtype: int, to_parent, from_parent,
+        absent_rank: int = -1) -> None:
+    """absent_rank >= 0: that rank connects and registers its sequences, then
+    never calls decode_step (it stops between steps, nothing of its own in
+    flight) and closes only when the parent says so; the other ranks try one
+    step, which must fail with B2_ERR_KERNEL once the barrier's bounded wait
+    runs out, and report (code, seconds)."""
     try:
         root = Path(__file__).resolve().parents[1]
         sys.path.insert(0, str(root / "tests"))
@@ -31,6 +37,23 @@ def run(rank: int, world: int, model_dir: str, prompts, n_new: int, dtype: int, 
         handles = from_parent.get(timeout=300)
         eng.tp_connect(handles)
         ids = [eng.add_sequence(p) for p in prompts]
+        if absent_rank >= 0:
+            import time
+            import lis_b200
+            if rank == absent_rank:
+                to_parent.put(("absent", rank, None))
+                from_parent.get(timeout=300)  # the others are done
+                eng.close()
+                return
+            t0 = time.perf_counter()
+            try:
+                eng.decode_step(ids)
+                code = 0
+            except lis_b200.B2Error as e:
+                code = e.code
+            to_parent.put(("failed_step", rank, (code, time.perf_counter() - t0, lis_b200.device_errors())))
+            eng.close()
+            return
         consumed = [0] * len(prompts)
         gen = [[] for _ in prompts]
         while any(len(g) < n_new for g in gen):
