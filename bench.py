@@ -1,10 +1,15 @@
 #!/usr/bin/env python3
-"""Paged-attention decode benchmark (HBM GB/s) for the sm_100a hot path.
+"""Paged-attention decode benchmark (HBM GB/s) and GPT-2 decode tokens/s for the sm_100a hot path.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload mha|gqa]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload mha|gqa|...]
 
-One step = one paged-attention call (the split kernel and its merge kernel)
-over one batch.  Workloads:
+One step = one paged-attention call over one batch.  The default run's line
+also carries the GPT-2 XL-shaped decode step through the engine at the same N
+(`gpt2_xl`: global batch 1024, sequence-sharded; at N >= 2 also
+`gpt2_xl_heads`: head-sharded with the all-gather fused into the attention
+epilogue and with ncclAllGather, plus a greedy-token check of both against one
+GPU) and, at N = 1, the GPT-2 small fp32 greedy job with the reference's own
+CPU path timed on the host cores (`gpt2_small`).  Workloads:
 
   mha (default, the headline): batch 64 per GPU, 12 heads, head_dim 64, fp16
       K/V and q ~ N(0,1) from a seed, context U[128,1024], block size 16,
@@ -316,7 +321,7 @@ def b2_workload(b2, device, seed: int, n_sets: int, pool_blocks: int, batch: int
                                    pool_blocks=pool_blocks, dtype=torch_dtype(), log_uniform=WL.log_uniform)
 
 
-def run_ours(args, rank: int, world: int, dist) -> None:
+def run_ours(args, rank: int, world: int, dist) -> dict | None:
     import torch
     b2 = import_package()
     b2.load()
@@ -370,29 +375,39 @@ def run_ours(args, rank: int, world: int, dist) -> None:
         for s_ in wl.sets:
             s_.args.flags = f
 
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                launch(i)
+        return g
+
     def timed_replay(flags, steps, sampler=None):
+        # Every timed launch comes from a graph: one of all the input sets,
+        # replayed, and one of the first `rem` sets for the remainder -- so no
+        # host launch (and its ~µs of Python overhead) sits in the timed region.
         set_flags(flags)
         for i in range(args.warmup):
             launch(i)
         torch.cuda.synchronize(dev)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(nsets):
-                launch(i)
         full_reps, rem = divmod(steps, nsets)
+        graph = capture(nsets)
+        graph_rem = capture(rem) if rem else None
         graph.replay()
+        if graph_rem is not None:
+            graph_rem.replay()
         barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with (sampler if sampler is not None else ClockSampler(-1)) as clk_:
             ev0.record(stream)
             for _ in range(full_reps):
                 graph.replay()
-            for i in range(rem):
-                launch(i)
+            if graph_rem is not None:
+                graph_rem.replay()
             ev1.record(stream)
             torch.cuda.synchronize(dev)
         barrier()
-        del graph
+        del graph, graph_rem
         return ev0.elapsed_time(ev1), clk_
 
     strict_steps = min(args.steps, 2000)
@@ -508,18 +523,20 @@ def run_ours(args, rank: int, world: int, dist) -> None:
         "gpu_launches": (2 if tc_path else 1) * args.steps,
         "device_errors": errs,
     }
-    print(json.dumps(line), flush=True)
+    return line
 
 
-ENGINE_NAMES = ("gpt2-xl", "gpt2-medium", "gpt2-xl-heads")
+ENGINE_NAMES = ("gpt2-xl", "gpt2-medium", "gpt2-xl-heads", "gpt2-small")
 
 
-def run_engine(args, rank: int, world: int, dist) -> None:
-    """GPT-2 decode tokens/s through b2_engine_decode_step (engine_bench.py)."""
+def engine_result(args, name: str, rank: int, world: int, dist, steps: int, warmup: int, allgather: int = 0,
+                  per_rank_batch: int | None = None) -> dict | None:
+    """GPT-2 decode tokens/s through b2_engine_decode_step (engine_bench.py) on
+    every rank; the whole job's line fields on rank 0, None elsewhere."""
     import torch
     import_package()
     from lis_b200 import engine_bench as EB
-    w = EB.ENGINE_WORKLOADS[args.workload]
+    w = EB.ENGINE_WORKLOADS[name]
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     samplers: list[ClockSampler] = []
@@ -528,7 +545,8 @@ def run_engine(args, rank: int, world: int, dist) -> None:
         samplers.append(ClockSampler(dev.index))
         return samplers[-1]
 
-    r = EB.run(w, args.steps, args.warmup, rank, world, dist, dev, timed_region)
+    r = EB.run(w, steps, warmup, rank, world, dist, dev, timed_region, per_rank_batch=per_rank_batch,
+               allgather=allgather)
     clk = samplers[0]
     for extra in samplers[1:]:
         clk.samples.extend(extra.samples)
@@ -545,46 +563,283 @@ def run_engine(args, rank: int, world: int, dist) -> None:
     tokens = reduce(float(r["tokens"]), tdist.ReduceOp.SUM if dist else None)
     nbytes = reduce(r["bytes"], tdist.ReduceOp.SUM if dist else None)
     if rank != 0:
-        return
+        return None
     peak, peak_kind = measured_peak()
     value = tokens / (t_max * 1e-3)
     achieved = nbytes / (t_max * 1e-3) / 1e9  # whole job, GB/s
     frac = achieved / (peak * world)
-    steps_total = args.steps * r["waves"]
-    es = EB.elem_bytes(w.dtype)
+    steps_total = steps * r["waves"]
+    head_sharded = w.head_sharded and world > 1
     # block-table update scatter, table gather, embedding, per layer LN/append/attention/LN/GELU, final LN,
-    # argmax (+ epoch bump and a barrier per layer when head-sharded)
-    ours_per_step = 2 + 1 + 5 * w.n_layer + 2 + (1 + w.n_layer if w.head_sharded and world > 1 else 0)
-    line = {
+    # argmax, error-word copy (+ per layer a barrier and an epoch bump per step when head-sharded with the
+    # fused epilogue; an interleave kernel per layer with NCCL)
+    ours_per_step = 2 + 1 + 5 * w.n_layer + 3
+    if head_sharded:
+        ours_per_step += w.n_layer if allgather else 1 + w.n_layer
+    if head_sharded:
+        par = (f"head-sharded x{world}: " + ("attention output all-gathered with ncclAllGather (captured in the "
+                                             "step graph) and interleaved for the projection" if allgather else
+                                             "attention output all-gathered over NVLink in the attention epilogue, "
+                                             "one flag barrier per layer"))
+    else:
+        par = f"sequence-sharded x{world}, one engine and KV pool per GPU, no collective"
+    return {
         "metric": "GPT-2 decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_max / steps_total, 4),
+        "steps": steps, "warmup": warmup, "ms_per_step": round(t_max / steps_total, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": {BF16_CODE: "bf16", 1: "f16", 0: "f32"}[w.dtype], "data": "synthetic",
         "config": {"workload": w.description, "name": w.name, "global_batch": w.global_batch,
                    "per_gpu_batch": r["per_rank"], "waves_per_gpu": r["waves"], "wave": r["wave"],
                    "l2": "inputs larger than L2: every step reads all weights (GB) and every cached KV row",
-                   "parallelism": (f"head-sharded x{world}: attention output all-gathered over NVLink in the "
-                                   "attention epilogue, one flag barrier per layer" if w.head_sharded else
-                                   f"sequence-sharded x{world}, one engine and KV pool per GPU, no collective")},
+                   "parallelism": par},
         "roofline": {"bound": "hbm", "achieved": round(achieved / world, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(frac, 4), "peak_kind": peak_kind, "traffic": None,
                      "traffic_note": "per GPU; algorithmic bytes per step = all weights + every cached K/V row "
                                      "of every layer + the appended rows",
                      "roofline_tok_s": round(value / frac, 1)},
-        "cpu_baseline": None,
         "e2e": {"value": round(value, 1), "unit": "tok/s",
                 # tokens, positions, seq_lens and table slots (4 int32 per sequence) + one 12-byte
                 # (slot, index, block) update per newly allocated block: one per sequence every 16 steps
                 "h2d_bytes_per_step": 16 * r["wave"] + (12 * r["wave"] + 15) // 16,
-                "d2h_bytes_per_step": 4 * r["wave"],
+                "d2h_bytes_per_step": 4 * r["wave"] + 4,
                 "path": "value is already end to end: b2_engine_decode_step (device-resident block tables updated "
-                        "incrementally, one upload of the step inputs, graph replay, download of next tokens, "
-                        "stream sync) timed with CUDA events on the engine stream"},
+                        "incrementally, one upload of the step inputs, graph replay, download of next tokens and "
+                        "the device error word, stream sync) timed with CUDA events on the engine stream"},
         "clocks": clk.summary(),
         "gpu_launches": ours_per_step * steps_total,
-        "elem_bytes": es,
     }
-    print(json.dumps(line), flush=True)
+
+
+def tp_token_check(rank: int, world: int, dist, modes=(0, 1)) -> dict | None:
+    """Greedy tokens of the head-sharded engine (every rank, both all-gather
+    modes) against the one-GPU engine (rank 0) on the same synthetic GPT-2
+    XL-shaped model and prompts.  f32, so a greedy choice cannot flip on
+    rounding: the GEMMs of the two layouts reduce in different orders.  16
+    prompts of 8 random tokens, 16 generated tokens each."""
+    import torch
+    import_package()
+    from lis_b200 import engine as E
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    shape = E.ModelShape(n_layer=48, n_head=25, d_model=1600, vocab_size=50257, n_ctx=1024, layer_norm_epsilon=1e-5,
+                         eos_token_id=-1)
+    rng = np.random.Generator(np.random.PCG64(77))
+    plen, n_new = 8, 16
+    prompts = [rng.integers(0, shape.vocab_size, size=plen).tolist() for _ in range(16)]
+
+    def greedy(tp_size: int, mode: int) -> list[list[int]]:
+        eng = E.Engine()
+        eng.init_synthetic(shape, E.Config(max_batch=len(prompts), max_seq_len=64, kv_block_budget=96, dtype=0,
+                                           use_cuda_graphs=True, device=dev.index,
+                                           tp_rank=rank if tp_size > 1 else 0, tp_size=tp_size, tp_allgather=mode),
+                           seed=3, std=0.02)
+        if tp_size > 1 and mode:
+            box = [E.Engine.tp_nccl_id() if rank == 0 else None]
+            dist.broadcast_object_list(box, src=0)
+            eng.tp_connect_nccl(box[0])
+        elif tp_size > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, eng.tp_handle())
+            eng.tp_connect(handles)
+        ids = [eng.add_sequence(p) for p in prompts]
+        gen = [[] for _ in prompts]
+        for step in range(plen + n_new - 1):  # equal prompt lengths: every sequence moves in lockstep
+            out = eng.decode_step(ids)
+            if step >= plen - 1:
+                for g, t in zip(gen, out):
+                    g.append(int(t))
+        eng.close()
+        return gen
+
+    sharded = {m: greedy(world, m) for m in modes}
+    if dist is not None:
+        dist.barrier()
+    if rank != 0:
+        return None
+    full = greedy(1, 0)
+    res = {"dtype": "f32", "prompts": len(prompts), "prompt_len": plen, "new_tokens": n_new,
+           "model": "GPT-2 XL shape (48 layers, 25 heads, d_model 1600), synthetic weights N(0,0.02)"}
+    for m, gen in sharded.items():
+        same = sum(a == b for ga, gb in zip(gen, full) for a, b in zip(ga, gb))
+        key = "nccl" if m else "fused"
+        res[f"tokens_match_{key}"] = same == len(prompts) * n_new
+        res[f"tokens_equal_{key}"] = f"{same}/{len(prompts) * n_new}"
+    return res
+
+
+def engine_records(args, rank: int, world: int, dist) -> dict:
+    """The GPT-2 XL decode records attached to the default bench line: the
+    sequence-sharded step at N GPUs, and at N >= 2 the head-sharded step with
+    its two all-gather implementations and the token check."""
+    steps, warmup = min(args.steps, 20), 3
+    out: dict = {}
+    xl = engine_result(args, "gpt2-xl", rank, world, dist, steps, warmup)
+    if rank == 0:
+        out["gpt2_xl"] = xl
+    if world >= 2:
+        fused = engine_result(args, "gpt2-xl-heads", rank, world, dist, steps, warmup, allgather=0)
+        nccl = engine_result(args, "gpt2-xl-heads", rank, world, dist, steps, warmup, allgather=1)
+        check = tp_token_check(rank, world, dist)
+        if rank == 0:
+            out["gpt2_xl_heads"] = {"fused_epilogue": fused, "nccl_allgather": nccl, "token_check": check,
+                                    "fused_vs_nccl": round(fused["value"] / nccl["value"], 4)}
+    return out
+
+
+def gpt2_small_cpu(model_dir: str, prompts, n_new: int, nthreads: int, sample_new: int) -> dict:
+    """The reference's CPUModel::greedy_generate (cpu_model.cpp:198-216, built
+    from the reference's sources into oracle/_ref) on the host cores: the whole
+    job on min(prompts, cores) threads (one CPUModel per thread, one prompt
+    each), and a 1-thread sample of the shortest prompt with sample_new new
+    tokens, scaled to the job by its forward steps."""
+    from oracle import oracle as O
+    gen, secs = O.ref_greedy_generate(model_dir, prompts, n_new, n_threads=nthreads)
+    short = min(prompts, key=len)
+    _, secs1 = O.ref_greedy_generate(model_dir, [short], sample_new, n_threads=1)
+    steps1 = len(short) + sample_new - 1
+    job_steps = sum(len(p) + n_new - 1 for p in prompts)
+    est1 = secs1 / steps1 * job_steps
+    return {"tokens": gen, "value": round(len(prompts) * n_new / secs, 3), "secs": secs,
+            "one_thread_tok_s": round(len(prompts) * n_new / est1, 3),
+            "one_thread_sample": f"1 prompt of {len(short)} tokens + {sample_new} new on 1 thread in {secs1:.2f} s "
+                                 f"({steps1 / secs1:.2f} forward steps/s), scaled to the job's {job_steps} steps"}
+
+
+def cpu_model_name() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_gpt2_small(args, rank: int, world: int, cpu: bool = True) -> dict | None:
+    """GPT-2 small fp32 greedy decode (8 prompts of U[16,128] random tokens,
+    64 new tokens each, weights N(0,0.02) seed 0 in the reference exporter's
+    format): one step is the whole job through the engine's public calls --
+    add_sequence, one b2_engine_prefill (first token), 63 decode_steps --
+    timed with CUDA events on the engine stream.  The tokens are checked
+    against the reference CPUModel's (committed fixture), and the reference's
+    own CPU path is timed on the host cores as the baseline.  Rank 0 only."""
+    if rank != 0:
+        return None
+    import torch
+    import_package()
+    from lis_b200 import engine as E
+    from lis_b200 import model_files as MF
+    fx = json.loads((ROOT / "tests" / "golden" / "gpt2_small_greedy.json").read_text())
+    prompts, n_new = fx["prompts"], fx["n_new"]
+    mdir = ROOT / "_models" / f"gpt2_small_seed{fx['seed']}"
+    if not (mdir / "weights.bin").exists():
+        MF.write_model_dir(mdir, MF.GPT2_SMALL, seed=fx["seed"], std=fx["std"])
+    torch.cuda.set_device(0)
+    eng = E.Engine()
+    total = sum(len(p) for p in prompts)
+    if not eng.init(str(mdir), E.Config(max_batch=len(prompts), max_seq_len=1024, kv_block_budget=1024, dtype=0,
+                                         use_cuda_graphs=True, device=0, max_prefill_tokens=max(2048, total))):
+        raise RuntimeError(eng.last_error())
+    stream = torch.cuda.ExternalStream(eng.stream_handle(), device=torch.device("cuda:0"))
+
+    def job():
+        ids = [eng.add_sequence(p) for p in prompts]
+        gen = [[t] for t in eng.prefill(ids)]
+        for _ in range(n_new - 1):
+            for g, t in zip(gen, eng.decode_step(ids)):
+                g.append(t)
+        for i in ids:
+            eng.free_sequence(i)
+        return gen
+
+    steps, warmup = min(args.steps, 10), max(3, min(args.warmup, 5))
+    for _ in range(warmup):
+        gen = job()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        ev0.record(stream)
+        for _ in range(steps):
+            gen = job()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    eng.close()
+    match = sum(g == want[:n_new] for g, want in zip(gen, fx["generated"]))
+    rec = {"metric": "GPT-2 small fp32 greedy tok/s", "value": round(len(prompts) * n_new / (ms * 1e-3), 1),
+           "unit": "tok/s", "n_gpus": 1, "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 3),
+           "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "GPT-2 small (12 layers, 12 heads, d_model 768, vocab 50257), fp32, weights "
+                                  "N(0,0.02) seed 0, LN gamma 1 beta 0; 8 prompts of U[16,128] random token ids, "
+                                  "64 greedy tokens each; one step = add_sequence x8, b2_engine_prefill, 63 "
+                                  "b2_engine_decode_step", "prompt_tokens": total},
+           "tokens_match_reference": f"{match}/{len(prompts)} prompts identical to CPUModel::greedy_generate",
+           "clocks": clk.summary(), "cpu_baseline": None}
+    if cpu:
+        from oracle import oracle as O
+        if O.ref_available():
+            nth = min(len(prompts), os.cpu_count() or 1)
+            c = gpt2_small_cpu(str(mdir), prompts, n_new, nth, sample_new=8)
+            rec["cpu_baseline"] = {
+                "value": c["value"], "unit": "tok/s", "cores": nth, "kind": "reference",
+                "cpu_model": cpu_model_name(), "host_cores": os.cpu_count(),
+                "sample": f"the whole job (8 prompts x 64 tokens) by the reference CPUModel::greedy_generate, one "
+                          f"CPUModel per thread, {nth} threads, {c['secs']:.1f} s; tokens identical to the GPU run: "
+                          f"{c['tokens'] == gen}",
+                "one_thread": {"value": c["one_thread_tok_s"], "unit": "tok/s", "sample": c["one_thread_sample"]}}
+        else:
+            rec["cpu_baseline_note"] = "oracle/_ref/libref_cpu.so (the reference CPU path) is not built here"
+    return rec
+
+
+def run_gpt2_small_reference(args, rank: int) -> None:
+    """--impl reference --workload gpt2-small: the reference's own CPU forward
+    path, CPUModel::greedy_generate (built from its sources into oracle/_ref),
+    on the host cores -- the same 8 prompts x 64 tokens job, metric and unit as
+    our arm.  Each step is the whole job on min(8, cores) threads.  Rank 0."""
+    if rank != 0:
+        return
+    import_package()
+    from lis_b200 import model_files as MF
+    from oracle import oracle as O
+    if not O.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_cpu.so (the reference CPUModel "
+                          "compiled from its sources) is not built"}), flush=True)
+        return
+    fx = json.loads((ROOT / "tests" / "golden" / "gpt2_small_greedy.json").read_text())
+    prompts, n_new = fx["prompts"], fx["n_new"]
+    mdir = ROOT / "_models" / f"gpt2_small_seed{fx['seed']}"
+    if not (mdir / "weights.bin").exists():
+        MF.write_model_dir(mdir, MF.GPT2_SMALL, seed=fx["seed"], std=fx["std"])
+    nth = min(len(prompts), os.cpu_count() or 1)
+    # each step is the whole job; bound the run: at most a few steps of it
+    steps, warmup = min(args.steps, 3), min(args.warmup, 1)
+    for _ in range(warmup):
+        O.ref_greedy_generate(str(mdir), prompts, n_new, n_threads=nth)
+    secs = 0.0
+    for _ in range(steps):
+        _, t = O.ref_greedy_generate(str(mdir), prompts, n_new, n_threads=nth)
+        secs += t
+    value = round(len(prompts) * n_new * steps / secs, 3)
+    sample = (f"the whole job per step (8 prompts x 64 greedy tokens), CPUModel::greedy_generate with one CPUModel "
+              f"per thread on {nth} threads ({cpu_model_name()}); {steps} timed of the requested {args.steps} "
+              f"steps, {warmup} warm-up")
+    print(json.dumps({"metric": "GPT-2 small fp32 greedy tok/s", "value": value, "unit": "tok/s", "impl": "reference",
+                      "n_gpus": 1, "steps": steps, "warmup": warmup, "ms_per_step": round(secs / steps * 1e3, 3),
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                      "data": "synthetic", "config": {"workload": "GPT-2 small fp32 greedy, 8 prompts x 64 tokens"},
+                      "cpu_baseline": {"value": value, "unit": "tok/s", "cores": nth, "kind": "reference",
+                                       "sample": sample},
+                      "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
+def run_engine(args, rank: int, world: int, dist) -> None:
+    """One engine workload as the bench line (--workload gpt2-xl | gpt2-medium | gpt2-xl-heads)."""
+    line = engine_result(args, args.workload, rank, world, dist, args.steps, args.warmup,
+                         allgather=args.allgather, per_rank_batch=args.batch)
+    if line is not None:
+        line["cpu_baseline"] = None
+        print(json.dumps(line), flush=True)
 
 
 BF16_CODE = 2
@@ -661,30 +916,37 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (default 50; 3 for engine workloads)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample duration")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--no-engine", action="store_true",
+                    help="default workload: skip the GPT-2 records attached to the attention line")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + list(ENGINE_NAMES) + ["serve-medium", "prefill-medium"],
                     default="mha",
-                    help="mha: the headline microbench; gqa: grouped-query long contexts (tensor-core kernel); "
-                         "gpt2-xl / gpt2-medium: GPT-2 decode tokens/s through the engine")
+                    help="mha: the headline microbench (+ GPT-2 XL / small decode records); gqa: grouped-query long "
+                         "contexts (tensor-core kernel); gpt2-xl / gpt2-medium / gpt2-xl-heads: GPT-2 decode "
+                         "tokens/s through the engine; gpt2-small: the fp32 greedy job against the reference CPU")
     ap.add_argument("--sets", type=int, default=None, help="rotating input sets (profiling uses fewer)")
     ap.add_argument("--pool-blocks", type=int, default=None, help="KV pool size in blocks (profiling uses fewer)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (profiling uses fewer)")
+    ap.add_argument("--allgather", type=int, choices=[0, 1], default=0,
+                    help="gpt2-xl-heads: 0 all-gather fused into the attention epilogue, 1 ncclAllGather")
     ap.add_argument("--requests", type=int, default=200, help="serve-medium: requests in the trace")
     ap.add_argument("--requests-compare", type=int, default=24,
                     help="serve-medium: requests replayed with both prefill modes")
     args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
     engine = args.workload in ENGINE_NAMES
     if args.workload == "serve-medium":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the serving trace has no CPU arm"}), flush=True)
             return
-        run_serve(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
+        run_serve(args, rank, world)
         return
     if args.workload == "prefill-medium":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the reference has no batched prefill"}), flush=True)
             return
-        run_prefill(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
+        run_prefill(args, rank, world)
         return
     if args.steps is None:
         args.steps = 20 if engine else 5000
@@ -696,13 +958,15 @@ def main() -> None:
     if not engine:
         WL = WORKLOADS[args.workload]
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
+        if args.workload == "gpt2-small":
+            run_gpt2_small_reference(args, rank)
+            return
         if engine:
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": "the reference CPU arm is timed for the "
-                                  "attention workloads; engine workloads report no CPU arm"}), flush=True)
+                                  "attention workloads and gpt2-small; the GPT-2 XL / medium shapes have no CPU "
+                                  "arm"}), flush=True)
             return
         run_reference_arm(args, rank, world)
         return
@@ -713,13 +977,34 @@ def main() -> None:
         import torch
         import torch.distributed as tdist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist
     try:
-        if engine:
+        if args.workload == "gpt2-small":
+            rec = run_gpt2_small(args, rank, world, cpu=not args.no_cpu)
+            if rec is not None:
+                rec.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                            "e2e": {"value": rec["value"], "unit": "tok/s", "h2d_bytes_per_step": None,
+                                    "d2h_bytes_per_step": None, "path": "already end to end through "
+                                    "b2_engine_add_sequence / b2_engine_prefill / b2_engine_decode_step"}})
+                print(json.dumps(rec), flush=True)
+        elif engine:
             run_engine(args, rank, world, dist)
         else:
-            run_ours(args, rank, world, dist)
+            line = run_ours(args, rank, world, dist)
+            import gc
+
+            import torch
+            gc.collect()
+            torch.cuda.empty_cache()
+            if WL.name == "mha" and not args.no_engine:
+                extra = engine_records(args, rank, world, dist)
+                if world == 1:
+                    extra["gpt2_small"] = run_gpt2_small(args, rank, world, cpu=not args.no_cpu)
+                if rank == 0:
+                    line.update(extra)
+            if rank == 0:
+                print(json.dumps(line), flush=True)
     finally:
         if dist is not None:
             dist.destroy_process_group()

@@ -91,9 +91,13 @@ def step_bytes(w: EngineWorkload, ctx: np.ndarray, world: int = 1) -> float:
     return float(weights * es + (ctx.astype(np.float64) + 1).sum() * kv_row)
 
 
-def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist, device, timed_region=None) -> dict:
+def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist, device, timed_region=None,
+        per_rank_batch: int | None = None, allgather: int = 0) -> dict:
     """Runs the workload's waves on this rank; timed_region() (optional) gives a
-    context manager entered around each wave's timed steps."""
+    context manager entered around each wave's timed steps.  per_rank_batch
+    overrides the sequences per rank (profiling one GPU's share of a larger
+    job).  allgather (head-sharded only): 0 = the attention epilogue stores
+    into every rank's gathered buffer over NVLink; 1 = ncclAllGather."""
     import torch
 
     from . import engine as E
@@ -104,6 +108,8 @@ def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist,
     if w.global_batch % world:
         raise ValueError(f"global batch {w.global_batch} does not split over {world} ranks")
     per_rank = w.global_batch if sharded else w.global_batch // world
+    if per_rank_batch:
+        per_rank = per_rank_batch
     wave = min(per_rank, w.wave_cap)
     n_waves = (per_rank + wave - 1) // wave
     total = warmup + steps
@@ -119,9 +125,14 @@ def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist,
     eng = E.Engine()
     eng.init_synthetic(shape, E.Config(max_batch=wave, max_seq_len=w.n_ctx, kv_block_budget=blocks_needed + 64,
                                        dtype=w.dtype, use_cuda_graphs=True, device=device.index,
-                                       tp_rank=rank if sharded else 0, tp_size=world if sharded else 1),
+                                       tp_rank=rank if sharded else 0, tp_size=world if sharded else 1,
+                                       tp_allgather=allgather if sharded else 0),
                        seed=1, std=0.02)
-    if sharded:
+    if sharded and allgather:
+        ids_box = [E.Engine.tp_nccl_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids_box, src=0)
+        eng.tp_connect_nccl(ids_box[0])
+    elif sharded:
         handles = [None] * world
         dist.all_gather_object(handles, eng.tp_handle())
         eng.tp_connect(handles)
