@@ -234,6 +234,73 @@ __device__ __forceinline__ unsigned count_piece(unsigned* counter) {
     return old;
 }
 
+// Before griddepcontrol.wait, when the inputs may still be written by the
+// kernel ahead of this one (p.early == 0): runs the prologue on whatever
+// seq_lens and block tables hold now and asks for this CTA's first K/V rows
+// (up to two paged blocks of its first sequence) and that sequence's q row to
+// be brought into L2.  Every value it reads may be stale; it only decides
+// which addresses to prefetch, and a prefetch into L2 changes no value any
+// thread reads afterwards (L2 is where all reads and writes meet; these loads
+// bypass L1).  After the wait, the real prologue's dependent loads and the
+// first stages then come from L2 instead of DRAM.  Uses misc[0..34]; ends with
+// a CTA barrier.
+template <int DH>
+__device__ __forceinline__ void speculative_prefetch(const AttnParams& p, int* misc, int es) {
+    const int tid = threadIdx.x;
+    const int B = p.batch;
+    const int per = (B + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
+    const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
+    int local = 0;
+    for (int b = b_lo; b < b_hi; ++b) local += clamp_seq_len(__ldcg(p.seq_lens + b), p.mbps);
+    if (tid == 0) misc[0] = -1;
+    int N = 0;
+    const int excl = block_exclusive_scan(local, misc + 2, &N);  // its barriers also order misc[0] = -1
+    const int G = min(static_cast<int>(gridDim.x), max(N, 1));
+    const int cta = blockIdx.x;
+    const long long s_unit = cta < G ? static_cast<long long>(cta) * N / G : 0;
+    const long long e_unit = cta < G ? static_cast<long long>(cta + 1) * N / G : 0;
+    int run = excl;
+    for (int b = b_lo; b < b_hi; ++b) {
+        const int cl = clamp_seq_len(__ldcg(p.seq_lens + b), p.mbps);
+        if (cl > 0 && run <= s_unit && s_unit < run + cl) {
+            misc[0] = b;
+            misc[1] = run;
+        }
+        run += cl;
+    }
+    __syncthreads();
+    const int b0 = misc[0];
+    if (tid < 32 && b0 >= 0 && e_unit > s_unit) {
+        const int lane = tid;
+        const int cs = clamp_seq_len(__ldcg(p.seq_lens + b0), p.mbps);
+        const int t_lo = static_cast<int>(s_unit - misc[1]);
+        const int t_hi = static_cast<int>(min(e_unit - misc[1], static_cast<long long>(cs)));
+        const int j0 = t_lo / kBlockTokens;
+        const size_t row_elems = static_cast<size_t>(p.n_kv_head) * DH;
+        const size_t slab_elems = row_elems * kBlockTokens;
+        if (lane < 2) {
+            const int j = j0 + lane;
+            const int r_lo = max(t_lo - j * kBlockTokens, 0);
+            const int r_hi = min(t_hi - j * kBlockTokens, kBlockTokens);
+            if (r_hi > r_lo) {
+                const int blk = __ldcg(p.block_tables + static_cast<size_t>(b0) * p.mbps + j);
+                if (blk >= 0 && blk < p.num_blocks) {
+                    const char* src = static_cast<const char*>(p.pool) +
+                                      ((static_cast<size_t>(blk) * p.n_layer + p.layer_idx) * 2 * slab_elems +
+                                       static_cast<size_t>(r_lo) * row_elems) * es;
+                    const uint32_t bytes = static_cast<uint32_t>((r_hi - r_lo) * row_elems * es);
+                    bulk_prefetch_l2(src, bytes);
+                    bulk_prefetch_l2(src + slab_elems * es, bytes);
+                }
+            }
+        } else if (lane == 2) {
+            bulk_prefetch_l2(static_cast<const char*>(p.q) + static_cast<size_t>(b0) * p.q_row_stride * es,
+                             static_cast<uint32_t>(p.n_head * DH * es));
+        }
+    }
+    __syncthreads();
+}
+
 // Shared-memory ring between the softmax threads and the bookkeeping warp:
 // one entry per finished sequence piece.
 constexpr int kPieceRing = 8;
@@ -287,13 +354,19 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     // -- and, with p.early == 2, the producer before reading each sequence's
     // newest key row.
     pdl_launch_dependents();
-    if (p.early == 0) pdl_wait();
+    if (p.early == 0) {
+        __syncthreads();  // the barriers are initialised before misc is reused below
+        speculative_prefetch<DH>(p, misc, ES);
+        pdl_wait();
+    }
 
     // ---- prologue: per-sequence row counts, global prefix, this CTA's range
+    // (L2 loads: with p.early == 0 the speculative pass may have read these
+    // addresses before the wait, so nothing may come from a stale L1 line)
     const int per = (B + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
     const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
     int local = 0;
-    for (int b = b_lo; b < b_hi; ++b) local += clamp_seq_len(__ldg(p.seq_lens + b), p.mbps);
+    for (int b = b_lo; b < b_hi; ++b) local += clamp_seq_len(__ldcg(p.seq_lens + b), p.mbps);
     int N = 0;
     const int excl = block_exclusive_scan(local, misc + 2, &N);
     const int G = min(static_cast<int>(gridDim.x), max(N, 1));
@@ -302,7 +375,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     {
         int run = excl;
         for (int b = b_lo; b < b_hi; ++b) {
-            const int raw = __ldg(p.seq_lens + b);
+            const int raw = __ldcg(p.seq_lens + b);
             const int cl = clamp_seq_len(raw, p.mbps);
             if (cl > 0 && run <= s_unit && s_unit < run + cl) {
                 misc[0] = b;
@@ -349,7 +422,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         while (u < e_unit && !failed && bb < B) {
             const int b = bb + lane;
             int cl = 0;
-            if (b < B) cl = clamp_seq_len(__ldg(p.seq_lens + b), p.mbps);
+            if (b < B) cl = clamp_seq_len(__ldcg(p.seq_lens + b), p.mbps);
             int incl = cl;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
@@ -372,7 +445,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                     const int jj = jc + lane;
                     int blk_l = 0;
                     if (jj < j1) {
-                        blk_l = __ldg(p.block_tables + static_cast<size_t>(bs) * p.mbps + jj);
+                        blk_l = __ldcg(p.block_tables + static_cast<size_t>(bs) * p.mbps + jj);
                         if (blk_l < 0 || blk_l >= p.num_blocks) {
                             flag_error(B2_DEVERR_BLOCK_ID);
                             blk_l = 0;

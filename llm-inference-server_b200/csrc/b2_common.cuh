@@ -285,6 +285,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Asks the TMA engine to bring [src, src + bytes) into L2 (no destination, no
+// completion): a hint that cannot change any value read later, since L2 is
+// where every SM's reads and writes meet.  src 16-byte aligned, bytes a
+// multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Named barrier over the first nthreads threads of the CTA (multiple of 32).
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
