@@ -530,7 +530,7 @@ ENGINE_NAMES = ("gpt2-xl", "gpt2-medium", "gpt2-xl-heads", "gpt2-small")
 
 
 def engine_result(args, name: str, rank: int, world: int, dist, steps: int, warmup: int, allgather: int = 0,
-                  per_rank_batch: int | None = None) -> dict | None:
+                  per_rank_batch: int | None = None, linear: bool | None = None) -> dict | None:
     """GPT-2 decode tokens/s through b2_engine_decode_step (engine_bench.py) on
     every rank; the whole job's line fields on rank 0, None elsewhere."""
     import torch
@@ -545,8 +545,9 @@ def engine_result(args, name: str, rank: int, world: int, dist, steps: int, warm
         samplers.append(ClockSampler(dev.index))
         return samplers[-1]
 
+    linear = bool(getattr(args, "linear", 0)) if linear is None else linear
     r = EB.run(w, steps, warmup, rank, world, dist, dev, timed_region, per_rank_batch=per_rank_batch,
-               allgather=allgather)
+               allgather=allgather, linear=linear)
     clk = samplers[0]
     for extra in samplers[1:]:
         clk.samples.extend(extra.samples)
@@ -929,6 +930,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (profiling uses fewer)")
     ap.add_argument("--allgather", type=int, choices=[0, 1], default=0,
                     help="gpt2-xl-heads: 0 all-gather fused into the attention epilogue, 1 ncclAllGather")
+    ap.add_argument("--linear", type=int, choices=[0, 1], default=0,
+                    help="engine workloads: decode GEMMs on b2_linear (tcgen05) instead of cuBLAS")
     ap.add_argument("--requests", type=int, default=200, help="serve-medium: requests in the trace")
     ap.add_argument("--requests-compare", type=int, default=24,
                     help="serve-medium: requests replayed with both prefill modes")

@@ -110,6 +110,12 @@ B2_API int b2_engine_prefill(b2_engine* eng, const int32_t* seq_ids, int32_t n, 
  * bf16 models of head_dim 64).  0 selects the decode-attention rows instead. */
 B2_API int b2_engine_set_prefill_tensor_cores(b2_engine* eng, int32_t enabled);
 
+/* The decode step's linear layers on b2_linear (tcgen05, weights streamed
+ * while the kernel before it runs, bias + GELU fused into the FC layer) for
+ * f16 / bf16 models and batches of at most 256 rows; cuBLAS otherwise (and
+ * for the lm_head).  Default off.  Switching drops the captured graphs. */
+B2_API int b2_engine_set_linear_tensor_cores(b2_engine* eng, int32_t enabled);
+
 /* Engine::free_sequence: returns the sequence's blocks; unknown ids are ignored. */
 B2_API int b2_engine_free_sequence(b2_engine* eng, int32_t seq_id);
 

@@ -17,17 +17,31 @@
 
 #include <cstddef>
 #include <stdexcept>
+#include <cstdlib>
 #include <string>
 
 #include "b2_engine.h"
 
 namespace b2 {
 
+// The storage dtype an EngineConfig starts with: B2_F16 (the reference engine
+// is fp16), or what the B2_ENGINE_DTYPE environment variable names ("f32",
+// "f16", "bf16") -- so a caller that builds its config without naming a dtype
+// (the reference's GpuEngineGenerator) can still run an f32 or bf16 engine.
+inline int default_engine_dtype() {
+    const char* v = std::getenv("B2_ENGINE_DTYPE");
+    if (v == nullptr) return B2_F16;
+    const std::string s(v);
+    if (s == "f32") return B2_F32;
+    if (s == "bf16") return B2_BF16;
+    return B2_F16;
+}
+
 struct EngineConfig {
     int max_batch = 8;
     int max_seq_len = 1024;
     int kv_block_budget = 4096;
-    int dtype = B2_F16;  // the reference engine is fp16
+    int dtype = default_engine_dtype();
     bool use_cuda_graphs = true;
     int device = -1;  // -1: the device current on the calling thread
     int tp_rank = 0;  // head-sharded engines (include/b2_engine.h)

@@ -263,6 +263,7 @@ struct Engine {
     // row activations, and the per-sequence tail (last rows, logits, next tokens).
     int prefill_cap = 0;
     bool prefill_tc = true;  // b2_engine_set_prefill_tensor_cores
+    bool linear_tc = false;  // b2_engine_set_linear_tensor_cores
     int32_t *d_pin = nullptr, *h_pin = nullptr, *d_pseq_post = nullptr, *d_pnext = nullptr, *h_pnext = nullptr;
     void *p_resid = nullptr, *p_x = nullptr, *p_qkv = nullptr, *p_attn = nullptr, *p_attn_out = nullptr,
          *p_ff = nullptr, *p_ff_out = nullptr, *p_last = nullptr, *p_logits = nullptr, *p_attn_ws = nullptr;
@@ -513,7 +514,40 @@ struct Engine {
     // Row-major Y[batch, O] = X[batch, I] . W^T with W row-major [O, I]: the
     // convention of gpu-engine/include/engine/kernels.h:9-20.  ldy (>= O) is the
     // row stride of Y.
+    // The decode step's GEMMs go to b2_linear (tcgen05, split-K over a cluster,
+    // weights streamed before griddepcontrol.wait so they overlap the kernel
+    // before) when switched on, for 16-bit models, batches of at most 256 rows
+    // and layers whose 128-feature tiles fit the GPU in one wave; cuBLAS
+    // otherwise.  With gelu_bias the caller's bias + GELU is fused into the
+    // GEMM's epilogue; the return value says whether that happened.
+    bool linear_ok(int batch, int O) const {
+        return linear_tc && dt != B2_F32 && batch <= 256 && (O + 127) / 128 <= 148;
+    }
+    bool gemm_fused(int batch, int I, int O, const void* X, const void* W, void* Y, const void* gelu_bias) {
+        if (!linear_ok(batch, O)) {
+            gemm(batch, I, O, X, W, Y);
+            return false;
+        }
+        B2LinearArgs la{};
+        la.dtype = dt;
+        la.x = X;
+        la.x_row_stride = I;
+        la.w = W;
+        la.bias = gelu_bias;
+        la.y = Y;
+        la.y_row_stride = O;
+        la.batch = batch;
+        la.in_features = I;
+        la.out_features = O;
+        la.epilogue = gelu_bias ? B2_LINEAR_GELU : B2_LINEAR_STORE;
+        b2_ok(b2_linear(&la, stream), "linear");
+        return gelu_bias != nullptr;
+    }
     void gemm(int batch, int I, int O, const void* X, const void* W, void* Y, int ldy = 0) {
+        if (ldy == 0 && linear_ok(batch, O)) {
+            gemm_fused(batch, I, O, X, W, Y, nullptr);
+            return;
+        }
         const float alpha = 1.0f, beta = 0.0f;
         const cudaDataType_t t = dt == B2_F32 ? CUDA_R_32F : (dt == B2_F16 ? CUDA_R_16F : CUDA_R_16BF);
         cublas_ok(cublasGemmEx(cublas, CUBLAS_OP_T, CUBLAS_OP_N, O, batch, I, &alpha, W, t, I, X, t, I, &beta, Y, t,
@@ -596,8 +630,8 @@ struct Engine {
                 gemm(bucket, D, D, d_attn, w.proj_w, d_attn_out);
             }
             b2_ok(b2_add_layernorm(dt, d_x, d_resid, d_attn_out, w.proj_b, d_resid, w.ln2_g, w.ln2_b, bucket, D, eps, s), "ln2");
-            gemm(bucket, D, 4 * D, d_x, w.fc_w, d_ff);
-            b2_ok(b2_bias_gelu(dt, d_ff, d_ff, w.fc_b, bucket, 4 * D, s), "bias_gelu");
+            if (!gemm_fused(bucket, D, 4 * D, d_x, w.fc_w, d_ff, w.fc_b))
+                b2_ok(b2_bias_gelu(dt, d_ff, d_ff, w.fc_b, bucket, 4 * D, s), "bias_gelu");
             gemm(bucket, 4 * D, D, d_ff, w.fc_proj_w, d_ff_out);
             delta = d_ff_out;
             delta_bias = w.fc_proj_b;
@@ -1246,6 +1280,17 @@ int b2_engine_set_prefill_tensor_cores(b2_engine* eng, int32_t enabled) {
     if (!eng) return B2_ERR_NULL;
     eng->prefill_tc = enabled != 0;
     return B2_OK;
+}
+
+int b2_engine_set_linear_tensor_cores(b2_engine* eng, int32_t enabled) {
+    if (!eng) return B2_ERR_NULL;
+    return guarded([&] {
+        b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
+        b2::eng::cuda_ok(cudaStreamSynchronize(eng->stream), "linear switch");
+        for (auto& g : eng->graphs) cudaGraphExecDestroy(g.second);  // captured with the other GEMMs
+        eng->graphs.clear();
+        eng->linear_tc = enabled != 0;
+    });
 }
 
 int b2_engine_shape(const b2_engine* eng, B2ModelShape* out) {

@@ -27,7 +27,7 @@ ENGINE_SYMBOLS = (
     "b2_engine_shape", "b2_engine_stream",
     "b2_engine_last_error", "b2_block_pool_create", "b2_block_pool_destroy", "b2_block_pool_allocate",
     "b2_block_pool_free", "b2_block_pool_num_free", "b2_engine_tp_handle", "b2_engine_tp_connect",
-    "b2_engine_prefill", "b2_engine_tp_nccl_id", "b2_engine_tp_connect_nccl",
+    "b2_engine_prefill", "b2_engine_tp_nccl_id", "b2_engine_tp_connect_nccl", "b2_engine_set_linear_tensor_cores",
 )
 
 TP_HANDLE_BYTES = 128
@@ -96,6 +96,7 @@ def load() -> ctypes.CDLL:
     lib.b2_engine_tp_connect.argtypes = [_vp, ctypes.c_char_p]
     lib.b2_engine_prefill.argtypes = [_vp, P(_i32), _i32, P(_i32)]
     lib.b2_engine_tp_nccl_id.argtypes = [ctypes.c_char_p]
+    lib.b2_engine_set_linear_tensor_cores.argtypes = [_vp, _i32]
     lib.b2_engine_tp_connect_nccl.argtypes = [_vp, ctypes.c_char_p]
     _lib = lib
     return lib
@@ -197,6 +198,9 @@ class Engine:
 
     def set_use_cuda_graphs(self, enabled: bool) -> None:
         _check(self._lib.b2_engine_set_use_cuda_graphs(self._handle(), 1 if enabled else 0))
+
+    def set_linear_tensor_cores(self, enabled: bool) -> None:
+        _check(self._lib.b2_engine_set_linear_tensor_cores(self._handle(), 1 if enabled else 0))
 
     def set_prefill_tensor_cores(self, enabled: bool) -> None:
         _check(self._lib.b2_engine_set_prefill_tensor_cores(self._handle(), 1 if enabled else 0))

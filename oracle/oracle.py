@@ -21,9 +21,40 @@ _lib = None
 _ref = None
 
 
+def _reference_checkout() -> Path | None:
+    """The reference checkout: $B2_REFERENCE, else /root/reference where it exists
+    (the build container; GPU boxes use the prebuilt _ref files)."""
+    import os
+    for c in (os.environ.get("B2_REFERENCE"), "/root/reference"):
+        if c and (Path(c) / "gpu-engine" / "src" / "reference" / "cpu_model.cpp").exists():
+            return Path(c)
+    return None
+
+
+def _json_include() -> Path | None:
+    """A directory holding nlohmann/json.hpp ($B2_JSON_INCLUDE, system include
+    dirs, then copies vendored by installed Python packages)."""
+    import os
+    import site
+    cands = [Path(os.environ["B2_JSON_INCLUDE"])] if os.environ.get("B2_JSON_INCLUDE") else []
+    cands += [Path("/usr/include"), Path("/usr/local/include")]
+    for sp in site.getsitepackages():
+        cands += sorted(Path(sp).glob("include/*/thirdparty"))
+        cands += sorted(Path(sp).glob("*/include"))
+    for c in cands:
+        if (c / "nlohmann" / "json.hpp").exists():
+            return c
+    return None
+
+
 def build() -> None:
-    """Builds liboracle.so (and _ref/libref_cpu.so when the reference checkout exists)."""
-    subprocess.run(["make", "-s", "-C", str(HERE), "all"], check=True)
+    """Builds liboracle.so, and -- when the reference checkout is present -- the
+    reference's CPU path and scheduler harnesses under _ref/."""
+    cmd = ["make", "-s", "-C", str(HERE), "all"]
+    ref, js = _reference_checkout(), _json_include()
+    if ref is not None and js is not None:
+        cmd += [f"REF={ref}", f"JSON={js}"]
+    subprocess.run(cmd, check=True)
 
 
 def load() -> ctypes.CDLL:
