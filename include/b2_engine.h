@@ -116,6 +116,23 @@ B2_API int b2_engine_set_prefill_tensor_cores(b2_engine* eng, int32_t enabled);
  * for the lm_head).  Default off.  Switching drops the captured graphs. */
 B2_API int b2_engine_set_linear_tensor_cores(b2_engine* eng, int32_t enabled);
 
+/* How the decode step's GEMMs of f16 / bf16 engines run on cuBLAS (no effect
+ * on f32 engines, which keep cublasGemmEx in pedantic fp32).  Bit 1: cuBLASLt
+ * with the algorithm for each (batch bucket, layer shape) chosen by timing the
+ * library's top candidates once, before the bucket's graph is captured
+ * (cublasGemmEx runs the heuristic's first choice).  Bit 2 (with bit 1): the
+ * FC layer's bias + GELU in that GEMM's epilogue (CUBLASLT_EPILOGUE_GELU_BIAS,
+ * fp32 before the one rounding) instead of a separate launch.  Switching drops
+ * the captured graphs. */
+B2_API int b2_engine_set_gemm_mode(b2_engine* eng, int32_t mode);
+
+/* Inspection (no reference counterpart): copies the first `rows` lanes of the
+ * last decode_step's final LayerNorm output ([rows][d_model]) and logits
+ * ([rows][vocab_size]) into host buffers (either may be NULL), in the engine's
+ * dtype.  Synchronises the engine's stream.  For parity tests: a prompt fed
+ * through decode_step is a teacher-forced token stream. */
+B2_API int b2_engine_last_step_outputs(const b2_engine* eng, int32_t rows, void* hidden_out, void* logits_out);
+
 /* Engine::free_sequence: returns the sequence's blocks; unknown ids are ignored. */
 B2_API int b2_engine_free_sequence(b2_engine* eng, int32_t seq_id);
 

@@ -80,7 +80,7 @@ def build_engine(verbose: bool = False) -> Path:
     if _stale(out, deps):
         LIB.mkdir(exist_ok=True)
         cmd = [_nvcc(), *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-I", str(_json_include()),
-               "-shared", "-o", str(out), *map(str, srcs), "-L", str(LIB), "-lb2decode", "-lcublas", "-lnccl",
+               "-shared", "-o", str(out), *map(str, srcs), "-L", str(LIB), "-lb2decode", "-lcublas", "-lcublasLt", "-lnccl",
                "-Xlinker", "-rpath,$ORIGIN"]
         _run(cmd, verbose)
     return out

@@ -92,6 +92,7 @@ struct AttnParams {
     unsigned int* counters;  // [batch] pieces finished per sequence; zero between launches
     OutSpec out;
     int early;  // 0 wait first; 1 inputs complete; 2 only each sequence's newest row pending
+    int local_merge;  // 1: a sequence whose rows all lie in one CTA is merged there, in shared memory
 };
 
 struct CombineParams {
@@ -329,6 +330,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     uint64_t* piece_full = empty + S;  // [R], one arrival per softmax warp
     uint64_t* piece_empty = piece_full + R;  // [R]
     uint64_t* book_done = piece_empty + R;
+    uint64_t* lm_bar = book_done + 1;  // [2] consumer-warp barriers of the in-CTA merge
     int* misc = reinterpret_cast<int*>(smem + p.off_misc);  // [0..1] first sequence and its row prefix, [2..34] scan
     int4* pieces = reinterpret_cast<int4*>(smem + p.off_misc + 160);  // [R] (b, i0, nseg, final)
     int* final_merge = misc + 36;  // [0] merge the final piece's sequence here, [1] b, [2] i0, [3] nseg
@@ -342,6 +344,8 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             mbar_init(&piece_empty[s], 1);
         }
         mbar_init(book_done, 1);
+        mbar_init(&lm_bar[0], static_cast<uint32_t>(ncw));
+        mbar_init(&lm_bar[1], static_cast<uint32_t>(ncw));
         final_merge[0] = 0;
         fence_mbar_init();
     }
@@ -535,8 +539,9 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             if (p.early) pdl_wait();  // counters and outputs are written below
             __syncwarp();  // every lane has read the entry before it is released
             if (lane == 0) mbar_arrive(&piece_empty[rk]);
-            int last = 0;
-            if (lane == 0) last = count_piece(p.counters + pc.x) == static_cast<unsigned>(pc.z - 1) ? 1 : 0;
+            int last = 0;  // pc.z == 0: the piece was merged by the softmax threads (one-piece sequence)
+            if (lane == 0 && pc.z > 0)
+                last = count_piece(p.counters + pc.x) == static_cast<unsigned>(pc.z - 1) ? 1 : 0;
             last = __shfl_sync(0xffffffffu, last, 0);
             if (last) {
                 if (pc.w) {
@@ -596,6 +601,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     const float scale_log2 = p.scale_log2;
 
     int npieces = 0;
+    int npieces_local = 0;  // pieces merged in shared memory (phase of lm_bar)
     for (int n = 0;; ++n) {
         const int st = n % S;
         const uint32_t ph = static_cast<uint32_t>(n / S) & 1u;
@@ -704,15 +710,89 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
+        // A sequence whose rows all lie in this CTA (one piece, nseg == 1) is
+        // merged right here through shared memory -- the stage just consumed
+        // serves as scratch, so it is released only afterwards.
+        const bool local = last && p.local_merge != 0 && meta.w == 1;
+        if (!local) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
 
         if (last) {
-            if (p.early) pdl_wait();  // the workspace is written from here on
+            if (p.early) pdl_wait();  // outputs / the workspace are written from here on
+        }
+        if (local) {
+            // (1) every consumer warp is done with the stage's K/V; (2) every
+            // subgroup's (m, l, acc) is in the scratch; (3) item-parallel merge.
+            // The barriers are mbarriers with bounded waits (no CTA barrier: a
+            // warp that timed out has left).
+            float* acc_s = reinterpret_cast<float*>(stage);
+            float2* ml_s = reinterpret_cast<float2*>(acc_s + static_cast<size_t>(ks) * H * DH);
+            const uint32_t lph = static_cast<uint32_t>(npieces_local) & 1u;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&lm_bar[0]);
+            if (__any_sync(0xffffffffu, !mbar_wait_bounded(&lm_bar[0], lph))) {
+                if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+                return;
+            }
+            if (active) {
+#pragma unroll
+                for (int g = 0; g < QG; ++g) {
+                    const int h = hk * QG + g;
+                    float* dst = acc_s + (static_cast<size_t>(ts) * H + h) * DH + dgt * CPT * E;
+#pragma unroll
+                    for (int e = 0; e < CPT * E; e += 4)
+                        *reinterpret_cast<float4*>(dst + e) =
+                            make_float4(acc[g][e], acc[g][e + 1], acc[g][e + 2], acc[g][e + 3]);
+                    if (dgt == 0) ml_s[ts * H + h] = make_float2(m_run[g], l_run[g]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&lm_bar[1]);
+            if (__any_sync(0xffffffffu, !mbar_wait_bounded(&lm_bar[1], lph))) {
+                if (lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+                return;
+            }
+            constexpr int EO = Elem<OutT>::kPer16B;  // output elements per item (one 16-byte store)
+            constexpr int CH = DH / EO;
+            for (int it = tid; it < H * CH; it += p.ncons) {
+                const int h = it / CH;
+                const int c = it - h * CH;
+                float mrun = -INFINITY, l = 0.0f, a[EO];
+#pragma unroll
+                for (int e = 0; e < EO; ++e) a[e] = 0.0f;
+                for (int j = 0; j < ks; ++j) {
+                    const float2 ml = ml_s[j * H + h];
+                    float a2[EO];
+                    const float* src = acc_s + (static_cast<size_t>(j) * H + h) * DH + c * EO;
+#pragma unroll
+                    for (int e = 0; e < EO; e += 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(src + e);
+                        a2[e] = v.x;
+                        a2[e + 1] = v.y;
+                        a2[e + 2] = v.z;
+                        a2[e + 3] = v.w;
+                    }
+                    fold_state(mrun, l, a, EO, ml.x, ml.y, a2);
+                }
+                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+                for (int e = 0; e < EO; ++e) a[e] *= inv;
+                store_out<OutT, EO>(p.out, b, H, h, DH, c, a);
+            }
+            ++npieces_local;
+            // the scratch was written through the generic proxy; the producer's
+            // next bulk copy into this stage writes through the async proxy
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);  // the scratch reads are done
+        }
+        if (last) {
             // ---- piece end: this subgroup's partial goes to the workspace.
             // Slot (cta + b) is unique per (CTA, sequence) pair: along the CTA
             // order both indices only grow, so cta + b never repeats.
-            if (active) {
+            if (active && !local) {
                 const size_t slot = (static_cast<size_t>(cta) + b) * ks + ts;
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
@@ -735,7 +815,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             if (tid == 0) {
                 if (!mbar_wait_bounded(&piece_empty[rk], (static_cast<uint32_t>(npieces / R) & 1u) ^ 1u))
                     flag_error(B2_DEVERR_TIMEOUT);
-                pieces[rk] = make_int4(b, meta.z, meta.w, final_stage ? 1 : 0);
+                pieces[rk] = make_int4(b, meta.z, local ? 0 : meta.w, final_stage ? 1 : 0);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&piece_full[rk]);

@@ -263,11 +263,14 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     p.slab_bytes = slab;
     p.q_bytes = qbytes;
     p.off_meta = off_meta;
+    // One-piece sequences are merged in shared memory, over the stage just
+    // consumed: [ks][H][head_dim] fp32 states and [ks][H] (m, l) must fit it.
+    p.local_merge = static_cast<long long>(best_k) * H * (a->head_dim * 4 + 8) <= stage ? 1 : 0;
     int off = best_s * stage;
     p.off_misc = off;
     off += kMiscBytes;
     p.off_bars = off;
-    off += (2 * best_s + 2 * kPieceRing + 1) * 8;
+    off += (2 * best_s + 2 * kPieceRing + 1 + 2) * 8;  // stages full/empty, piece ring, book_done, merge barriers
     pl->smem = off;
     pl->threads = p.ncons + 64;
     pl->grid = a->max_ctas > 0 ? std::min(di.sms * best_cps, a->max_ctas) : di.sms * best_cps;

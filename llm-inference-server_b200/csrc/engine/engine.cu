@@ -41,6 +41,7 @@
 #include "b2_decode.h"
 #include "b2_engine.h"
 #include "block_pool.h"
+#include "lt_gemm.h"
 
 namespace b2 {
 namespace eng {
@@ -264,6 +265,12 @@ struct Engine {
     int prefill_cap = 0;
     bool prefill_tc = true;  // b2_engine_set_prefill_tensor_cores
     bool linear_tc = false;  // b2_engine_set_linear_tensor_cores
+    // b2_engine_set_gemm_mode: 16-bit decode-step GEMMs on cuBLASLt with the
+    // algorithm per shape chosen by timing (bit 1), the FC layer's bias + GELU
+    // in that GEMM's epilogue (bit 2).
+    int gemm_mode = 0;
+    std::unique_ptr<LtGemm> lt;
+    bool in_decode = false;  // run_step_kernels is issuing the decode step
     int32_t *d_pin = nullptr, *h_pin = nullptr, *d_pseq_post = nullptr, *d_pnext = nullptr, *h_pnext = nullptr;
     void *p_resid = nullptr, *p_x = nullptr, *p_qkv = nullptr, *p_attn = nullptr, *p_attn_out = nullptr,
          *p_ff = nullptr, *p_ff_out = nullptr, *p_last = nullptr, *p_logits = nullptr, *p_attn_ws = nullptr;
@@ -434,6 +441,10 @@ struct Engine {
         cublas_ok(cublasSetWorkspace(cublas, cublas_ws, ws), "cublasSetWorkspace");
         cublas_ok(cublasSetMathMode(cublas, dt == B2_F32 ? CUBLAS_PEDANTIC_MATH : CUBLAS_DEFAULT_MATH),
                   "cublasSetMathMode");
+        if (dt != B2_F32) {
+            lt = std::make_unique<LtGemm>();
+            lt->init(dt == B2_F16 ? CUDA_R_16F : CUDA_R_16BF, cublas_ws, ws);
+        }
     }
 
     void setup_buffers() {
@@ -523,8 +534,18 @@ struct Engine {
     bool linear_ok(int batch, int O) const {
         return linear_tc && dt != B2_F32 && batch <= 256 && (O + 127) / 128 <= 148;
     }
+    bool lt_on() const { return lt && (gemm_mode & 1) && in_decode; }
+    bool capturing() const {
+        cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(stream, &st);
+        return st != cudaStreamCaptureStatusNone;
+    }
     bool gemm_fused(int batch, int I, int O, const void* X, const void* W, void* Y, const void* gelu_bias) {
         if (!linear_ok(batch, O)) {
+            if (gelu_bias && lt_on() && (gemm_mode & 2)) {
+                lt->run(batch, I, O, X, W, Y, O, LtGemm::kGeluBias, gelu_bias, stream, !capturing());
+                return true;
+            }
             gemm(batch, I, O, X, W, Y);
             return false;
         }
@@ -548,6 +569,10 @@ struct Engine {
             gemm_fused(batch, I, O, X, W, Y, nullptr);
             return;
         }
+        if (lt_on()) {
+            lt->run(batch, I, O, X, W, Y, ldy > 0 ? ldy : O, LtGemm::kNone, nullptr, stream, !capturing());
+            return;
+        }
         const float alpha = 1.0f, beta = 0.0f;
         const cudaDataType_t t = dt == B2_F32 ? CUDA_R_32F : (dt == B2_F16 ? CUDA_R_16F : CUDA_R_16BF);
         cublas_ok(cublasGemmEx(cublas, CUBLAS_OP_T, CUBLAS_OP_N, O, batch, I, &alpha, W, t, I, X, t, I, &beta, Y, t,
@@ -556,6 +581,11 @@ struct Engine {
     }
 
     void run_step_kernels(int bucket) {
+        in_decode = true;
+        struct Leave {
+            bool& f;
+            ~Leave() { f = false; }
+        } leave{in_decode};
         const int D = shape.d_model, V = shape.vocab_size, L = shape.n_layer;
         const float eps = shape.layer_norm_epsilon;
         b2_stream_t s = stream;
@@ -598,8 +628,12 @@ struct Engine {
             B2PagedAttnArgs aa = attn_args(bucket, l);
             aa.q_bias = qkv_b;
             // Past layer 0, seq_lens_post, the block tables, q and every key row
-            // but the newest were complete before kv_append started.
-            if (l > 0) aa.flags = B2_ATTN_NEWEST_ROW_PENDING;
+            // but the newest were complete before kv_append started -- when the
+            // QKV GEMM was cuBLAS, which lets kv_append start only once it has
+            // finished.  b2_linear lets its dependents start early (kv_append
+            // may begin while q is still being written), so then attention
+            // waits for kv_append before reading anything.
+            if (l > 0 && !linear_ok(bucket, 3 * QD)) aa.flags = B2_ATTN_NEWEST_ROW_PENDING;
             if (tp_nccl) {
                 // this rank's heads, then ncclAllGather of every rank's slice and
                 // the interleave into [row][rank slices] for the projection
@@ -667,6 +701,9 @@ struct Engine {
     cudaGraphExec_t graph_for(int bucket) {
         auto it = graphs.find(bucket);
         if (it != graphs.end()) return it->second;
+        // cuBLASLt shapes are timed outside any capture: one eager pass of the
+        // step first (the step is idempotent: same inputs, same writes).
+        if (lt && (gemm_mode & 1)) run_step_kernels(bucket);
         cudaGraph_t g = nullptr;
         cuda_ok(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
         try {
@@ -1280,6 +1317,36 @@ int b2_engine_set_prefill_tensor_cores(b2_engine* eng, int32_t enabled) {
     if (!eng) return B2_ERR_NULL;
     eng->prefill_tc = enabled != 0;
     return B2_OK;
+}
+
+int b2_engine_last_step_outputs(const b2_engine* eng, int32_t rows, void* hidden_out, void* logits_out) {
+    if (!eng) return B2_ERR_NULL;
+    return guarded([&] {
+        if (rows < 0 || rows > eng->cfg.max_batch) throw Error(B2_ERR_SHAPE, "rows must be in [0, max_batch]");
+        b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
+        b2::eng::cuda_ok(cudaStreamSynchronize(eng->stream), "last step outputs");
+        const size_t es = static_cast<size_t>(eng->es);
+        const size_t D = static_cast<size_t>(eng->shape.d_model), V = static_cast<size_t>(eng->shape.vocab_size);
+        if (hidden_out && rows > 0)
+            b2::eng::cuda_ok(cudaMemcpy(hidden_out, eng->d_x, static_cast<size_t>(rows) * D * es, cudaMemcpyDeviceToHost),
+                             "copy final LayerNorm rows");
+        if (logits_out && rows > 0)
+            b2::eng::cuda_ok(cudaMemcpy2D(logits_out, V * es, eng->d_logits, static_cast<size_t>(eng->vocab_padded()) * es,
+                                          V * es, static_cast<size_t>(rows), cudaMemcpyDeviceToHost),
+                             "copy logits");
+    });
+}
+
+int b2_engine_set_gemm_mode(b2_engine* eng, int32_t mode) {
+    if (!eng) return B2_ERR_NULL;
+    return guarded([&] {
+        if (mode < 0 || mode > 3) throw Error(B2_ERR_SHAPE, "gemm mode must be 0..3");
+        b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
+        b2::eng::cuda_ok(cudaStreamSynchronize(eng->stream), "gemm mode switch");
+        for (auto& g : eng->graphs) cudaGraphExecDestroy(g.second);
+        eng->graphs.clear();
+        eng->gemm_mode = eng->dt == B2_F32 ? 0 : mode;
+    });
 }
 
 int b2_engine_set_linear_tensor_cores(b2_engine* eng, int32_t enabled) {

@@ -28,6 +28,7 @@ ENGINE_SYMBOLS = (
     "b2_engine_last_error", "b2_block_pool_create", "b2_block_pool_destroy", "b2_block_pool_allocate",
     "b2_block_pool_free", "b2_block_pool_num_free", "b2_engine_tp_handle", "b2_engine_tp_connect",
     "b2_engine_prefill", "b2_engine_tp_nccl_id", "b2_engine_tp_connect_nccl", "b2_engine_set_linear_tensor_cores",
+    "b2_engine_last_step_outputs", "b2_engine_set_gemm_mode",
 )
 
 TP_HANDLE_BYTES = 128
@@ -97,6 +98,8 @@ def load() -> ctypes.CDLL:
     lib.b2_engine_prefill.argtypes = [_vp, P(_i32), _i32, P(_i32)]
     lib.b2_engine_tp_nccl_id.argtypes = [ctypes.c_char_p]
     lib.b2_engine_set_linear_tensor_cores.argtypes = [_vp, _i32]
+    lib.b2_engine_last_step_outputs.argtypes = [_vp, _i32, _vp, _vp]
+    lib.b2_engine_set_gemm_mode.argtypes = [_vp, _i32]
     lib.b2_engine_tp_connect_nccl.argtypes = [_vp, ctypes.c_char_p]
     _lib = lib
     return lib
@@ -139,6 +142,7 @@ class Engine:
 
     def __init__(self) -> None:
         self._h = None
+        self.cfg = None
         self._lib = load()
 
     def init(self, weights_dir: str | Path, cfg: Config) -> bool:
@@ -149,6 +153,7 @@ class Engine:
         if rc != 0:
             return False
         self._h = h
+        self.cfg = cfg
         return True
 
     def init_synthetic(self, shape: ModelShape, cfg: Config, seed: int = 0, std: float = 0.02) -> None:
@@ -157,6 +162,7 @@ class Engine:
         _check(self._lib.b2_engine_create_synthetic(ctypes.byref(shape), seed, std, ctypes.byref(cfg.to_c()),
                                                     ctypes.byref(h)))
         self._h = h
+        self.cfg = cfg
 
     def last_error(self) -> str:
         return self._lib.b2_engine_last_error().decode()
@@ -198,6 +204,22 @@ class Engine:
 
     def set_use_cuda_graphs(self, enabled: bool) -> None:
         _check(self._lib.b2_engine_set_use_cuda_graphs(self._handle(), 1 if enabled else 0))
+
+    def last_step_outputs(self, rows: int):
+        """(final LayerNorm rows [rows, d_model], logits [rows, vocab]) of the last
+        decode_step as numpy arrays in the engine dtype (uint16 bit patterns for
+        f16 / bf16)."""
+        import numpy as np
+        s = self.shape()
+        dt = np.float32 if self.cfg.dtype == 0 else np.uint16
+        h = np.empty((rows, s.d_model), dtype=dt)
+        lg = np.empty((rows, s.vocab_size), dtype=dt)
+        _check(self._lib.b2_engine_last_step_outputs(self._handle(), rows, h.ctypes.data, lg.ctypes.data))
+        return h, lg
+
+    def set_gemm_mode(self, mode: int) -> None:
+        """Bit 1: cuBLASLt with timed algorithm choice; bit 2: FC bias + GELU in its epilogue."""
+        _check(self._lib.b2_engine_set_gemm_mode(self._handle(), mode))
 
     def set_linear_tensor_cores(self, enabled: bool) -> None:
         _check(self._lib.b2_engine_set_linear_tensor_cores(self._handle(), 1 if enabled else 0))

@@ -92,7 +92,7 @@ def step_bytes(w: EngineWorkload, ctx: np.ndarray, world: int = 1) -> float:
 
 
 def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist, device, timed_region=None,
-        per_rank_batch: int | None = None, allgather: int = 0, linear: bool = False) -> dict:
+        per_rank_batch: int | None = None, allgather: int = 0, linear: bool = False, gemm_mode: int = 0) -> dict:
     """Runs the workload's waves on this rank; timed_region() (optional) gives a
     context manager entered around each wave's timed steps.  per_rank_batch
     overrides the sequences per rank (profiling one GPU's share of a larger
@@ -130,6 +130,8 @@ def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist,
                        seed=1, std=0.02)
     if linear:
         eng.set_linear_tensor_cores(True)
+    if gemm_mode:
+        eng.set_gemm_mode(gemm_mode)
     if sharded and allgather:
         ids_box = [E.Engine.tp_nccl_id() if rank == 0 else None]
         dist.broadcast_object_list(ids_box, src=0)
