@@ -71,6 +71,7 @@ class Workload:
     pool_blocks: int
     profile: str        # committed ncu summary holding traffic_bytes_per_launch
     description: str
+    layout: str = ""    # "blocks" / "layer-major": 48-layer KV cache, one launch per layer
 
 
 WORKLOADS = {
@@ -86,6 +87,14 @@ WORKLOADS = {
                     "grouped-query paged-attention decode: batch 256 per GPU, 32 query / 8 kv heads, head_dim 128, "
                     "bf16 K/V and q N(0,1), context log-uniform [512,32768], block 16, random permutation of a "
                     "140000-block pool, scale 1/sqrt(128)"),
+    "xl-blocks": Workload("xl-blocks", 128, 25, 25, 64, "bf16", 256, 1011, False, 48, 0, "",
+                          "paged-attention decode over the reference's all-layers-per-block pool (kv_cache.h:6-8): "
+                          "GPT-2 XL shape, batch 128, 25 heads x 64, bf16, 48 layers per 4.9 MB block, launch l reads "
+                          "layer l, context U[256,1011], random block permutation", "blocks"),
+    "xl-layers": Workload("xl-layers", 128, 25, 25, 64, "bf16", 256, 1011, False, 48, 0, "",
+                          "paged-attention decode over the engine's layer-major KV cache: GPT-2 XL shape, batch 128, "
+                          "25 heads x 64, bf16, one arena per layer (48), launch l reads layer l, context "
+                          "U[256,1011], the same random block permutation", "layer-major"),
 }
 WL = WORKLOADS["mha"]  # set by main()
 
@@ -131,7 +140,7 @@ def measured_peak():
 def profiled_traffic():
     """dram bytes per launch of the attention kernel from the committed ncu summary, if any."""
     p = ROOT / "profiles" / WL.profile
-    if not p.exists():
+    if not WL.profile or not p.is_file():
         return None, None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
     n = re.search(r"algorithmic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
@@ -315,7 +324,11 @@ def host_workload(seed: int, n_seq=None):
 
 
 def b2_workload(b2, device, seed: int, n_sets: int, pool_blocks: int, batch: int | None = None):
-    from lis_b200.workloads import make_attention_workload
+    from lis_b200.workloads import make_attention_workload, make_layered_workload
+    if WL.layout:
+        return make_layered_workload(device, WL.layout, seed=seed, batch=batch or WL.batch, n_head=WL.n_head,
+                                     head_dim=WL.head_dim, ctx_lo=WL.ctx_lo, ctx_hi=WL.ctx_hi, n_layer=WL.n_sets,
+                                     dtype=torch_dtype())
     return make_attention_workload(device, seed=seed, n_sets=n_sets, batch=batch or WL.batch, n_head=WL.n_head,
                                    n_kv_head=WL.n_kv_head, head_dim=WL.head_dim, ctx_lo=WL.ctx_lo, ctx_hi=WL.ctx_hi,
                                    pool_blocks=pool_blocks, dtype=torch_dtype(), log_uniform=WL.log_uniform)

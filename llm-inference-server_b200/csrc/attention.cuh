@@ -81,7 +81,7 @@ struct AttnParams {
     int ncons;         // consumer threads, multiple of 32
     int stages;
     int stage_bytes;
-    int stage_rows;  // key rows a stage holds at most: 16 (a block) or 8
+    int stage_rows;  // key rows a stage holds at most: 16 (a block), 8 or 4
     int slab_bytes;  // stage_rows * n_kv_head * head_dim * sizeof(T): K (then V) capacity of a stage
     int q_bytes;     // n_head * head_dim * sizeof(T)
     int off_meta;    // within a stage

@@ -220,7 +220,13 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
         int cps, rows, cpt, min_k;
     };
     const bool cpt2_ok = es == 2 && H / a->n_kv_head <= 2;
-    const Cand cands[3] = {{2, B2_BLOCK_TOKENS, 1, 1}, {2, B2_BLOCK_TOKENS / 2, 2, 2}, {1, B2_BLOCK_TOKENS, cpt2_ok ? 2 : 1, 1}};
+    // 4./5. last resorts for rows too wide for a ring of whole blocks (f32 with many heads, e.g. 25 x 64 fp32 =
+    //    6.4 KB a row): one CTA per SM, stages of 8 or 4 rows.
+    const Cand cands[5] = {{2, B2_BLOCK_TOKENS, 1, 1},
+                           {2, B2_BLOCK_TOKENS / 2, 2, 2},
+                           {1, B2_BLOCK_TOKENS, cpt2_ok ? 2 : 1, 1},
+                           {1, B2_BLOCK_TOKENS / 2, cpt2_ok ? 2 : 1, 1},
+                           {1, B2_BLOCK_TOKENS / 4, cpt2_ok ? 2 : 1, 1}};
     int best_k = 0, best_s = 0, best_cps = 0, best_cpt = 1, best_rows = 0;
     int slab = 0, off_meta = 0, stage = 0;
     for (const Cand& cd : cands) {

@@ -103,6 +103,61 @@ def make_attention_workload(device, seed: int = 0, n_sets: int = 16, batch: int 
     return wl
 
 
+def make_layered_workload(device, layout: str, seed: int = 0, batch: int = 128, n_head: int = 25, head_dim: int = 64,
+                          ctx_lo: int = 256, ctx_hi: int = 1011, n_layer: int = 48, dtype=None) -> AttnWorkload:
+    """One batch of sequences whose KV cache holds n_layer layers, one set per
+    layer (launch l reads layer l), in one of two layouts:
+      "blocks"      -- the reference's pool (kv_cache.h:6-8): one block holds
+                       all layers, [block][layer][K|V][16][H][Dh]; launch l
+                       passes layer_idx = l, n_layer = n_layer;
+      "layer-major" -- the engine's: one [blocks][K|V][16][H][Dh] arena per
+                       layer; launch l addresses layer l's arena (its block ids
+                       offset by l * blocks), n_layer = 1.
+    Same block permutation, same bytes per launch: the two differ only in where
+    one layer's slabs sit (a block apart, or packed)."""
+    import torch
+
+    dtype = dtype or torch.bfloat16
+    rng = np.random.Generator(np.random.PCG64(seed))
+    ctx = rng.integers(ctx_lo, ctx_hi + 1, size=batch)
+    nb = (ctx + BLOCK_TOKENS - 1) // BLOCK_TOKENS
+    nblk = int(nb.sum())
+    mbps = (ctx_hi + BLOCK_TOKENS - 1) // BLOCK_TOKENS
+    perm = rng.permutation(nblk).astype(np.int32)
+    bt = np.zeros((batch, mbps), np.int32)
+    o = 0
+    for b in range(batch):
+        bt[b, : nb[b]] = perm[o:o + nb[b]]
+        o += int(nb[b])
+    row = n_head * head_dim
+    pool_blocks = nblk if layout == "blocks" else nblk * n_layer
+    n_el = pool_blocks * (n_layer if layout == "blocks" else 1) * 2 * BLOCK_TOKENS * row
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    pool = torch.empty(n_el, dtype=dtype, device=device)
+    chunk = 1 << 28
+    for i in range(0, n_el, chunk):
+        n = min(chunk, n_el - i)
+        pool[i:i + n] = torch.randn(n, generator=gen, device=device, dtype=torch.float32).to(dtype)
+    wl = AttnWorkload(batch, n_head, n_head, head_dim, dtype, pool_blocks, mbps, pool)
+    es = wl.elem
+    d_sl = torch.from_numpy(ctx.astype(np.int32)).to(device)
+    q = torch.randn(batch, row, generator=gen, device=device, dtype=torch.float32).to(dtype)
+    out = torch.empty(batch, n_head, head_dim, dtype=dtype, device=device)
+    for l in range(n_layer):
+        tab = bt if layout == "blocks" else bt + l * nblk
+        s = AttnSet(ctx.astype(np.int32), tab)
+        s.d_seq_lens = d_sl
+        s.d_block_tables = torch.from_numpy(np.ascontiguousarray(tab)).to(device)
+        s.d_q, s.d_out = q, out
+        s.args = attn_args(q, row, pool, s.d_block_tables, d_sl, out, n_head=n_head, n_kv_head=n_head,
+                           head_dim=head_dim, max_blocks_per_seq=mbps, layer_idx=l if layout == "blocks" else 0,
+                           n_layer=n_layer if layout == "blocks" else 1, num_blocks=pool_blocks)
+        s.bytes = attention_bytes(ctx, n_head, n_head, head_dim, es, es, es)
+        wl.sets.append(s)
+    return wl
+
+
 def host_subset(wl: AttnWorkload, set_index: int, n_seq: int | None = None):
     """Copies one set's blocks to host as a compact pool (for the CPU leg).
     Returns (pool uint16/float32 array, block tables remapped, seq_lens, q)."""

@@ -18,7 +18,9 @@ activation rounding, so the bar is a stated tolerance, not bit equality:
 
 Models: small synthetic GPT-2s with the medium head shape (16 x 64) and the
 XL head shape (25 x 64), two layers, weights N(0, 0.02); four streams of 40
-tokens decoded together (batch 4); the decode GEMMs on cuBLAS and on b2_linear.
+tokens decoded together (batch 4); the decode GEMMs on cublasGemmEx, on
+cuBLASLt with timed algorithm choice and the FC bias + GELU in its epilogue
+(b2_engine_set_gemm_mode 3), and on b2_linear.
 """
 from __future__ import annotations
 
@@ -50,18 +52,20 @@ def models(b2, tmp_path_factory):
     return out
 
 
-@pytest.mark.parametrize("linear", [False, True], ids=["cublas", "b2_linear"])
+@pytest.mark.parametrize("gemm", ["cublas", "cublaslt", "b2_linear"])
 @pytest.mark.parametrize("dt", [O.F16, O.BF16], ids=["f16", "bf16"])
 @pytest.mark.parametrize("shape", list(SHAPES))
-def test_16bit_engine_matches_oracle_teacher_forced(b2, cuda, models, shape, dt, linear):
+def test_16bit_engine_matches_oracle_teacher_forced(b2, cuda, models, shape, dt, gemm):
     from lis_b200 import engine as E
     d, cfg, tensors = models[shape]
     rng = np.random.Generator(np.random.PCG64(7 + len(shape)))
     streams = [rng.integers(0, cfg["vocab_size"], size=T).tolist() for _ in range(STREAMS)]
     eng = E.Engine()
     assert eng.init(str(d), E.Config(max_batch=STREAMS, max_seq_len=256, kv_block_budget=64, dtype=dt, device=0))
-    if linear:
+    if gemm == "b2_linear":
         eng.set_linear_tensor_cores(True)
+    elif gemm == "cublaslt":
+        eng.set_gemm_mode(3)
     ids = [eng.add_sequence(s) for s in streams]
     hid = np.empty((T, STREAMS, cfg["d_model"]), np.float32)
     lg = np.empty((T, STREAMS, cfg["vocab_size"]), np.float32)
@@ -81,7 +85,7 @@ def test_16bit_engine_matches_oracle_teacher_forced(b2, cuda, models, shape, dt,
         clear = (top2[:, 1] - top2[:, 0]) > 2 * LOGIT_TOL[dt]
         checked += int(clear.sum())
         agree += int((np.argmax(lg[:, i], axis=1) == np.argmax(rl, axis=1))[clear].sum())
-    print(f"{shape} dt={dt} linear={linear}: hidden max-abs {worst_h:.4g}, logits max-abs {worst_l:.4g}, "
+    print(f"{shape} dt={dt} gemm={gemm}: hidden max-abs {worst_h:.4g}, logits max-abs {worst_l:.4g}, "
           f"argmax agrees at {agree}/{checked} clear positions")
     assert worst_h <= HIDDEN_TOL[dt], f"final LayerNorm max-abs {worst_h:.4g} > {HIDDEN_TOL[dt]}"
     assert worst_l <= LOGIT_TOL[dt], f"logits max-abs {worst_l:.4g} > {LOGIT_TOL[dt]}"

@@ -94,7 +94,7 @@ def _two_gpus() -> bool:
 def test_head_sharded_step_fails_when_a_rank_stops(b2, tmp_path_factory):
     import tp_worker
     from lis_b200 import model_files as MF
-    shape = MF.GPT2Shape(n_layer=4, n_head=4, d_model=256, vocab_size=1024, n_ctx=128)
+    shape = MF.GPT2Shape(n_layer=4, n_head=4, d_model=256, vocab_size=1024, n_ctx=256)
     d = MF.write_model_dir(tmp_path_factory.mktemp("tp_absent"), shape, seed=3, std=0.02)
     prompts = [[5, 6, 7], [8, 9]]
     ctx = mp.get_context("spawn")

@@ -103,6 +103,7 @@ ATTN_CASES = [
     ("bf16-skew", O.BF16, 64, 12, 12, [6000] + list(range(1, 41)), 1, 0),
     ("f16-empty-sequences", O.F16, 64, 4, 4, [0, 7, 0, 100, 0], 1, 0),
     ("f16-gpt2-medium-heads", O.F16, 64, 16, 16, (40, 1, 1000), 1, 0),  # 3 token subgroups
+    ("f32-xl-heads", O.F32, 64, 25, 25, (6, 1, 300), 2, 1),  # 6.4 KB rows: the 8-row-stage fallback plan
 ]
 
 
