@@ -86,6 +86,7 @@ struct AttnParams {
     int q_bytes;     // n_head * head_dim * sizeof(T)
     int off_meta;    // within a stage
     int off_misc, off_bars;
+    int off_seqlens;  // >= 0: shared int[batch] holding the clamped seq_lens (the producer's copy); -1: none
     int2* seq_info;   // [batch] (first CTA, number of segments) for the combine kernel
     float2* part_ml;  // [(grid + batch) * ksplit][n_head] (m, l)
     float* part_acc;  // [(grid + batch) * ksplit][n_head][head_dim]
@@ -381,6 +382,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         for (int b = b_lo; b < b_hi; ++b) {
             const int raw = __ldcg(p.seq_lens + b);
             const int cl = clamp_seq_len(raw, p.mbps);
+            if (p.off_seqlens >= 0) reinterpret_cast<int*>(smem + p.off_seqlens)[b] = cl;
             if (cl > 0 && run <= s_unit && s_unit < run + cl) {
                 misc[0] = b;
                 misc[1] = run;
@@ -426,7 +428,9 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         while (u < e_unit && !failed && bb < B) {
             const int b = bb + lane;
             int cl = 0;
-            if (b < B) cl = clamp_seq_len(__ldcg(p.seq_lens + b), p.mbps);
+            if (b < B)  // the prologue's copy in shared memory when there is one (no second trip to L2)
+                cl = p.off_seqlens >= 0 ? reinterpret_cast<const int*>(smem + p.off_seqlens)[b]
+                                        : clamp_seq_len(__ldcg(p.seq_lens + b), p.mbps);
             int incl = cl;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {

@@ -99,6 +99,8 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 constexpr int kAttnMaxThreads = 512;
 // Shared bytes of the attention kernel's misc area (first sequence, scan).
 constexpr int kMiscBytes = 320;
+// Batches up to this size keep their seq_lens in the attention kernel's shared memory.
+constexpr int kSeqLenCache = 2048;
 
 // ---------------------------------------------------------- attention plan
 
@@ -219,6 +221,10 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     struct Cand {
         int cps, rows, cpt, min_k;
     };
+    // The prologue leaves the clamped seq_lens in shared memory for the producer
+    // warp (its first block-table read then needs no second trip to L2), for
+    // batches up to kSeqLenCache.
+    const int seq_cache = a->batch <= kSeqLenCache ? static_cast<int>(align_up(static_cast<size_t>(a->batch) * 4, 16)) : 0;
     const bool cpt2_ok = es == 2 && H / a->n_kv_head <= 2;
     // 4./5. last resorts for rows too wide for a ring of whole blocks (f32 with many heads, e.g. 25 x 64 fp32 =
     //    6.4 KB a row): one CTA per SM, stages of 8 or 4 rows.
@@ -242,7 +248,7 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
             const int ncons = static_cast<int>(align_up(static_cast<size_t>(k) * CT, 32));
             if (ncons + 64 > thread_cap) continue;  // + producer warp + bookkeeping warp
             if (k > 1 && k * CT > 512) continue;  // enough warps
-            int s = (smem_cap - kMiscBytes - 512) / stage;  // 512: barriers + alignment padding
+            int s = (smem_cap - kMiscBytes - seq_cache - 512) / stage;  // 512: barriers + alignment padding
             if (s > 8) s = 8;
             if (s < 2) continue;
             best_k = k;
@@ -275,6 +281,8 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     int off = best_s * stage;
     p.off_misc = off;
     off += kMiscBytes;
+    p.off_seqlens = seq_cache > 0 ? off : -1;
+    off += seq_cache;
     p.off_bars = off;
     off += (2 * best_s + 2 * kPieceRing + 1 + 2) * 8;  // stages full/empty, piece ring, book_done, merge barriers
     pl->smem = off;
