@@ -761,12 +761,22 @@ struct Engine {
         act(&p_ff_out, cap, D, "malloc prefill ff out");
         act(&p_last, B, D, "malloc prefill last rows");
         act(&p_logits, B, static_cast<size_t>(vocab_padded()), "malloc prefill logits");
-        B2PagedAttnArgs a = attn_args(cap, 0);
+        prefill_cap = cap;
+    }
+
+    // The decode-attention workspace of the row-per-token prefill path (f32
+    // models, or tensor-core prefill switched off), made on first use: the
+    // tcgen05 prefill attention needs none, so an engine that only uses it can
+    // take prompt-token budgets larger than one decode-attention launch allows.
+    void prefill_rows_workspace() {
+        if (p_attn_ws) return;
+        B2PagedAttnArgs a = attn_args(prefill_cap, 0);
         p_attn_ws_bytes = b2_paged_attention_workspace_bytes(&a);
-        if (p_attn_ws_bytes == 0) throw Error(B2_ERR_UNSUPPORTED, std::string("prefill attention: ") + b2_last_error_string());
+        if (p_attn_ws_bytes == 0)
+            throw Error(B2_ERR_UNSUPPORTED, std::string("prefill through decode-attention rows (max_prefill_tokens too "
+                                                        "large for one launch?): ") + b2_last_error_string());
         cuda_ok(cudaMalloc(&p_attn_ws, p_attn_ws_bytes), "malloc prefill attention workspace");
         cuda_ok(cudaMemsetAsync(p_attn_ws, 0, p_attn_ws_bytes, stream), "zero prefill attention workspace");
-        prefill_cap = cap;
     }
 
     // One pass over every remaining prompt token of the listed sequences: the
@@ -796,6 +806,7 @@ struct Engine {
             need += std::max(0, want - have);
         }
         if (rows > prefill_cap) throw Error(B2_ERR_SHAPE, "more prompt tokens than max_prefill_tokens in one call");
+        if (!tc_prefill()) prefill_rows_workspace();
         if (need > blocks->num_free()) throw Error(B2_ERR_POOL, "KV cache block pool exhausted");
         const int cap = prefill_cap, B = cfg.max_batch, D = shape.d_model, V = shape.vocab_size, L = shape.n_layer;
         const size_t seq_off = 3 * static_cast<size_t>(cap);          // last, pre, start, rows: B each
