@@ -681,6 +681,23 @@ def tp_token_check(rank: int, world: int, dist, modes=(0, 1)) -> dict | None:
     return res
 
 
+def gqa_record(args, rank: int, world: int, dist) -> dict | None:
+    """configs[2] (grouped-query long-context decode on the tensor-core kernel)
+    as a record of the default line: the gqa workload's own measurement, at
+    most 40 timed launches (each ~1.2 ms over ~7 GB), no CPU leg."""
+    import argparse as _ap
+    global WL
+    saved = WL
+    WL = WORKLOADS["gqa"]
+    sub = _ap.Namespace(**vars(args))
+    sub.steps, sub.warmup, sub.no_cpu = min(args.steps, 40), 3, True
+    sub.sets = sub.pool_blocks = sub.batch = None
+    try:
+        return run_ours(sub, rank, world, dist)
+    finally:
+        WL = saved
+
+
 def engine_records(args, rank: int, world: int, dist) -> dict:
     """The GPT-2 XL decode records attached to the default bench line: the
     sequence-sharded step at N GPUs, and at N >= 2 the head-sharded step with
@@ -1095,7 +1112,12 @@ def main() -> None:
             gc.collect()
             torch.cuda.empty_cache()
             if WL.name == "mha" and not args.no_engine:
-                extra = engine_records(args, rank, world, dist)
+                extra = {}
+                if world == 1:
+                    extra["gqa"] = gqa_record(args, rank, world, dist)
+                    gc.collect()
+                    torch.cuda.empty_cache()
+                extra.update(engine_records(args, rank, world, dist))
                 if world == 1:
                     extra["gpt2_small"] = run_gpt2_small(args, rank, world, cpu=not args.no_cpu)
                 if rank == 0:

@@ -26,8 +26,10 @@
  *     any launch, > 0 = the cudaError_t seen right after the launch.
  *     The reference launchers return void and never check.
  *
- * All buffers are caller-owned device memory.  No entry point allocates,
- * frees or synchronises, so every launch can be captured in a CUDA graph.
+ * All buffers are caller-owned device memory.  No entry point allocates or
+ * frees, and none synchronises except b2_device_errors and
+ * b2_paged_attention_host (a synchronous call by design), so every other
+ * launch can be captured in a CUDA graph.
  * All pointers handed to the attention and append kernels must be 16-byte
  * aligned, and every row stride times the element size a multiple of 16 bytes.
  */
@@ -180,7 +182,9 @@ typedef struct B2PagedAttnArgs {
  * current device (depends on the SM count). */
 B2_API size_t b2_paged_attention_workspace_bytes(const B2PagedAttnArgs* args);
 
-/* Two launches on `stream`: the split attention kernel, then the merge. */
+/* One launch on `stream` (the CUDA-core kernel merges each sequence's pieces
+ * itself); the tensor-core kernel for 8 kv heads of head_dim 128 adds a small
+ * merge kernel. */
 B2_API int b2_paged_attention(const B2PagedAttnArgs* args, void* workspace, size_t workspace_bytes,
                               b2_stream_t stream);
 
@@ -200,7 +204,10 @@ B2_API int b2_paged_attention(const B2PagedAttnArgs* args, void* workspace, size
  * When io->out is page-locked memory mapped into the device's address space
  * (cudaHostAlloc / cudaHostRegister memory on a unified-addressing system)
  * and 16-byte aligned, the kernel stores the output into it directly (the
- * PCIe writes overlap the kernel) and args->out is not written.
+ * PCIe writes overlap the kernel) and args->out is not written.  The call
+ * waits for the stream by polling it (cudaStreamQuery), spending the calling
+ * thread's core until the GPU is done -- it returns within about a microsecond
+ * instead of after a blocking-sync wake-up.
  * Byte counts: q ((batch-1)*q_row_stride + n_head*head_dim) elements of
  * dtype; block tables batch*max_blocks_per_seq int32; seq_lens batch int32;
  * out batch*n_head*head_dim elements of out_dtype.

@@ -25,15 +25,18 @@
 //    FMAs, see dot16) and keeps that head's online-softmax state (m, l) and
 //    its slice of the accumulator in registers, rescaling once per batch of
 //    up to four tokens.  Warps meet only at the stage mbarriers.
-//  * Merge.  At a segment's end every token subgroup stores its (m, l, acc)
-//    to the workspace slot of (CTA, sequence, subgroup) and hands the piece
-//    to the CTA's bookkeeping warp, which counts it on the sequence's
-//    counter with one acquire-release atomic.  The CTA that completes the
-//    count merges the sequence's slots (max-rescaled sums) and writes the
-//    output in the output dtype: the bookkeeping warp for pieces in the
+//  * Merge.  At a segment's end the token subgroups' (m, l, acc) go to the
+//    workspace -- one slot per subgroup, or, where the planner folds pieces
+//    (one CTA per SM), one slot per piece after a fold in shared memory -- and
+//    the piece goes to the CTA's bookkeeping warp, which counts it on the
+//    sequence's counter with one acquire-release atomic.  The CTA that
+//    completes the count merges the sequence's slots (max-rescaled sums, in
+//    slot order, so the bits do not depend on which CTA merges) and writes
+//    the output in the output dtype: the bookkeeping warp for pieces in the
 //    middle of the CTA's range, all softmax threads for the final piece,
-//    which is on the kernel's tail.  One kernel per call; the counters are
-//    left at zero for the next launch.
+//    which is on the kernel's tail.  A sequence that lies in one CTA is
+//    folded in shared memory and written out directly.  One kernel per call;
+//    the counters are left at zero for the next launch.
 //
 // Every wait is bounded (b2_common.cuh): on timeout the CTA flags
 // B2_DEVERR_TIMEOUT, drains its own copies in flight and returns.
@@ -87,8 +90,9 @@ struct AttnParams {
     int off_meta;    // within a stage
     int off_misc, off_bars;
     int off_seqlens;  // >= 0: shared int[batch] holding the clamped seq_lens (the producer's copy); -1: none
+    int fold_pieces;  // with local_merge: every piece's subgroups are folded in shared memory (one slot per piece)
     int2* seq_info;   // [batch] (first CTA, number of segments) for the combine kernel
-    float2* part_ml;  // [(grid + batch) * ksplit][n_head] (m, l)
+    float2* part_ml;  // [(grid + batch) * ksplit][n_head] (m, l); fold_pieces: one slot per piece
     float* part_acc;  // [(grid + batch) * ksplit][n_head][head_dim]
     unsigned int* counters;  // [batch] pieces finished per sequence; zero between launches
     OutSpec out;
@@ -143,15 +147,18 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* 
     return warp_sums[warp] + incl - v;
 }
 
-// Merges the partials (m, l, acc) of sequence b -- slots (i0 + b) * ks ...
-// (i0 + nseg + b) * ks - 1, one per (CTA, token subgroup) -- with a running
+// Merges the partials (m, l, acc) of sequence b -- slots (i0 + b) * sk ...
+// (i0 + nseg + b) * sk - 1, sk per (CTA, sequence) piece -- with a running
 // maximum and writes out[b] in OutT.  Each (head, E-element chunk) item is
-// taken by TPI adjacent threads, thread k of them folding slots k, k + TPI,
-// ...; the loads of SB slots per thread are issued together, so TPI * SB
-// slots cost one L2 round trip, and the TPI states are then folded with xor
-// shuffles.  A subgroup that saw no rows has l == 0 and is skipped.
-// Partials are read through L2 (__ldcg): other CTAs wrote them.  nthr must be
-// a multiple of 32 and tid / nthr cover whole warps.
+// taken by TPI adjacent threads, each folding E / TPI of its elements over
+// all slots in slot order (the (m, l) fold is repeated in each).  So the
+// result is the same to the bit whatever TPI is, and every merging path (the
+// bookkeeping warp at TPI 1, the softmax threads at up to 4) writes the same
+// bits: a launch is deterministic although which CTA merges a sequence can
+// depend on timing.  The loads of SB slots are issued together (one L2 round
+// trip per SB slots).  A partial that saw no rows has l == 0 and is skipped.
+// Partials are read through L2 (__ldcg): other CTAs wrote them.  nthr must
+// be a multiple of 32 and tid / nthr cover whole warps.
 __device__ __forceinline__ void fold_state(float& m, float& l, float* a, int E, float m2, float l2, const float* a2) {
     if (!(l2 > 0.0f)) return;
     const float mn = fmaxf(m, m2);
@@ -162,13 +169,36 @@ __device__ __forceinline__ void fold_state(float& m, float& l, float* a, int E, 
     for (int e = 0; e < E; ++e) a[e] = fmaf(a2[e], wn, a[e] * wo);
 }
 
+// EP consecutive floats from global memory through L2, EP in {1, 2, 4, 8}.
+template <int EP>
+__device__ __forceinline__ void ldcg_floats(const float* src, float* d) {
+    if constexpr (EP == 1) {
+        d[0] = __ldcg(src);
+    } else if constexpr (EP == 2) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(src));
+        d[0] = v.x;
+        d[1] = v.y;
+    } else {
+#pragma unroll
+        for (int q = 0; q < EP / 4; ++q) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + q);
+            d[4 * q] = v.x;
+            d[4 * q + 1] = v.y;
+            d[4 * q + 2] = v.z;
+            d[4 * q + 3] = v.w;
+        }
+    }
+}
+
 template <int DH, int E, int TPI, typename OutT>
 __device__ __forceinline__ void merge_partials(const float2* part_ml, const float* part_acc, const OutSpec& out, int H,
-                                               int ks, int b, int i0, int nseg, int tid, int nthr) {
+                                               int sk, int b, int i0, int nseg, int tid, int nthr) {
     constexpr int GL = DH / E;
-    constexpr int SB = 8;
-    const int nslots = nseg * ks;
-    const size_t slot0 = (static_cast<size_t>(i0) + b) * ks;
+    constexpr int EP = E / TPI;  // elements per thread
+    constexpr int SB = 8;  // slots in flight per thread (more spill in the wider instantiations)
+    static_assert(E % TPI == 0 && (EP == 1 || EP == 2 || EP % 4 == 0), "threads per merge item");
+    const int nslots = nseg * sk;
+    const size_t slot0 = (static_cast<size_t>(i0) + b) * sk;
     const int items = H * GL;
     const int per_round = nthr / TPI;
     const int sub = tid % TPI;
@@ -178,52 +208,35 @@ __device__ __forceinline__ void merge_partials(const float2* part_ml, const floa
         const bool valid = item < items;
         const int h = valid ? item / GL : 0;
         const int dc = valid ? item - h * GL : 0;
-        float mrun = -INFINITY, l = 0.0f, a[E];
+        float mrun = -INFINITY, l = 0.0f, a[EP];
 #pragma unroll
-        for (int e = 0; e < E; ++e) a[e] = 0.0f;
-        for (int s0 = 0; s0 < nslots; s0 += SB * TPI) {
+        for (int e = 0; e < EP; ++e) a[e] = 0.0f;
+        for (int s0 = 0; s0 < nslots; s0 += SB) {
             float2 ml[SB];
-            float4 v[SB][E / 4];
+            float v[SB][EP];
 #pragma unroll
             for (int j = 0; j < SB; ++j) {
-                const int s = s0 + j * TPI + sub;
+                const int s = s0 + j;
                 ml[j] = make_float2(-INFINITY, 0.0f);
                 if (valid && s < nslots) {
                     const size_t sl = slot0 + s;
                     ml[j] = __ldcg(part_ml + sl * H + h);
-                    const float4* src = reinterpret_cast<const float4*>(part_acc + (sl * H + h) * DH + dc * E);
-#pragma unroll
-                    for (int q = 0; q < E / 4; ++q) v[j][q] = __ldcg(src + q);
+                    ldcg_floats<EP>(part_acc + (sl * H + h) * DH + dc * E + sub * EP, v[j]);
                 }
             }
 #pragma unroll
-            for (int j = 0; j < SB; ++j) {
-                float a2[E];
-#pragma unroll
-                for (int q = 0; q < E / 4; ++q) {
-                    a2[4 * q] = v[j][q].x;
-                    a2[4 * q + 1] = v[j][q].y;
-                    a2[4 * q + 2] = v[j][q].z;
-                    a2[4 * q + 3] = v[j][q].w;
-                }
-                fold_state(mrun, l, a, E, ml[j].x, ml[j].y, a2);
-            }
+            for (int j = 0; j < SB; ++j) fold_state(mrun, l, a, EP, ml[j].x, ml[j].y, v[j]);
         }
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        float o[E];
 #pragma unroll
-        for (int off = 1; off < TPI; off <<= 1) {
-            const float m2 = __shfl_xor_sync(0xffffffffu, mrun, off);
-            const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
-            float a2[E];
+        for (int e = 0; e < EP; ++e) o[e] = a[e] * inv;
+        // thread sub == 0 collects the item's other elements (16-byte stores)
 #pragma unroll
-            for (int e = 0; e < E; ++e) a2[e] = __shfl_xor_sync(0xffffffffu, a[e], off);
-            fold_state(mrun, l, a, E, m2, l2, a2);
-        }
-        if (valid && sub == 0) {
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        for (int k = 1; k < TPI; ++k)
 #pragma unroll
-            for (int e = 0; e < E; ++e) a[e] *= inv;
-            store_out<OutT, E>(out, b, H, h, DH, dc, a);
-        }
+            for (int e = 0; e < EP; ++e) o[k * EP + e] = __shfl_down_sync(0xffffffffu, o[e], k);
+        if (valid && sub == 0) store_out<OutT, E>(out, b, H, h, DH, dc, o);
     }
 }
 
@@ -556,7 +569,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                         final_merge[3] = pc.z;
                     }
                 } else {
-                    merge_partials<DH, E, 1, OutT>(p.part_ml, p.part_acc, p.out, H, p.ksplit,
+                    merge_partials<DH, E, 1, OutT>(p.part_ml, p.part_acc, p.out, H, p.fold_pieces ? 1 : p.ksplit,
                                                    pc.x, pc.y, pc.z, lane, 32);
                     if (lane == 0) p.counters[pc.x] = 0u;  // every launch leaves the counters at zero
                 }
@@ -714,11 +727,15 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 }
             }
         }
-        // A sequence whose rows all lie in this CTA (one piece, nseg == 1) is
-        // merged right here through shared memory -- the stage just consumed
-        // serves as scratch, so it is released only afterwards.
+        // A piece's token subgroups can be folded right here through shared
+        // memory -- the stage just consumed serves as scratch, so it is
+        // released only afterwards: a sequence whose rows all lie in this CTA
+        // (one piece, nseg == 1) is finished and written out; with
+        // fold_pieces, any other piece leaves one partial in the workspace
+        // instead of one per subgroup.
         const bool local = last && p.local_merge != 0 && meta.w == 1;
-        if (!local) {
+        const bool lm = local || (last && p.fold_pieces != 0);
+        if (!lm) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
         }
@@ -726,7 +743,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         if (last) {
             if (p.early) pdl_wait();  // outputs / the workspace are written from here on
         }
-        if (local) {
+        if (lm) {
             // (1) every consumer warp is done with the stage's K/V; (2) every
             // subgroup's (m, l, acc) is in the scratch; (3) item-parallel merge.
             // The barriers are mbarriers with bounded waits (no CTA barrier: a
@@ -760,7 +777,26 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             }
             constexpr int EO = Elem<OutT>::kPer16B;  // output elements per item (one 16-byte store)
             constexpr int CH = DH / EO;
-            for (int it = tid; it < H * CH; it += p.ncons) {
+            if (!local) {
+                // the piece's partial, slot (cta + b) of one per piece
+                const size_t slot = static_cast<size_t>(cta) + b;
+                for (int it = tid; it < H * (DH / 4); it += p.ncons) {
+                    const int h = it / (DH / 4);
+                    const int c = it - h * (DH / 4);
+                    float mrun = -INFINITY, l = 0.0f, a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    for (int j = 0; j < ks; ++j) {
+                        const float2 ml = ml_s[j * H + h];
+                        const float4 v =
+                            *reinterpret_cast<const float4*>(acc_s + (static_cast<size_t>(j) * H + h) * DH + c * 4);
+                        const float a2[4] = {v.x, v.y, v.z, v.w};
+                        fold_state(mrun, l, a, 4, ml.x, ml.y, a2);
+                    }
+                    __stcg(reinterpret_cast<float4*>(p.part_acc + (slot * H + h) * DH + c * 4),
+                           make_float4(a[0], a[1], a[2], a[3]));
+                    if (c == 0) __stcg(p.part_ml + slot * H + h, make_float2(mrun, l));
+                }
+            }
+            for (int it = tid; local && it < H * CH; it += p.ncons) {
                 const int h = it / CH;
                 const int c = it - h * CH;
                 float mrun = -INFINITY, l = 0.0f, a[EO];
@@ -796,7 +832,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             // ---- piece end: this subgroup's partial goes to the workspace.
             // Slot (cta + b) is unique per (CTA, sequence) pair: along the CTA
             // order both indices only grow, so cta + b never repeats.
-            if (active && !local) {
+            if (active && !lm) {
                 const size_t slot = (static_cast<size_t>(cta) + b) * ks + ts;
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
@@ -839,13 +875,14 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         // The bookkeeper's acquire on the counter, then its arrival on
         // book_done, order the other CTAs' partials before these reads.
         const int fb = final_merge[1], fi0 = final_merge[2], fn = final_merge[3];
+        const int sk = p.fold_pieces ? 1 : ks;  // partial slots per piece
         const OutSpec& o = p.out;
         if (p.ncons >= 4 * H * GL)
-            merge_partials<DH, E, 4, OutT>(p.part_ml, p.part_acc, o, H, ks, fb, fi0, fn, tid, p.ncons);
+            merge_partials<DH, E, 4, OutT>(p.part_ml, p.part_acc, o, H, sk, fb, fi0, fn, tid, p.ncons);
         else if (p.ncons >= 2 * H * GL)
-            merge_partials<DH, E, 2, OutT>(p.part_ml, p.part_acc, o, H, ks, fb, fi0, fn, tid, p.ncons);
+            merge_partials<DH, E, 2, OutT>(p.part_ml, p.part_acc, o, H, sk, fb, fi0, fn, tid, p.ncons);
         else
-            merge_partials<DH, E, 1, OutT>(p.part_ml, p.part_acc, o, H, ks, fb, fi0, fn, tid, p.ncons);
+            merge_partials<DH, E, 1, OutT>(p.part_ml, p.part_acc, o, H, sk, fb, fi0, fn, tid, p.ncons);
         if (tid == 0) p.counters[fb] = 0u;  // every launch leaves the counters at zero
     }
 }
