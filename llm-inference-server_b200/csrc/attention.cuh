@@ -91,6 +91,9 @@ struct AttnParams {
     int off_misc, off_bars;
     int off_seqlens;  // >= 0: shared int[batch] holding the clamped seq_lens (the producer's copy); -1: none
     int fold_pieces;  // with local_merge: every piece's subgroups are folded in shared memory (one slot per piece)
+    int spec_blocks;  // flags 0: paged blocks of the CTA's range the speculative pass prefetches into L2 (<= 31)
+    int off_stash;    // >= 0 (early start only): shared [sk][H][head_dim] fp32 + [sk][H] (m, l), sk = fold_pieces ? 1
+                      // : ksplit, holding the CTA's first mid-range piece until the bookkeeping warp writes it out
     int2* seq_info;   // [batch] (first CTA, number of segments) for the combine kernel
     float2* part_ml;  // [(grid + batch) * ksplit][n_head] (m, l); fold_pieces: one slot per piece
     float* part_acc;  // [(grid + batch) * ksplit][n_head][head_dim]
@@ -286,29 +289,42 @@ __device__ __forceinline__ void speculative_prefetch(const AttnParams& p, int* m
     __syncthreads();
     const int b0 = misc[0];
     if (tid < 32 && b0 >= 0 && e_unit > s_unit) {
+        // Lane k < spec_blocks: the k-th paged block of this CTA's range (its
+        // K and V runs), walking at most 8 sequences from the first one;
+        // lane 31: the first sequence's q row.
         const int lane = tid;
-        const int cs = clamp_seq_len(__ldcg(p.seq_lens + b0), p.mbps);
-        const int t_lo = static_cast<int>(s_unit - misc[1]);
-        const int t_hi = static_cast<int>(min(e_unit - misc[1], static_cast<long long>(cs)));
-        const int j0 = t_lo / kBlockTokens;
         const size_t row_elems = static_cast<size_t>(p.n_kv_head) * DH;
         const size_t slab_elems = row_elems * kBlockTokens;
-        if (lane < 2) {
-            const int j = j0 + lane;
-            const int r_lo = max(t_lo - j * kBlockTokens, 0);
-            const int r_hi = min(t_hi - j * kBlockTokens, kBlockTokens);
-            if (r_hi > r_lo) {
-                const int blk = __ldcg(p.block_tables + static_cast<size_t>(b0) * p.mbps + j);
-                if (blk >= 0 && blk < p.num_blocks) {
-                    const char* src = static_cast<const char*>(p.pool) +
-                                      ((static_cast<size_t>(blk) * p.n_layer + p.layer_idx) * 2 * slab_elems +
-                                       static_cast<size_t>(r_lo) * row_elems) * es;
-                    const uint32_t bytes = static_cast<uint32_t>((r_hi - r_lo) * row_elems * es);
-                    bulk_prefetch_l2(src, bytes);
-                    bulk_prefetch_l2(src + slab_elems * es, bytes);
+        if (lane < p.spec_blocks) {
+            int k = lane;
+            long long P = misc[1];  // rows before sequence b
+            for (int b = b0, walked = 0; b < B && P < e_unit && walked < 8; ++b, ++walked) {
+                const int cs = clamp_seq_len(__ldcg(p.seq_lens + b), p.mbps);
+                const long long u = max(s_unit, P);
+                const int t_lo = static_cast<int>(u - P);
+                const int t_hi = static_cast<int>(min(e_unit - P, static_cast<long long>(cs)));
+                if (t_hi > t_lo) {
+                    const int j0 = t_lo / kBlockTokens, j1 = (t_hi - 1) / kBlockTokens + 1;
+                    if (k < j1 - j0) {
+                        const int j = j0 + k;
+                        const int r_lo = max(t_lo - j * kBlockTokens, 0);
+                        const int r_hi = min(t_hi - j * kBlockTokens, kBlockTokens);
+                        const int blk = __ldcg(p.block_tables + static_cast<size_t>(b) * p.mbps + j);
+                        if (blk >= 0 && blk < p.num_blocks && r_hi > r_lo) {
+                            const char* src = static_cast<const char*>(p.pool) +
+                                              ((static_cast<size_t>(blk) * p.n_layer + p.layer_idx) * 2 * slab_elems +
+                                               static_cast<size_t>(r_lo) * row_elems) * es;
+                            const uint32_t bytes = static_cast<uint32_t>((r_hi - r_lo) * row_elems * es);
+                            bulk_prefetch_l2(src, bytes);
+                            bulk_prefetch_l2(src + slab_elems * es, bytes);
+                        }
+                        break;
+                    }
+                    k -= j1 - j0;
                 }
+                P += cs;
             }
-        } else if (lane == 2) {
+        } else if (lane == 31) {
             bulk_prefetch_l2(static_cast<const char*>(p.q) + static_cast<size_t>(b0) * p.q_row_stride * es,
                              static_cast<uint32_t>(p.n_head * DH * es));
         }
@@ -381,10 +397,34 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     // ---- prologue: per-sequence row counts, global prefix, this CTA's range
     // (L2 loads: with p.early == 0 the speculative pass may have read these
     // addresses before the wait, so nothing may come from a stale L1 line)
+    if (p.early != 0 && tid == 0) {
+        // The producer reads the block tables only once the scan below has
+        // placed this CTA; a small table is brought into L2 now, while the
+        // seq_lens loads are in flight, so that read is not a second DRAM
+        // round trip.  (With p.early == 0 the speculative pass has touched
+        // this CTA's entries already.)  Rounded out to 16-byte granules that
+        // each hold table bytes, so nothing outside mapped memory is named.
+        const size_t bt_bytes = static_cast<size_t>(B) * p.mbps * sizeof(int);
+        if (bt_bytes <= 32768) {
+            const uintptr_t lo = reinterpret_cast<uintptr_t>(p.block_tables) & ~static_cast<uintptr_t>(15);
+            const uintptr_t hi = (reinterpret_cast<uintptr_t>(p.block_tables) + bt_bytes + 15) &
+                                 ~static_cast<uintptr_t>(15);
+            bulk_prefetch_l2(reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo));
+        }
+    }
     const int per = (B + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
     const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
+    // A thread's first kSeqLenRegs values stay in registers for the second
+    // pass below (a second trip to L2 would sit on every CTA's start-up).
+    constexpr int kSeqLenRegs = 4;
+    int sl_raw[kSeqLenRegs];
     int local = 0;
-    for (int b = b_lo; b < b_hi; ++b) local += clamp_seq_len(__ldcg(p.seq_lens + b), p.mbps);
+#pragma unroll
+    for (int i = 0; i < kSeqLenRegs; ++i) {
+        sl_raw[i] = b_lo + i < b_hi ? __ldcg(p.seq_lens + b_lo + i) : 0;
+        local += clamp_seq_len(sl_raw[i], p.mbps);
+    }
+    for (int b = b_lo + kSeqLenRegs; b < b_hi; ++b) local += clamp_seq_len(__ldcg(p.seq_lens + b), p.mbps);
     int N = 0;
     const int excl = block_exclusive_scan(local, misc + 2, &N);
     const int G = min(static_cast<int>(gridDim.x), max(N, 1));
@@ -393,7 +433,11 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
     {
         int run = excl;
         for (int b = b_lo; b < b_hi; ++b) {
-            const int raw = __ldcg(p.seq_lens + b);
+            int raw = 0;
+#pragma unroll
+            for (int i = 0; i < kSeqLenRegs; ++i)
+                if (b == b_lo + i) raw = sl_raw[i];
+            if (b >= b_lo + kSeqLenRegs) raw = __ldcg(p.seq_lens + b);
             const int cl = clamp_seq_len(raw, p.mbps);
             if (p.off_seqlens >= 0) reinterpret_cast<int*>(smem + p.off_seqlens)[b] = cl;
             if (cl > 0 && run <= s_unit && s_unit < run + cl) {
@@ -552,16 +596,32 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             const int rk = k % R;
             ok = mbar_wait_bounded(&piece_full[rk], static_cast<uint32_t>(k / R) & 1u);
             if (!ok) break;
-            const int4 pc = pieces[rk];
+            const int4 pc = pieces[rk];  // w: bit 0 the CTA's final piece, bit 1 its partials are in the stash
             if (p.early) pdl_wait();  // counters and outputs are written below
             __syncwarp();  // every lane has read the entry before it is released
             if (lane == 0) mbar_arrive(&piece_empty[rk]);
+            if (pc.w & 2) {
+                // The consumers left this piece's partials in the stash (they
+                // did not wait for the kernel ahead); write them to the piece's
+                // workspace slots.  Each lane fences its stores before the
+                // warp barrier, so lane 0's counter update below publishes them.
+                const int sk = p.fold_pieces ? 1 : p.ksplit;
+                const size_t slot0 = (static_cast<size_t>(cta) + pc.x) * sk;
+                const float4* sa = reinterpret_cast<const float4*>(smem + p.off_stash);
+                float4* da = reinterpret_cast<float4*>(p.part_acc + slot0 * H * DH);
+                const int n4 = sk * H * DH / 4;
+                for (int i = lane; i < n4; i += 32) __stcg(da + i, sa[i]);
+                const float2* sm = reinterpret_cast<const float2*>(sa + n4);
+                for (int i = lane; i < sk * H; i += 32) __stcg(p.part_ml + slot0 * H + i, sm[i]);
+                __threadfence();
+                __syncwarp();
+            }
             int last = 0;  // pc.z == 0: the piece was merged by the softmax threads (one-piece sequence)
             if (lane == 0 && pc.z > 0)
                 last = count_piece(p.counters + pc.x) == static_cast<unsigned>(pc.z - 1) ? 1 : 0;
             last = __shfl_sync(0xffffffffu, last, 0);
             if (last) {
-                if (pc.w) {
+                if (pc.w & 1) {
                     if (lane == 0) {
                         final_merge[0] = 1;
                         final_merge[1] = pc.x;
@@ -574,7 +634,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                     if (lane == 0) p.counters[pc.x] = 0u;  // every launch leaves the counters at zero
                 }
             }
-            if (pc.w) break;
+            if (pc.w & 1) break;
         }
         if (!ok && lane == 0) flag_error(B2_DEVERR_TIMEOUT);
         __syncwarp();
@@ -735,12 +795,16 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
         // instead of one per subgroup.
         const bool local = last && p.local_merge != 0 && meta.w == 1;
         const bool lm = local || (last && p.fold_pieces != 0);
+        // An early-start launch's first piece, when it ends in mid-range,
+        // leaves its partials in the stash and the consumers stream on; the
+        // bookkeeping warp waits for the kernel ahead and writes them out.
+        const bool stash = last && !local && !final_stage && npieces == 0 && p.early != 0 && p.off_stash >= 0;
         if (!lm) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
         }
 
-        if (last) {
+        if (last && !stash) {
             if (p.early) pdl_wait();  // outputs / the workspace are written from here on
         }
         if (lm) {
@@ -778,8 +842,10 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             constexpr int EO = Elem<OutT>::kPer16B;  // output elements per item (one 16-byte store)
             constexpr int CH = DH / EO;
             if (!local) {
-                // the piece's partial, slot (cta + b) of one per piece
+                // the piece's partial, slot (cta + b) of one per piece (or the stash)
                 const size_t slot = static_cast<size_t>(cta) + b;
+                float* st_acc = reinterpret_cast<float*>(smem + p.off_stash);
+                float2* st_ml = reinterpret_cast<float2*>(st_acc + static_cast<size_t>(H) * DH);
                 for (int it = tid; it < H * (DH / 4); it += p.ncons) {
                     const int h = it / (DH / 4);
                     const int c = it - h * (DH / 4);
@@ -791,9 +857,15 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                         const float a2[4] = {v.x, v.y, v.z, v.w};
                         fold_state(mrun, l, a, 4, ml.x, ml.y, a2);
                     }
-                    __stcg(reinterpret_cast<float4*>(p.part_acc + (slot * H + h) * DH + c * 4),
-                           make_float4(a[0], a[1], a[2], a[3]));
-                    if (c == 0) __stcg(p.part_ml + slot * H + h, make_float2(mrun, l));
+                    if (stash) {
+                        *reinterpret_cast<float4*>(st_acc + static_cast<size_t>(h) * DH + c * 4) =
+                            make_float4(a[0], a[1], a[2], a[3]);
+                        if (c == 0) st_ml[h] = make_float2(mrun, l);
+                    } else {
+                        __stcg(reinterpret_cast<float4*>(p.part_acc + (slot * H + h) * DH + c * 4),
+                               make_float4(a[0], a[1], a[2], a[3]));
+                        if (c == 0) __stcg(p.part_ml + slot * H + h, make_float2(mrun, l));
+                    }
                 }
             }
             for (int it = tid; local && it < H * CH; it += p.ncons) {
@@ -832,7 +904,21 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             // ---- piece end: this subgroup's partial goes to the workspace.
             // Slot (cta + b) is unique per (CTA, sequence) pair: along the CTA
             // order both indices only grow, so cta + b never repeats.
-            if (active && !lm) {
+            if (active && !lm && stash) {
+                // the stash mirrors the slots' layout: [ts][h][head_dim], then [ts][h] (m, l)
+                float* st_acc = reinterpret_cast<float*>(smem + p.off_stash);
+                float2* st_ml = reinterpret_cast<float2*>(st_acc + static_cast<size_t>(ks) * H * DH);
+#pragma unroll
+                for (int g = 0; g < QG; ++g) {
+                    const int h = hk * QG + g;
+                    float* dst = st_acc + (static_cast<size_t>(ts) * H + h) * DH + dgt * CPT * E;
+#pragma unroll
+                    for (int e = 0; e < CPT * E; e += 4)
+                        *reinterpret_cast<float4*>(dst + e) =
+                            make_float4(acc[g][e], acc[g][e + 1], acc[g][e + 2], acc[g][e + 3]);
+                    if (dgt == 0) st_ml[ts * H + h] = make_float2(m_run[g], l_run[g]);
+                }
+            } else if (active && !lm) {
                 const size_t slot = (static_cast<size_t>(cta) + b) * ks + ts;
 #pragma unroll
                 for (int g = 0; g < QG; ++g) {
@@ -855,7 +941,7 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
             if (tid == 0) {
                 if (!mbar_wait_bounded(&piece_empty[rk], (static_cast<uint32_t>(npieces / R) & 1u) ^ 1u))
                     flag_error(B2_DEVERR_TIMEOUT);
-                pieces[rk] = make_int4(b, meta.z, local ? 0 : meta.w, final_stage ? 1 : 0);
+                pieces[rk] = make_int4(b, meta.z, local ? 0 : meta.w, (final_stage ? 1 : 0) | (stash ? 2 : 0));
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&piece_full[rk]);
