@@ -1020,6 +1020,72 @@ def run_serve_ref(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_lm_head(args, rank: int) -> None:
+    """The decode step's tied lm_head + greedy argmax at the GPT-2 XL shape
+    (d_model 1600, vocab 50257 padded to 50264 rows, bf16, weights N(0, 0.02),
+    x N(0, 1)): b2_lm_head_argmax (one tensor-core launch, no logits) against
+    the engine's unfused pair (cuBLAS GEMM into bf16 logits + b2_argmax_rows),
+    at batch 1 .. 512.  Four weight copies rotate (161 MB each) so every launch
+    streams its weights from HBM; a CUDA graph of 40 launches per timing, best
+    of 3.  The tokens of the two paths are compared on the last launch."""
+    import torch
+    if rank != 0:
+        return
+    b2 = import_package()
+    b2.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    V, Vp, D = 50257, 50264, 1600
+    g = torch.Generator(device=dev).manual_seed(5)
+    ws_ = [(torch.randn(Vp, D, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(4)]
+    rows = []
+    for B in (1, 32, 128, 256, 512):
+        x = torch.randn(B, D, generator=g, device=dev).to(torch.bfloat16)
+        tok = torch.empty(B, dtype=torch.int32, device=dev)
+        ref = torch.empty(B, dtype=torch.int32, device=dev)
+        logits = torch.empty(B, Vp, device=dev, dtype=torch.bfloat16)
+        wsp = b2.lm_head_argmax_workspace(B, dev)
+
+        def fused(i):
+            b2.lm_head_argmax(tok, x, ws_[i % 4], vocab=V, workspace=wsp)
+
+        def unfused(i):
+            torch.matmul(x, ws_[i % 4].T, out=logits)
+            b2.argmax(ref, logits, vocab=V)
+
+        def timeit(f):
+            for i in range(8):
+                f(i)
+            torch.cuda.synchronize(dev)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for i in range(40):
+                    f(i)
+            gr.replay()
+            torch.cuda.synchronize(dev)
+            best = 1e9
+            for _ in range(3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda._sleep(SPIN_CYCLES)
+                e0.record(stream)
+                gr.replay()
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+                best = min(best, e0.elapsed_time(e1) * 1e3 / 40)
+            return best
+
+        tf, tu = timeit(fused), timeit(unfused)
+        rows.append({"batch": B, "fused_us": round(tf, 2), "cublas_argmax_us": round(tu, 2),
+                     "fused_weight_gbs": round(Vp * D * 2 / tf / 1e3, 1),
+                     "tokens_identical": bool(torch.equal(tok, ref))})
+    print(json.dumps({"metric": "GPT-2 XL lm_head + argmax, us per call", "unit": "us", "higher_is_better": False,
+                      "dtype": "bf16", "data": "synthetic", "rows": rows, "device_errors": b2.device_errors(),
+                      "config": {"workload": "tied lm_head + greedy argmax, d_model 1600, vocab 50257, bf16",
+                                 "l2": "4 weight copies of 161 MB rotated"}}), flush=True)
+
+
 def run_prefill(args, rank: int, world: int) -> None:
     """Prompt tokens/s of b2_engine_prefill (prefill_bench.py), rank 0."""
     if rank != 0:
@@ -1061,7 +1127,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--no-engine", action="store_true",
                     help="default workload: skip the GPT-2 records attached to the attention line")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + list(ENGINE_NAMES) + ["serve-medium", "serve-ref", "prefill-medium"],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + list(ENGINE_NAMES) + ["serve-medium", "serve-ref", "prefill-medium", "lm-head"],
                     default="mha",
                     help="mha: the headline microbench (+ GPT-2 XL / small decode records); gqa: grouped-query long "
                          "contexts (tensor-core kernel); gpt2-xl / gpt2-medium / gpt2-xl-heads: GPT-2 decode "
@@ -1090,6 +1156,12 @@ def main() -> None:
             run_serve(args, rank, world)
         else:
             run_serve_ref(args, rank)
+        return
+    if args.workload == "lm-head":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the lm_head comparison has no CPU arm"}), flush=True)
+            return
+        run_lm_head(args, rank)
         return
     if args.workload == "prefill-medium":
         if args.impl == "reference":

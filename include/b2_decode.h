@@ -427,6 +427,43 @@ typedef struct B2LinearArgs {
 
 B2_API int b2_linear(const B2LinearArgs* args, b2_stream_t stream);
 
+/* ------------------------------------------------------------------ lm_head + argmax
+ * out_tokens[b] = the v < vocab that maximises T(x[b] . w[v]): the tied lm_head
+ * GEMM and the greedy argmax in one kernel on the tensor cores (tcgen05), the
+ * logits never written to memory.  Replaces gemm_rowmajor(bucket, D, vocab,
+ * d_x, wte, d_logits) + kernels::launch_argmax (gpu-engine/src/engine.cu:202-203;
+ * kernels.h:89-92, logits.cu:18-57).  Each logit is the fp32 dot product
+ * rounded to the dtype, as the unfused path stores it; ties go to the lowest
+ * index, like the reference CPU path's first maximum (cpu_model.cpp:182-196);
+ * NaN logits never win against a number.  The dot products are summed in a
+ * different order from cuBLAS's, so a near-tie can resolve differently from
+ * the unfused GEMM + b2_argmax_rows.  F16 and BF16 only (B2_ERR_DTYPE for F32).
+ *   x: [batch][x_row_stride], the final hidden states.
+ *   w: [>= vocab rows][d_model] row-major (rows past vocab are never read
+ *      into a result).
+ * x and w 16-byte aligned; d_model and x_row_stride multiples of 8.
+ * workspace: b2_lm_head_argmax_workspace_bytes(batch) bytes, 16-byte aligned,
+ * zeroed by the caller once; every launch leaves it zeroed (the last CTA to
+ * finish clears it, also after a bounded wait gave up).  Programmatic
+ * dependent launch: w streams while the
+ * previous kernel on the stream finishes (w must not be that kernel's output;
+ * x may be).  Launches that share a workspace must not overlap on the GPU. */
+typedef struct B2LmHeadArgmaxArgs {
+    int32_t dtype;        /* B2_F16 or B2_BF16, for x and w */
+    const void* x;        /* [batch][x_row_stride] */
+    int64_t x_row_stride; /* elements */
+    const void* w;        /* [vocab (or more) rows][d_model] */
+    int32_t batch;        /* 0 .. 65535 * 256 */
+    int32_t d_model;
+    int32_t vocab;
+    int32_t* out_tokens;  /* [batch] */
+    void* workspace;
+    size_t workspace_bytes;
+} B2LmHeadArgmaxArgs;
+
+B2_API size_t b2_lm_head_argmax_workspace_bytes(int32_t batch);
+B2_API int b2_lm_head_argmax(const B2LmHeadArgmaxArgs* args, b2_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -126,6 +126,15 @@ B2_API int b2_engine_set_linear_tensor_cores(b2_engine* eng, int32_t enabled);
  * the captured graphs. */
 B2_API int b2_engine_set_gemm_mode(b2_engine* eng, int32_t mode);
 
+/* The tied lm_head GEMM and the greedy argmax of decode steps and prefill as
+ * one b2_lm_head_argmax launch (tensor cores, no logits written) for f16 /
+ * bf16 models; f32 engines keep cuBLAS + argmax.  Replaces the pair
+ * gemm_rowmajor(.., wte, d_logits) + launch_argmax (gpu-engine/src/engine.cu:
+ * 202-203).  Default off: on B200 it measured slower than cuBLAS + argmax at
+ * every batch size tried.  With it on, b2_engine_last_step_outputs has no
+ * logits to copy (they are never formed).  Switching drops the captured graphs. */
+B2_API int b2_engine_set_lm_head_fused(b2_engine* eng, int32_t enabled);
+
 /* Inspection (no reference counterpart): copies the first `rows` lanes of the
  * last decode_step's final LayerNorm output ([rows][d_model]) and logits
  * ([rows][vocab_size]) into host buffers (either may be NULL), in the engine's

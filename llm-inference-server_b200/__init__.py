@@ -35,6 +35,7 @@ DECODE_SYMBOLS = (
     "b2_paged_attention_noalloc", "b2_argmax_rows", "b2_paged_attention_gather", "b2_tp_barrier",
     "b2_tp_epoch_bump", "b2_linear", "b2_prefill_attention", "b2_paged_attention_host",
     "b2_tp_barrier_timed", "b2_device_error_word", "b2_raise_device_error",
+    "b2_lm_head_argmax_workspace_bytes", "b2_lm_head_argmax",
 )
 
 _c_int, _c_float, _vp = ctypes.c_int32, ctypes.c_float, ctypes.c_void_p
@@ -64,6 +65,12 @@ class LinearArgs(ctypes.Structure):
     _fields_ = [("dtype", _c_int), ("x", _vp), ("x_row_stride", ctypes.c_int64), ("w", _vp), ("bias", _vp),
                 ("y", _vp), ("y_row_stride", ctypes.c_int64), ("batch", _c_int), ("in_features", _c_int),
                 ("out_features", _c_int), ("epilogue", _c_int)]
+
+
+class LmHeadArgmaxArgs(ctypes.Structure):
+    _fields_ = [("dtype", _c_int), ("x", _vp), ("x_row_stride", ctypes.c_int64), ("w", _vp), ("batch", _c_int),
+                ("d_model", _c_int), ("vocab", _c_int), ("out_tokens", _vp), ("workspace", _vp),
+                ("workspace_bytes", ctypes.c_size_t)]
 
 
 class PrefillAttnArgs(ctypes.Structure):
@@ -113,6 +120,9 @@ def load() -> ctypes.CDLL:
     lib.b2_argmax.argtypes = [_c_int, _vp, _vp, _c_int, _c_int, _vp]
     lib.b2_argmax_rows.argtypes = [_c_int, _vp, _vp, ctypes.c_int64, _c_int, _c_int, _vp]
     lib.b2_linear.argtypes = [ctypes.POINTER(LinearArgs), _vp]
+    lib.b2_lm_head_argmax_workspace_bytes.argtypes = [_c_int]
+    lib.b2_lm_head_argmax_workspace_bytes.restype = ctypes.c_size_t
+    lib.b2_lm_head_argmax.argtypes = [ctypes.POINTER(LmHeadArgmaxArgs), _vp]
     lib.b2_prefill_attention.argtypes = [ctypes.POINTER(PrefillAttnArgs), _vp]
     lib.b2_paged_attention_noalloc.argtypes = [ctypes.POINTER(PagedAttnArgs), _vp]
     lib.b2_tp_barrier.argtypes = [_vp, _vp, _c_int, _c_int, _vp, _c_int, _vp]
@@ -249,6 +259,30 @@ def linear(y, x, w, bias=None, epilogue=LINEAR_STORE, stream=None):
     a = LinearArgs(dtype_code(w.dtype), _ptr(x), x.stride(0), _ptr(w), _ptr(bias), _ptr(y), y.stride(0), x.shape[0],
                    w.shape[1], w.shape[0], epilogue)
     _check(load().b2_linear(ctypes.byref(a), _stream(stream)))
+
+
+def lm_head_argmax_workspace(batch: int, device=None):
+    """A zeroed workspace for lm_head_argmax at up to `batch` rows (every
+    launch leaves it zeroed again)."""
+    import torch
+    n = int(load().b2_lm_head_argmax_workspace_bytes(batch))
+    return torch.zeros(n, dtype=torch.uint8, device=device if device is not None else "cuda")
+
+
+def lm_head_argmax(out_tokens, x, w, vocab=None, workspace=None, stream=None):
+    """out_tokens[b] = argmax_v dtype(x[b] . w[v]) over v < vocab
+    (b2_lm_head_argmax: the tied lm_head GEMM and the greedy argmax in one
+    tensor-core kernel).  x [batch, d_model] (rows may be strided), w
+    [>= vocab, d_model] contiguous, out_tokens int32 [batch]."""
+    if not w.is_contiguous() or x.stride(1) != 1:
+        raise ValueError("w must be contiguous and x must have unit column stride")
+    batch, d = x.shape
+    vocab = w.shape[0] if vocab is None else vocab
+    if workspace is None:
+        workspace = lm_head_argmax_workspace(batch, x.device)
+    a = LmHeadArgmaxArgs(dtype_code(w.dtype), _ptr(x), x.stride(0), _ptr(w), batch, d, vocab, _ptr(out_tokens),
+                         _ptr(workspace), workspace.numel() * workspace.element_size())
+    _check(load().b2_lm_head_argmax(ctypes.byref(a), _stream(stream)))
 
 
 def prefill_attention(out, q, q_row_stride, kv_pool, block_tables, seq_lens_pre, q_start, q_len, *, n_head, n_kv_head,

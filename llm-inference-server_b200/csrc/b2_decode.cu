@@ -25,6 +25,7 @@
 #include "attention_tc.cuh"
 #include "b2_common.cuh"
 #include "linear_tc.cuh"
+#include "lm_head_tc.cuh"
 #include "prefill_tc.cuh"
 #include "rows.cuh"
 #include "tp.cuh"
@@ -1262,6 +1263,114 @@ extern "C" int b2_linear(const B2LinearArgs* a, b2_stream_t stream) {
                     "x, w and y must be 16-byte aligned with in_features, x_row_stride and y_row_stride multiples of 8");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     return a->dtype == B2_F16 ? linear_epi<__half>(a, s) : linear_epi<__nv_bfloat16>(a, s);
+}
+
+// ------------------------------------------------------------ lm_head + argmax
+namespace b2 {
+namespace {
+
+struct LmPlan {
+    int chunks = 0, bn = 0, kb_total = 0, n_tiles = 0, grid = 0, stages = 0, smem = 0;
+};
+
+size_t lm_workspace_bytes(int batch) {
+    return align_up(16 + static_cast<size_t>(batch > 0 ? batch : 0) * sizeof(unsigned long long), 256);
+}
+
+// Batch chunks of <= 256 rows (the MMA's N), whole K per work item; one
+// persistent CTA per SM (at most one per item) with as deep a ring as fits.
+int plan_lm_head(const B2LmHeadArgmaxArgs* a, LmPlan* pl) {
+    int dev = -1;
+    const DeviceInfo di = device_info(&dev);
+    if (dev < 0 || di.sms <= 0) return fail(B2_ERR_DEVICE, "no current CUDA device");
+    pl->chunks = (a->batch + kLmMaxCols - 1) / kLmMaxCols;
+    const int per = (a->batch + pl->chunks - 1) / pl->chunks;
+    pl->bn = (std::max(per, 16) + 15) / 16 * 16;
+    pl->kb_total = (a->d_model + kLmKBlock - 1) / kLmKBlock;
+    pl->n_tiles = (a->vocab + kLmRows - 1) / kLmRows;
+    const long long items = static_cast<long long>(pl->n_tiles) * pl->chunks;
+    if (items > (1LL << 30)) return fail(B2_ERR_SHAPE, "vocab x batch too large");
+    // (two CTAs per SM with 3-stage rings: faster at batch <= 32, slower
+    // from 128 up; 12 stages: no gain over 8)
+    pl->grid = static_cast<int>(std::min<long long>(items, di.sms));
+    int stages = 8;
+    while (stages > 2 && LmLayout::bytes(pl->bn, stages) > di.max_smem_optin) --stages;
+    if (LmLayout::bytes(pl->bn, stages) > di.max_smem_optin)
+        return fail(B2_ERR_UNSUPPORTED, "lm_head + argmax: tile does not fit in shared memory");
+    pl->stages = stages;
+    pl->smem = LmLayout::bytes(pl->bn, stages);
+    return B2_OK;
+}
+
+template <typename T>
+int lm_head_t(const B2LmHeadArgmaxArgs* a, cudaStream_t stream) {
+    auto kern = lm_head_argmax_kernel<T>;
+    static std::atomic<uint64_t> smem_set{0};
+    int dev = -1;
+    const DeviceInfo di = device_info(&dev);
+    int rc = ensure_max_smem(kern, smem_set, dev, di.max_smem_optin);
+    if (rc != B2_OK) return rc;
+    LmPlan pl;
+    rc = plan_lm_head(a, &pl);
+    if (rc != B2_OK) return rc;
+    CUtensorMap wm, xm;
+    rc = encode_rows_map(&wm, a->dtype, a->w, a->d_model, a->vocab, a->d_model, kLmRows);
+    if (rc != B2_OK) return rc;
+    rc = encode_rows_map(&xm, a->dtype, a->x, a->d_model, a->batch, a->x_row_stride, pl.bn);
+    if (rc != B2_OK) return rc;
+    LmParams lp;
+    lp.batch = a->batch;
+    lp.vocab = a->vocab;
+    lp.bn = pl.bn;
+    lp.kb_total = pl.kb_total;
+    lp.stages = pl.stages;
+    lp.n_tiles = pl.n_tiles;
+    lp.chunks = pl.chunks;
+
+    char* ws = static_cast<char*>(a->workspace);
+    lp.counter = reinterpret_cast<unsigned int*>(ws);
+    lp.keys = reinterpret_cast<unsigned long long*>(ws + 16);
+    lp.tokens = a->out_tokens;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
+    cfg.blockDim = dim3(kLmThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(pl.smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, lp, wm, xm);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        g_last_error = cudaGetErrorString(e);
+        return static_cast<int>(e);
+    }
+    return launch_status();
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" size_t b2_lm_head_argmax_workspace_bytes(int32_t batch) { return b2::lm_workspace_bytes(batch); }
+
+extern "C" int b2_lm_head_argmax(const B2LmHeadArgmaxArgs* a, b2_stream_t stream) {
+    using namespace b2;
+    if (a == nullptr) return fail(B2_ERR_NULL, "args is NULL");
+    if (a->dtype != B2_F16 && a->dtype != B2_BF16)
+        return fail(B2_ERR_DTYPE, "b2_lm_head_argmax runs F16 and BF16 on the tensor cores");
+    if (a->batch < 0 || a->d_model <= 0 || a->vocab <= 0) return fail(B2_ERR_SHAPE, "bad sizes");
+    if (a->batch == 0) return B2_OK;
+    if (!a->x || !a->w || !a->out_tokens || !a->workspace)
+        return fail(B2_ERR_NULL, "x, w, out_tokens and workspace are required");
+    if (a->x_row_stride < a->d_model) return fail(B2_ERR_SHAPE, "x_row_stride must cover d_model");
+    if (a->d_model % 8 != 0 || a->x_row_stride % 8 != 0 || !aligned16(a->x) || !aligned16(a->w))
+        return fail(B2_ERR_ALIGN, "x and w must be 16-byte aligned with d_model and x_row_stride multiples of 8");
+    if (!aligned16(a->workspace) || a->workspace_bytes < lm_workspace_bytes(a->batch))
+        return fail(B2_ERR_WORKSPACE, "workspace missing, misaligned or smaller than b2_lm_head_argmax_workspace_bytes");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return a->dtype == B2_F16 ? lm_head_t<__half>(a, s) : lm_head_t<__nv_bfloat16>(a, s);
 }
 
 // ------------------------------------------------------------ prefill attention

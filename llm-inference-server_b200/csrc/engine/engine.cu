@@ -229,6 +229,11 @@ struct Engine {
          *d_ff = nullptr, *d_ff_out = nullptr, *d_logits = nullptr;
     void* attn_ws = nullptr;
     size_t attn_ws_bytes = 0;
+    // b2_engine_set_lm_head_fused: the tied lm_head GEMM and the argmax as one
+    // b2_lm_head_argmax launch (f16 / bf16), with its workspace (zeroed once)
+    bool lm_fused = false;
+    void* lm_ws = nullptr;
+    size_t lm_ws_bytes = 0;
     std::unordered_map<int, Seq> seqs;
     int next_id = 0;
     bool use_graphs = true;
@@ -297,7 +302,7 @@ struct Engine {
                             d_attn, d_attn_out, d_ff, d_ff_out, d_logits, attn_ws, tp_weights, d_gath,
                             d_flags, d_epoch, d_peer_outs, d_peer_flags, d_pin, d_pseq_post, d_pnext,
                             p_resid, p_x, p_qkv, p_attn, p_attn_out, p_ff, p_ff_out, p_last, p_logits,
-                            p_attn_ws, d_slot_tables, d_upd, d_attn_loc};
+                            p_attn_ws, d_slot_tables, d_upd, d_attn_loc, lm_ws};
         for (void* p : dev_ptrs)
             if (p) cudaFree(p);
         if (h_in) cudaFreeHost(h_in);
@@ -671,12 +676,35 @@ struct Engine {
             delta_bias = w.fc_proj_b;
         }
         b2_ok(b2_add_layernorm(dt, d_x, d_resid, delta, delta_bias, d_resid, lnf_g, lnf_b, bucket, D, eps, s), "ln_f");
-        // lm_head tied to wte, over the padded vocabulary (pad logits are 0 and
-        // never read by the argmax)
-        gemm(bucket, D, vocab_padded(), d_x, wte, d_logits, vocab_padded());
-        b2_ok(b2_argmax_rows(dt, d_next, d_logits, vocab_padded(), bucket, V, s), "argmax");
+        lm_head_argmax(bucket, d_x, d_logits, d_next);
         copy_error_word_kernel<<<1, 32, 0, stream>>>(d_next + cfg.max_batch, d_err_word);
         cuda_ok(cudaGetLastError(), "copy error word");
+    }
+
+    // Next tokens of `rows` final hidden rows x [rows][D]: the lm_head tied to
+    // wte over the padded vocabulary into `logits` (pad logits are 0 and never
+    // read by the argmax), then the argmax -- or, with lm_fused, both in one
+    // b2_lm_head_argmax launch that writes no logits.
+    void lm_head_argmax(int rows, const void* x, void* logits, int32_t* next) {
+        cudaStream_t s = stream;
+        const int D = shape.d_model, V = shape.vocab_size;
+        if (lm_fused) {
+            B2LmHeadArgmaxArgs la{};
+            la.dtype = dt;
+            la.x = x;
+            la.x_row_stride = D;
+            la.w = wte;
+            la.batch = rows;
+            la.d_model = D;
+            la.vocab = V;
+            la.out_tokens = next;
+            la.workspace = lm_ws;
+            la.workspace_bytes = lm_ws_bytes;
+            b2_ok(b2_lm_head_argmax(&la, s), "lm_head_argmax");
+            return;
+        }
+        gemm(rows, D, vocab_padded(), x, wte, logits, vocab_padded());
+        b2_ok(b2_argmax_rows(dt, next, logits, vocab_padded(), rows, V, s), "argmax");
     }
 
     // After a step's synchronisation: a nonzero device error word (a bounded
@@ -925,8 +953,7 @@ struct Engine {
         gather_rows_kernel<<<std::min(n, 1024), 128, 0, stream>>>(static_cast<uint4*>(p_last),
                                                                   static_cast<const uint4*>(p_x), d_last, n, cols);
         cuda_ok(cudaGetLastError(), "gather last rows");
-        gemm(n, D, vocab_padded(), p_last, wte, p_logits, vocab_padded());
-        b2_ok(b2_argmax_rows(dt, d_pnext, p_logits, vocab_padded(), n, V, s), "argmax");
+        lm_head_argmax(n, p_last, p_logits, d_pnext);
         copy_error_word_kernel<<<1, 32, 0, stream>>>(d_pnext + B, d_err_word);
         cuda_ok(cudaGetLastError(), "copy error word");
         cuda_ok(cudaMemcpyAsync(h_pnext, d_pnext, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, stream),
@@ -1357,6 +1384,23 @@ int b2_engine_set_gemm_mode(b2_engine* eng, int32_t mode) {
         for (auto& g : eng->graphs) cudaGraphExecDestroy(g.second);
         eng->graphs.clear();
         eng->gemm_mode = eng->dt == B2_F32 ? 0 : mode;
+    });
+}
+
+int b2_engine_set_lm_head_fused(b2_engine* eng, int32_t enabled) {
+    if (!eng) return B2_ERR_NULL;
+    return guarded([&] {
+        b2::eng::cuda_ok(cudaSetDevice(eng->device), "cudaSetDevice");
+        b2::eng::cuda_ok(cudaStreamSynchronize(eng->stream), "lm_head switch");
+        for (auto& g : eng->graphs) cudaGraphExecDestroy(g.second);  // captured with the other lm_head
+        eng->graphs.clear();
+        const bool on = enabled != 0 && eng->dt != B2_F32;
+        if (on && eng->lm_ws == nullptr) {
+            eng->lm_ws_bytes = b2_lm_head_argmax_workspace_bytes(eng->cfg.max_batch);
+            b2::eng::cuda_ok(cudaMalloc(&eng->lm_ws, eng->lm_ws_bytes), "malloc lm_head workspace");
+            b2::eng::cuda_ok(cudaMemsetAsync(eng->lm_ws, 0, eng->lm_ws_bytes, eng->stream), "zero lm_head workspace");
+        }
+        eng->lm_fused = on;
     });
 }
 

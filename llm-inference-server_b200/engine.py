@@ -28,7 +28,7 @@ ENGINE_SYMBOLS = (
     "b2_engine_last_error", "b2_block_pool_create", "b2_block_pool_destroy", "b2_block_pool_allocate",
     "b2_block_pool_free", "b2_block_pool_num_free", "b2_engine_tp_handle", "b2_engine_tp_connect",
     "b2_engine_prefill", "b2_engine_tp_nccl_id", "b2_engine_tp_connect_nccl", "b2_engine_set_linear_tensor_cores",
-    "b2_engine_last_step_outputs", "b2_engine_set_gemm_mode",
+    "b2_engine_last_step_outputs", "b2_engine_set_gemm_mode", "b2_engine_set_lm_head_fused",
 )
 
 TP_HANDLE_BYTES = 128
@@ -100,6 +100,7 @@ def load() -> ctypes.CDLL:
     lib.b2_engine_set_linear_tensor_cores.argtypes = [_vp, _i32]
     lib.b2_engine_last_step_outputs.argtypes = [_vp, _i32, _vp, _vp]
     lib.b2_engine_set_gemm_mode.argtypes = [_vp, _i32]
+    lib.b2_engine_set_lm_head_fused.argtypes = [_vp, _i32]
     lib.b2_engine_tp_connect_nccl.argtypes = [_vp, ctypes.c_char_p]
     _lib = lib
     return lib
@@ -220,6 +221,10 @@ class Engine:
     def set_gemm_mode(self, mode: int) -> None:
         """Bit 1: cuBLASLt with timed algorithm choice; bit 2: FC bias + GELU in its epilogue."""
         _check(self._lib.b2_engine_set_gemm_mode(self._handle(), mode))
+
+    def set_lm_head_fused(self, enabled: bool) -> None:
+        """b2_engine_set_lm_head_fused: lm_head GEMM + argmax in one tensor-core launch (f16 / bf16)."""
+        _check(self._lib.b2_engine_set_lm_head_fused(self._handle(), 1 if enabled else 0))
 
     def set_linear_tensor_cores(self, enabled: bool) -> None:
         _check(self._lib.b2_engine_set_linear_tensor_cores(self._handle(), 1 if enabled else 0))

@@ -120,3 +120,34 @@ def test_barrier_limit_is_checked_on_the_host(b2):
     assert lib.b2_tp_barrier_timed(16, 32, 0, 2, 48, 0, 0, None) == -3  # zero limit: B2_ERR_SHAPE, no launch
     assert lib.b2_tp_barrier_timed(16, 32, 0, 2, 48, 0, 61 * 10**9, None) == -3
     assert lib.b2_tp_barrier_timed(16, 32, 2, 2, 48, 0, 10**6, None) == -3  # rank out of range
+
+
+def _lm_args(b2, **kw):
+    base = dict(dtype=b2.BF16, x=16, x_row_stride=1600, w=32, batch=4, d_model=1600, vocab=50257, out_tokens=48,
+                workspace=64, workspace_bytes=1 << 20)
+    base.update(kw)
+    return b2.LmHeadArgmaxArgs(**base)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(dtype=0), -2),  # F32
+    (dict(vocab=0), -3),
+    (dict(x=None), -1),
+    (dict(workspace=None), -1),
+    (dict(x_row_stride=1000), -3),
+    (dict(d_model=1604, x_row_stride=1604), -4),
+    (dict(x=24), -4),
+    (dict(workspace_bytes=16), -5),
+    (dict(workspace=72), -5),
+])
+def test_lm_head_argmax_host_checks(b2, kw, code):
+    lib = b2.load()
+    assert lib.b2_lm_head_argmax(ctypes.byref(_lm_args(b2, **kw)), None) == code
+    assert lib.b2_last_error_string().decode() != ""
+
+
+def test_lm_head_argmax_workspace_size_and_empty_batch(b2):
+    lib = b2.load()
+    assert lib.b2_lm_head_argmax_workspace_bytes(512) >= 16 + 8 * 512
+    assert lib.b2_lm_head_argmax_workspace_bytes(512) % 256 == 0
+    assert lib.b2_lm_head_argmax(ctypes.byref(_lm_args(b2, batch=0, x=None, w=None)), None) == 0

@@ -90,3 +90,56 @@ def test_16bit_engine_matches_oracle_teacher_forced(b2, cuda, models, shape, dt,
     assert worst_h <= HIDDEN_TOL[dt], f"final LayerNorm max-abs {worst_h:.4g} > {HIDDEN_TOL[dt]}"
     assert worst_l <= LOGIT_TOL[dt], f"logits max-abs {worst_l:.4g} > {LOGIT_TOL[dt]}"
     assert checked > 0 and agree == checked
+
+
+@pytest.mark.parametrize("dt", [O.F16, O.BF16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("shape", list(SHAPES))
+def test_fused_lm_head_engine_tokens_match_oracle(b2, cuda, models, shape, dt):
+    """b2_engine_set_lm_head_fused: the tokens decode_step and prefill return
+    (now from b2_lm_head_argmax, no logits formed) equal the oracle's greedy
+    choice at every position where the oracle's top-2 margin exceeds
+    2 * LOGIT_TOL, and the unfused engine's tokens wherever its own logits'
+    top two are more than two ulps apart."""
+    from lis_b200 import engine as E
+    d, cfg, tensors = models[shape]
+    rng = np.random.Generator(np.random.PCG64(11 + len(shape)))
+    streams = [rng.integers(0, cfg["vocab_size"], size=T).tolist() for _ in range(STREAMS)]
+    toks, logits = {}, None
+    for fused in (False, True):
+        eng = E.Engine()
+        assert eng.init(str(d), E.Config(max_batch=STREAMS, max_seq_len=256, kv_block_budget=64, dtype=dt, device=0))
+        eng.set_lm_head_fused(fused)
+        ids = [eng.add_sequence(s) for s in streams]
+        out = np.empty((T, STREAMS), np.int64)
+        lg = np.empty((T, STREAMS, cfg["vocab_size"]), np.float32)
+        for t in range(T):
+            out[t] = eng.decode_step(ids)
+            if not fused:
+                lg[t] = O.widen(dt, eng.last_step_outputs(STREAMS)[1])
+        toks[fused] = out
+        if not fused:
+            logits = lg
+        # the same prompts through the batched prefill: each stream's first token
+        eng2 = E.Engine()
+        assert eng2.init(str(d), E.Config(max_batch=STREAMS, max_seq_len=256, kv_block_budget=64, dtype=dt, device=0))
+        eng2.set_lm_head_fused(fused)
+        toks[("prefill", fused)] = eng2.prefill([eng2.add_sequence(s) for s in streams])
+        eng2.close()
+        eng.close()
+    ref_t = _rounded(dt, tensors)
+    checked = 0
+    mant = 7 if dt == O.BF16 else 10
+    for i, s in enumerate(streams):
+        _, rl = gpt2.teacher_forced(cfg, ref_t, s, nthreads=8)
+        top2 = np.sort(rl, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 2 * LOGIT_TOL[dt]
+        want = np.argmax(rl, axis=1)
+        assert np.array_equal(toks[True][clear, i], want[clear]), f"stream {i}: fused tokens differ from the oracle"
+        checked += int(clear.sum())
+        if clear[-1]:
+            assert toks[("prefill", True)][i] == want[-1], f"stream {i}: fused prefill token differs from the oracle"
+        u2 = np.sort(logits[:, i], axis=1)[:, -2:]
+        ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(u2[:, 1]), 2.0 ** -14))) - mant)
+        apart = (u2[:, 1] - u2[:, 0]) > 2 * ulp
+        assert np.array_equal(toks[True][apart, i], toks[False][apart, i]), f"stream {i}: fused vs unfused engine"
+    assert checked > T
