@@ -8,26 +8,32 @@
 // fp32 logits (reference/cpu_model.cpp:182-196).  Here the logits never
 // leave the chip:
 //
-//   * work items of (128-row vocabulary tile, chunk of <= 256 batch rows):
-//     swapped operands as in linear_tc.cuh -- MMA M = 128 vocabulary rows,
-//     N = the batch chunk, K in 64-element SWIZZLE_128B TMA boxes -- with the
-//     fp32 logits tile in TMEM.  Whole K per item: a max does not distribute
-//     over partial sums, so there is no split-K;
+//   * work items of (VN <= 256 vocabulary rows, 128 batch rows): MMA M = the
+//     batch rows (zero rows past the batch), N = VN vocabulary rows, K in
+//     64-element SWIZZLE_128B TMA boxes, the fp32 logits tile D[batch][vocab]
+//     in TMEM.  Weights on the N side: each tcgen05.mma instruction takes in
+//     up to 8 KB of weight rows.  (With the weights as M = 128, the operand
+//     order of linear_tc.cuh, per-CTA stamps showed ~0.5 us per 64-element K
+//     block whatever the batch -- 16 or 256 columns -- so the instruction
+//     count per weight byte, not the arithmetic, paced the stream.)  Whole K
+//     per item: a max does not distribute over partial sums;
+//   * VN is sized so the items spread evenly over the SMs (GPT-2's 50257 rows
+//     at batch <= 128: 176 rows, 286 items, two per SM at most; 256-row items
+//     left a third of the SMs with twice the weights of the rest);
 //   * persistent: one CTA per SM walks its items (blockIdx.x, + grid, ...)
-//     with one ring running across item boundaries, and two TMEM
-//     accumulators, so the argmax epilogue of one item overlaps the MMAs of
-//     the next (a grid of one CTA per item left a third of the GPT-2
-//     vocabulary's 393 tiles to a lone second wave);
+//     with one ring running across item boundaries and two TMEM
+//     accumulators, so the argmax of one item overlaps the MMAs of the next;
 //   * the weight rows stream before griddepcontrol.wait (the tied embedding
 //     never depends on the previous kernel), x after it;
-//   * epilogue: each logit is rounded to T exactly as the unfused path stores
-//     it, and packed into a 32-bit key (order-preserving 16-bit image of the
-//     T value, then 0xFFFF - row) so that the larger key is the larger logit
-//     and, among equal logits, the lower row.  A warp reduces the keys of its
-//     32 rows for 32 batch columns at once by a shuffle transpose (31
-//     exchanges), the four epilogue warps meet in shared memory, and one
-//     64-bit atomic max per batch row -- (order-preserving image of the
-//     value, 0xFFFFFFFF - vocabulary index) -- merges the CTAs;
+//   * epilogue: a thread owns one batch row (its TMEM lane) and every other
+//     group of 32 of the item's columns.  Each logit is rounded to T exactly
+//     as the unfused path stores it and packed into a 32-bit key
+//     (order-preserving 16-bit image of the T value, then 0xFFFF - column) so
+//     that the larger key is the larger logit and, among equal logits, the
+//     lower index; the thread keeps the largest, the two warps of a lane
+//     quadrant meet in shared memory, and one 64-bit atomic max per batch row
+//     -- (order-preserving image of the value, 0xFFFFFFFF - vocabulary index)
+//     -- merges the CTAs;
 //   * the last CTA to finish (an acquire-release counter) turns the keys
 //     into tokens and leaves keys and counter at zero for the next launch.
 //
@@ -43,43 +49,41 @@
 
 namespace b2 {
 
-constexpr int kLmRows = 128;                       // vocabulary rows per CTA (MMA M)
-constexpr int kLmKBlock = 64;                      // K elements per stage (one 128-B swizzle row)
-constexpr int kLmWBytes = kLmRows * kLmKBlock * 2;  // weight box: 16 KiB
-constexpr int kLmEpiWarps = 8;  // two per TMEM lane quadrant, each taking alternate column groups
+constexpr int kLmMaxVRows = 256;  // vocabulary rows per work item at most (MMA N)
+constexpr int kLmBRows = 128;     // batch rows per work item (MMA M)
+constexpr int kLmKBlock = 64;     // K elements per stage (one 128-B swizzle row)
+constexpr int kLmXBytes = kLmBRows * kLmKBlock * 2;  // x box: 16 KiB
+constexpr int kLmEpiWarps = 8;  // two per TMEM lane quadrant, taking alternate groups of 32 columns
 constexpr int kLmThreads = 64 + 32 * kLmEpiWarps;
-constexpr int kLmMaxCols = 256;  // batch rows per CTA (MMA N limit)
+constexpr uint32_t kLmAccCols = kLmMaxVRows;  // TMEM columns per accumulator; the kernel holds two
 
 struct LmParams {
     int batch, vocab;
-    int bn;        // batch rows per work item: multiple of 16, <= 256
-    int kb_total;  // 64-element K blocks
-    int stages;    // ring slots
+    int vn;               // vocabulary rows per work item: a multiple of 16, 16 .. 256 (the MMA's N)
+    int kb_total;         // 64-element K blocks
+    int stages;           // ring slots
     int n_tiles, chunks;  // work item w: vocabulary tile w / chunks, batch chunk w % chunks
     unsigned long long* keys;  // [batch] best keys so far; zero between launches
     unsigned int* counter;     // CTAs finished; zero between launches
     int* tokens;               // [batch]
 };
 
-// Shared-memory plan (bytes from the 1024-aligned base): the ring, the
-// epilogue warps' keys [4][bn], the last-CTA flag, the barriers (ring
-// full/empty, two accumulator full/empty pairs), the TMEM slot.
+// Shared-memory plan (bytes from the 1024-aligned base): the ring of
+// [weights | x] stages, the two column halves' keys [2][128], the last-CTA
+// flag, the barriers (ring full/empty, two accumulator full/empty pairs),
+// the TMEM slot.
 struct LmLayout {
-    __host__ __device__ static constexpr int stage_bytes(int bn) { return kLmWBytes + bn * 128; }
-    __host__ __device__ static constexpr int off_red(int bn, int stages) { return stages * stage_bytes(bn); }
-    __host__ __device__ static constexpr int off_flag(int bn, int stages) { return off_red(bn, stages) + 16 * bn; }
-    __host__ __device__ static constexpr int off_bars(int bn, int stages) { return off_flag(bn, stages) + 16; }
-    __host__ __device__ static constexpr int off_tmem(int bn, int stages) {
-        return off_bars(bn, stages) + 8 * (2 * stages + 4);
+    // a stage: vn weight rows of 128 bytes (vn a multiple of 16, so 1 KiB-aligned), then the x box
+    __host__ __device__ static constexpr int w_bytes(int vn) { return vn * kLmKBlock * 2; }
+    __host__ __device__ static constexpr int stage_bytes(int vn) { return w_bytes(vn) + kLmXBytes; }
+    __host__ __device__ static constexpr int off_red(int vn, int stages) { return stages * stage_bytes(vn); }
+    __host__ __device__ static constexpr int off_flag(int vn, int stages) { return off_red(vn, stages) + 2 * kLmBRows * 4; }
+    __host__ __device__ static constexpr int off_bars(int vn, int stages) { return off_flag(vn, stages) + 16; }
+    __host__ __device__ static constexpr int off_tmem(int vn, int stages) {
+        return off_bars(vn, stages) + 8 * (2 * stages + 4);
     }
-    __host__ __device__ static constexpr int bytes(int bn, int stages) { return off_tmem(bn, stages) + 16 + 1024; }
+    __host__ __device__ static constexpr int bytes(int vn, int stages) { return off_tmem(vn, stages) + 16 + 1024; }
 };
-
-// Columns of one accumulator (bn fp32 columns, rounded to an allocation
-// size); the kernel holds two.
-__host__ __device__ constexpr uint32_t lm_acc_cols(int bn) {
-    return bn <= 32 ? 32u : (bn <= 64 ? 64u : (bn <= 128 ? 128u : 256u));
-}
 
 // Order-preserving 16-bit image of an f16 / bf16 value: a larger image is a
 // larger value; -0 maps like +0; NaN maps to 0, below every number.
@@ -123,24 +127,6 @@ __device__ __forceinline__ uint32_t lm_key(float v, uint32_t rowkey, bool valid)
     return valid && !nan ? (o << 16) | rowkey : 0u;
 }
 
-// Lane l ends up with the maximum over the warp's 32 lanes of k[l]: five
-// exchange steps, each halving the columns a lane holds (31 shuffles).
-__device__ __forceinline__ uint32_t warp_transpose_max32(uint32_t (&k)[32]) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int w = 16; w >= 1; w >>= 1) {
-        const bool hi = (lane & w) != 0;
-#pragma unroll
-        for (int j = 0; j < w; ++j) {
-            const uint32_t send = hi ? k[j] : k[j + w];
-            const uint32_t keep = hi ? k[j + w] : k[j];
-            const uint32_t got = __shfl_xor_sync(0xffffffffu, send, w);
-            k[j] = keep > got ? keep : got;
-        }
-    }
-    return k[0];
-}
-
 template <typename T>
 __global__ void __launch_bounds__(kLmThreads, 1)
     lm_head_argmax_kernel(const LmParams p, const __grid_constant__ CUtensorMap w_map,
@@ -152,8 +138,9 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     const int lane = tid & 31;
     const int nkb = p.kb_total;
     const int ST = p.stages;
-    const int SB = LmLayout::stage_bytes(p.bn);
-    const uint32_t acc_cols = lm_acc_cols(p.bn);
+    const int VN = p.vn;
+    const int SBY = LmLayout::stage_bytes(VN);
+    const int WBY = LmLayout::w_bytes(VN);
     const int n_items = p.n_tiles * p.chunks;
     const int G = static_cast<int>(gridDim.x);
     // this CTA's work items: blockIdx.x, + G, ... (CTAs next to each other
@@ -162,13 +149,13 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     const int my_items = (n_items - static_cast<int>(blockIdx.x) + G - 1) / G;
     const int total = my_items * nkb;  // K blocks through the ring
 
-    uint32_t* red = reinterpret_cast<uint32_t*>(smem + LmLayout::off_red(p.bn, ST));  // [4][bn]
-    int* last_flag = reinterpret_cast<int*>(smem + LmLayout::off_flag(p.bn, ST));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + LmLayout::off_bars(p.bn, ST));
+    uint32_t* red = reinterpret_cast<uint32_t*>(smem + LmLayout::off_red(VN, ST));  // [2 halves][128 rows]
+    int* last_flag = reinterpret_cast<int*>(smem + LmLayout::off_flag(VN, ST));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + LmLayout::off_bars(VN, ST));
     uint64_t* empty = full + ST;
-    uint64_t* acc_full = empty + ST;   // [2] MMA -> epilogue
+    uint64_t* acc_full = empty + ST;     // [2] MMA -> epilogue
     uint64_t* acc_empty = acc_full + 2;  // [2] epilogue (every epilogue warp) -> MMA
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LmLayout::off_tmem(p.bn, ST));
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LmLayout::off_tmem(VN, ST));
 
     if (tid == 0) {
         for (int s = 0; s < ST; ++s) {
@@ -183,7 +170,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 2 * acc_cols);
+        tmem_alloc(tmem_slot, 2 * kLmAccCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -200,13 +187,13 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             const int npre = min(total, ST);
             for (int i = 0; i < npre; ++i) {
                 const int w = static_cast<int>(blockIdx.x) + (i / nkb) * G;
-                mbar_arrive_expect_tx(&full[i], static_cast<uint32_t>(SB));
-                tma_load_2d(smem + i * SB, &w_map, (i % nkb) * kLmKBlock, (w / p.chunks) * kLmRows, &full[i]);
+                mbar_arrive_expect_tx(&full[i], static_cast<uint32_t>(SBY));
+                tma_load_2d(smem + i * SBY, &w_map, (i % nkb) * kLmKBlock, (w / p.chunks) * VN, &full[i]);
             }
             pdl_wait();  // x is the previous kernel's output
             for (int i = 0; i < npre; ++i) {
                 const int w = static_cast<int>(blockIdx.x) + (i / nkb) * G;
-                tma_load_2d(smem + i * SB + kLmWBytes, &x_map, (i % nkb) * kLmKBlock, (w % p.chunks) * p.bn,
+                tma_load_2d(smem + i * SBY + WBY, &x_map, (i % nkb) * kLmKBlock, (w % p.chunks) * kLmBRows,
                             &full[i]);
             }
             issued = npre;
@@ -218,15 +205,15 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 }
                 const int w = static_cast<int>(blockIdx.x) + (i / nkb) * G;
                 const int kc = (i % nkb) * kLmKBlock;
-                mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(SB));
-                tma_load_2d(smem + s * SB, &w_map, kc, (w / p.chunks) * kLmRows, &full[s]);
-                tma_load_2d(smem + s * SB + kLmWBytes, &x_map, kc, (w % p.chunks) * p.bn, &full[s]);
+                mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(SBY));
+                tma_load_2d(smem + s * SBY, &w_map, kc, (w / p.chunks) * VN, &full[s]);
+                tma_load_2d(smem + s * SBY + WBY, &x_map, kc, (w % p.chunks) * kLmBRows, &full[s]);
                 issued = i + 1;
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc<T>(kLmRows, p.bn, false, false);
+            const uint32_t idesc = umma_idesc<T>(kLmBRows, VN, false, false);
             for (int i = 0; i < total; ++i) {
                 const int j = i / nkb, kb = i - j * nkb;
                 const int buf = j & 1;
@@ -243,72 +230,65 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a = smem_addr(smem + s * SB);
-                const uint32_t b = a + kLmWBytes;
-                const uint32_t d = tmem + static_cast<uint32_t>(buf) * acc_cols;
+                const uint32_t bw = smem_addr(smem + s * SBY);        // B: VN weight rows
+                const uint32_t ax = bw + static_cast<uint32_t>(WBY);  // A: 128 batch rows
+                const uint32_t d = tmem + static_cast<uint32_t>(buf) * kLmAccCols;
 #pragma unroll
                 for (int k = 0; k < kLmKBlock / 16; ++k)
-                    umma_f16(d, sw128_desc(a + 32 * k, 16, 1024), sw128_desc(b + 32 * k, 16, 1024), idesc,
+                    umma_f16(d, sw128_desc(ax + 32 * k, 16, 1024), sw128_desc(bw + 32 * k, 16, 1024), idesc,
                              (kb | k) != 0);
                 umma_commit(&empty[s]);  // the slot is free once these MMAs have read it
                 if (kb == nkb - 1) umma_commit(&acc_full[buf]);
             }
         }
     } else {
-        // ---- epilogue warps: TMEM lane quadrant q holds vocabulary rows n0 + 32q ...;
-        // the two warps of a quadrant take alternate groups of CW columns
+        // ---- epilogue warps: TMEM lane quadrant q holds batch rows b0 + 32q ...;
+        // the two warps of a quadrant take alternate groups of 32 of the VN columns
         const int q = warp & 3;
         const int half = (warp - 2) >> 2;
-        const int row = q * 32 + lane;  // this thread's vocabulary row in a tile
+        const int row = q * 32 + lane;  // this thread's batch row in the item
         const int t = tid - 64;
-        const int CW = acc_cols >= 64u ? 64 : 32;  // columns per TMEM load (never past the allocation)
         bool ok = true;
         for (int j = 0; j < my_items && ok; ++j) {
             const int w = static_cast<int>(blockIdx.x) + j * G;
-            const int n0 = (w / p.chunks) * kLmRows;
-            const int b0 = (w % p.chunks) * p.bn;
+            const int n0 = (w / p.chunks) * VN;
+            const int b0 = (w % p.chunks) * kLmBRows;
             const int buf = j & 1;
             ok = mbar_wait_bounded(&acc_full[buf], static_cast<uint32_t>(j >> 1) & 1u);
             if (!ok && lane == 0) flag_error(B2_DEVERR_TIMEOUT);
             __syncwarp();
             tc_fence_after();
-            const bool valid = n0 + row < p.vocab && ok;
-            const uint32_t rowkey = static_cast<uint32_t>(0xFFFF - row);
-            const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf) * acc_cols;
+            const uint32_t taddr =
+                tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf) * kLmAccCols;
+            uint32_t best = 0u;
 #pragma unroll 1
-            for (int c = half * CW; c < p.bn; c += 2 * CW) {
-                float v[64];
-                if (CW == 64)
-                    tmem_ld64(taddr + static_cast<uint32_t>(c), v);
-                else
-                    tmem_ld32(taddr + static_cast<uint32_t>(c), v);
+            for (int c = half * 32; c < VN; c += 64) {  // columns past VN: allocated, never counted
+                float v[32];
+                tmem_ld32(taddr + static_cast<uint32_t>(c), v);
 #pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    if (g * 32 < CW) {
-                        uint32_t k[32];
-#pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) k[jj] = lm_key<T>(v[g * 32 + jj], rowkey, valid);
-                        const uint32_t best = warp_transpose_max32(k);  // column c + 32g + lane over 32 rows
-                        if (c + g * 32 + lane < p.bn) red[q * p.bn + c + g * 32 + lane] = best;
-                    }
+                for (int jj = 0; jj < 32; ++jj) {
+                    const int col = c + jj;  // vocabulary row n0 + col
+                    const uint32_t key =
+                        lm_key<T>(v[jj], static_cast<uint32_t>(0xFFFF - col), ok && col < VN && n0 + col < p.vocab);
+                    best = key > best ? key : best;
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);  // the MMAs may overwrite this accumulator
+            red[half * kLmBRows + row] = best;
             named_sync(1, kLmThreads - 64);
             if (j == 0) pdl_wait();  // the keys of the launch before this one are cleared by its last CTA
-            for (int col = t; col < p.bn; col += kLmThreads - 64) {
-                uint32_t best = red[col];
-#pragma unroll
-                for (int ww = 1; ww < 4; ++ww) best = max(best, red[ww * p.bn + col]);
-                if (best != 0u && b0 + col < p.batch) {
-                    const uint32_t o = best >> 16;
-                    const int n = n0 + static_cast<int>(0xFFFFu - (best & 0xFFFFu));
+            if (t < kLmBRows) {
+                const uint32_t k0 = red[t], k1 = red[kLmBRows + t];
+                const uint32_t k = k0 > k1 ? k0 : k1;
+                if (k != 0u && b0 + t < p.batch) {
+                    const uint32_t o = k >> 16;
+                    const int n = n0 + static_cast<int>(0xFFFFu - (k & 0xFFFFu));
                     const uint32_t hi = o == 0u ? 0u : lm_ord32(lm_from_ord16<T>(o));
                     const unsigned long long key = (static_cast<unsigned long long>(hi) << 32) |
                                                    static_cast<unsigned long long>(0xFFFFFFFFu - n);
-                    atomicMax(p.keys + b0 + col, key);
+                    atomicMax(p.keys + b0 + t, key);
                 }
             }
             named_sync(1, kLmThreads - 64);  // red is rewritten by the next item
@@ -348,7 +328,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, 2 * acc_cols);
+    if (warp == 1) tmem_dealloc(tmem, 2 * kLmAccCols);
 }
 
 }  // namespace b2
