@@ -1322,12 +1322,15 @@ int lm_head_t(const B2LmHeadArgmaxArgs* a, cudaStream_t stream) {
     CUtensorMap wm, xm;
     rc = encode_rows_map(&wm, a->dtype, a->w, a->d_model, a->vocab, a->d_model, pl.vn);
     if (rc != B2_OK) return rc;
-    rc = encode_rows_map(&xm, a->dtype, a->x, a->d_model, a->batch, a->x_row_stride, kLmBRows);
+    // x boxes of the batch's rows (rounded to 16) while one batch chunk holds them all
+    const int xrows = pl.chunks > 1 ? kLmBRows : std::max(16, (a->batch + 15) / 16 * 16);
+    rc = encode_rows_map(&xm, a->dtype, a->x, a->d_model, a->batch, a->x_row_stride, xrows);
     if (rc != B2_OK) return rc;
     LmParams lp;
     lp.batch = a->batch;
     lp.vocab = a->vocab;
     lp.vn = pl.vn;
+    lp.xrows = xrows;
     lp.kb_total = pl.kb_total;
     lp.stages = pl.stages;
     lp.n_tiles = pl.n_tiles;

@@ -60,6 +60,8 @@ constexpr uint32_t kLmAccCols = kLmMaxVRows;  // TMEM columns per accumulator; t
 struct LmParams {
     int batch, vocab;
     int vn;               // vocabulary rows per work item: a multiple of 16, 16 .. 256 (the MMA's N)
+    int xrows;            // x rows each stage loads: the batch rounded up to 16 (at most 128); the
+                          // A tile's rows past them hold stale bytes and feed only unused result rows
     int kb_total;         // 64-element K blocks
     int stages;           // ring slots
     int n_tiles, chunks;  // work item w: vocabulary tile w / chunks, batch chunk w % chunks
@@ -141,6 +143,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     const int VN = p.vn;
     const int SBY = LmLayout::stage_bytes(VN);
     const int WBY = LmLayout::w_bytes(VN);
+    const uint32_t TX = static_cast<uint32_t>(WBY + p.xrows * kLmKBlock * 2);  // bytes a stage receives
     const int n_items = p.n_tiles * p.chunks;
     const int G = static_cast<int>(gridDim.x);
     // this CTA's work items: blockIdx.x, + G, ... (CTAs next to each other
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             const int npre = min(total, ST);
             for (int i = 0; i < npre; ++i) {
                 const int w = static_cast<int>(blockIdx.x) + (i / nkb) * G;
-                mbar_arrive_expect_tx(&full[i], static_cast<uint32_t>(SBY));
+                mbar_arrive_expect_tx(&full[i], TX);
                 tma_load_2d(smem + i * SBY, &w_map, (i % nkb) * kLmKBlock, (w / p.chunks) * VN, &full[i]);
             }
             pdl_wait();  // x is the previous kernel's output
@@ -205,7 +208,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 }
                 const int w = static_cast<int>(blockIdx.x) + (i / nkb) * G;
                 const int kc = (i % nkb) * kLmKBlock;
-                mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(SBY));
+                mbar_arrive_expect_tx(&full[s], TX);
                 tma_load_2d(smem + s * SBY, &w_map, kc, (w / p.chunks) * VN, &full[s]);
                 tma_load_2d(smem + s * SBY + WBY, &x_map, kc, (w % p.chunks) * kLmBRows, &full[s]);
                 issued = i + 1;
