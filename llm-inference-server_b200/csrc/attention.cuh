@@ -28,15 +28,16 @@
 //  * Merge.  At a segment's end the token subgroups' (m, l, acc) go to the
 //    workspace -- one slot per subgroup, or, where the planner folds pieces
 //    (one CTA per SM), one slot per piece after a fold in shared memory -- and
-//    the piece goes to the CTA's bookkeeping warp, which counts it on the
-//    sequence's counter with one acquire-release atomic.  The CTA that
-//    completes the count merges the sequence's slots (max-rescaled sums, in
-//    slot order, so the bits do not depend on which CTA merges) and writes
-//    the output in the output dtype: the bookkeeping warp for pieces in the
-//    middle of the CTA's range, all softmax threads for the final piece,
-//    which is on the kernel's tail.  A sequence that lies in one CTA is
-//    folded in shared memory and written out directly.  One kernel per call;
-//    the counters are left at zero for the next launch.
+//    the piece goes to the CTA's bookkeeping warp.  The CTA holding a
+//    sequence's last piece (its own first piece) merges the sequence at its
+//    end; every other piece is published with one fire-and-forget release-add
+//    on the sequence's counter, so those CTAs never wait for an answer.  The
+//    merging CTA's bookkeeping warp waits (bounded, acquire loads) for the
+//    count, then all its softmax threads merge the slots (max-rescaled sums,
+//    in slot order) and write the output in the output dtype.  A sequence
+//    that lies in one CTA is folded in shared memory and written out
+//    directly.  One kernel per call; the counters are left at zero for the
+//    next launch.
 //
 // Every wait is bounded (b2_common.cuh): on timeout the CTA flags
 // B2_DEVERR_TIMEOUT, drains its own copies in flight and returns.
@@ -243,13 +244,24 @@ __device__ __forceinline__ void merge_partials(const float2* part_ml, const floa
     }
 }
 
-// Counts one finished piece of a sequence: release (publishes the partials
-// this CTA wrote before it) and acquire (the other pieces' partials are
-// visible after it) at GPU scope.  Returns the previous count.
-__device__ __forceinline__ unsigned count_piece(unsigned* counter) {
-    unsigned old;
-    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
-    return old;
+// Publishes one finished piece of a sequence: a release at GPU scope (the
+// partials this CTA wrote before it are visible to whoever acquires the
+// count), fire and forget.
+__device__ __forceinline__ void publish_piece(unsigned* counter) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+}
+
+// Waits (bounded, 1 s of %globaltimer) until *counter reaches `target`, with
+// acquire loads: the partials published before each count are visible after
+// it.  Returns false if the limit passed first.
+__device__ __forceinline__ bool wait_count(const unsigned* counter, unsigned target) {
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 0;; ++it) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+        if (v >= target) return true;
+        if ((it & 15u) == 15u && global_timer_ns() - t0 > kWaitLimitNs) return false;
+    }
 }
 
 // Before griddepcontrol.wait, when the inputs may still be written by the
@@ -585,13 +597,15 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
 
     if (warp == ncw + 1) {
         // ============================================== bookkeeping warp
-        // For each finished piece: publish it (fence, then count it on the
-        // sequence's counter); the CTA whose count completes the sequence
-        // merges it -- here, one warp, while the softmax warps stream on,
-        // except for this CTA's final piece, whose merge is left to the
-        // softmax threads once they are done (it is on the kernel's tail).
+        // For each finished piece of a sequence spread over several CTAs:
+        // the CTA holding the sequence's last piece (always that CTA's first
+        // piece) merges the sequence at its end; every other piece is
+        // published with one release-add on the sequence's counter and needs
+        // no answer, so its CTA leaves as soon as its own work is done (a
+        // last-arriver merge made every CTA wait for its count's round trip).
         const int lane = tid & 31;
         bool ok = true;
+        int mb = -1, mi0 = 0, mn = 0;  // the sequence this CTA merges at its end
         for (int k = 0; ok; ++k) {
             const int rk = k % R;
             ok = mbar_wait_bounded(&piece_full[rk], static_cast<uint32_t>(k / R) & 1u);
@@ -616,27 +630,32 @@ __global__ void __launch_bounds__(MAXT, 1) paged_decode_kernel(const AttnParams 
                 __threadfence();
                 __syncwarp();
             }
-            int last = 0;  // pc.z == 0: the piece was merged by the softmax threads (one-piece sequence)
-            if (lane == 0 && pc.z > 0)
-                last = count_piece(p.counters + pc.x) == static_cast<unsigned>(pc.z - 1) ? 1 : 0;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-                if (pc.w & 1) {
-                    if (lane == 0) {
-                        final_merge[0] = 1;
-                        final_merge[1] = pc.x;
-                        final_merge[2] = pc.y;
-                        final_merge[3] = pc.z;
-                    }
-                } else {
-                    merge_partials<DH, E, 1, OutT>(p.part_ml, p.part_acc, p.out, H, p.fold_pieces ? 1 : p.ksplit,
-                                                   pc.x, pc.y, pc.z, lane, 32);
-                    if (lane == 0) p.counters[pc.x] = 0u;  // every launch leaves the counters at zero
+            // pc.z == 0: a one-piece sequence, merged by the softmax threads
+            if (pc.z > 0) {
+                if (cta == pc.y + pc.z - 1) {
+                    mb = pc.x;
+                    mi0 = pc.y;
+                    mn = pc.z;
+                } else if (lane == 0) {
+                    publish_piece(p.counters + pc.x);
                 }
             }
             if (pc.w & 1) break;
         }
         if (!ok && lane == 0) flag_error(B2_DEVERR_TIMEOUT);
+        if (ok && mb >= 0 && lane == 0) {
+            // Wait (bounded) for the sequence's other pieces; the acquire
+            // orders their partials before the softmax threads' merge (through
+            // book_done below).
+            if (wait_count(p.counters + mb, static_cast<unsigned>(mn - 1))) {
+                final_merge[0] = 1;
+                final_merge[1] = mb;
+                final_merge[2] = mi0;
+                final_merge[3] = mn;
+            } else {
+                flag_error(B2_DEVERR_TIMEOUT);
+            }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(book_done);  // also on failure: nobody waits on a dead warp
         return;
