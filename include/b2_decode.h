@@ -194,13 +194,18 @@ B2_API int b2_paged_attention(const B2PagedAttnArgs* args, void* workspace, size
  * Engine::decode_step (gpu-engine/src/engine.cu:343-368): upload the step's
  * inputs with cudaMemcpyAsync, launch, download the output, synchronise.
  *
- * Copies io->q, io->block_tables and io->seq_lens (each optional: NULL skips
- * that upload) into args->q, args->block_tables and args->seq_lens, runs
+ * Uploads io->q, io->block_tables and io->seq_lens (each optional: NULL
+ * skips that upload) into args->q, args->block_tables and args->seq_lens, runs
  * b2_paged_attention on `stream`, copies args->out into io->out (optional),
- * and waits for the stream.  Uploads whose host AND device ranges are both
- * back to back (q, then block tables, then seq_lens at the same offsets in one
- * host and one device allocation) go as one copy.  Host buffers should be
- * pinned (page-locked); pageable memory works but copies synchronously.
+ * and waits for the stream.  When every given host input is page-locked
+ * memory mapped into the device's address space (cudaHostAlloc /
+ * cudaHostRegister memory on a unified-addressing system), one small kernel
+ * reads them over the bus and stores them into the device arrays -- no
+ * copy-engine set-up on the call's path -- and the attention launch waits for
+ * it whatever args->flags says.  Otherwise the uploads are copies, and those
+ * whose host AND device ranges are both back to back (q, then block tables,
+ * then seq_lens at the same offsets in one host and one device allocation) go
+ * as one copy; pageable memory works but copies synchronously.
  * When io->out is page-locked memory mapped into the device's address space
  * (cudaHostAlloc / cudaHostRegister memory on a unified-addressing system)
  * and 16-byte aligned, the kernel stores the output into it directly (the

@@ -338,6 +338,12 @@ int plan_attention(const B2PagedAttnArgs* a, AttnPlan* pl) {
     return B2_OK;
 }
 
+// Set while b2_paged_attention_host launches an early-start attention
+// (B2_ATTN_INPUTS_READY / B2_ATTN_NEWEST_ROW_PENDING) behind the kernel that
+// writes its inputs: that launch must then start only once the kernel before
+// it has completed, so launch_pdl leaves the programmatic attribute off.
+thread_local bool t_full_dependency = false;
+
 // Launch with programmatic dependent launch: the kernel waits on
 // griddepcontrol.wait before reading what the kernel before it wrote, so its
 // launch and set-up overlap that kernel's tail.
@@ -352,7 +358,7 @@ int launch_pdl(K kern, dim3 grid, dim3 block, int smem, cudaStream_t stream, con
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = t_full_dependency ? 0 : 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm...);
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -706,6 +712,57 @@ cudaError_t wait_stream_polling(cudaStream_t s) {
 }
 }  // namespace
 
+namespace b2 {
+// The uploads of one b2_paged_attention_host call when every host buffer is
+// page-locked and mapped: pieces of 16-byte units (both sides 16-byte
+// aligned) or of single bytes, walked as one index space.
+constexpr int kMaxHostPieces = 6;
+struct HostPieces {
+    char* dst[kMaxHostPieces];
+    const char* src[kMaxHostPieces];  // device addresses of the mapped host pages
+    unsigned long long units[kMaxHostPieces];
+    int wide[kMaxHostPieces];  // 16-byte units (1) or bytes (0)
+    int n;
+    unsigned long long total;
+};
+
+// Reads the call's inputs straight out of mapped host memory over the bus and
+// stores them where the attention launch reads them: the loads of the whole
+// upload are in flight at once (one unit per thread at the sizes a decode
+// step uploads), with no copy-engine set-up on the call's critical path.
+// ld.global.cv fetches every line again, so a host buffer refilled between
+// calls is never served from a cached copy.  The attention launch after it
+// may start (griddepcontrol) and waits for this grid before reading.
+__global__ void __launch_bounds__(256) pull_host_inputs_kernel(HostPieces g) {
+    pdl_launch_dependents();
+    const unsigned long long nth = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+    for (unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < g.total;
+         i += nth) {
+        int s = 0;
+        unsigned long long k = i;
+        while (s + 1 < g.n && k >= g.units[s]) k -= g.units[s++];
+        if (g.wide[s])
+            reinterpret_cast<uint4*>(g.dst[s])[k] = __ldcv(reinterpret_cast<const uint4*>(g.src[s]) + k);
+        else
+            reinterpret_cast<unsigned char*>(g.dst[s])[k] = __ldcv(reinterpret_cast<const unsigned char*>(g.src[s]) + k);
+    }
+}
+}  // namespace b2
+
+namespace {
+
+// The device address of page-locked host memory mapped into the device's
+// address space, or nullptr (pageable memory, device memory, failure).
+const char* mapped_host_address(const void* h) {
+    cudaPointerAttributes pa;
+    const char* d = nullptr;
+    if (cudaPointerGetAttributes(&pa, h) == cudaSuccess && pa.type == cudaMemoryTypeHost)
+        d = static_cast<const char*>(pa.devicePointer);
+    cudaGetLastError();
+    return d;
+}
+}  // namespace
+
 int b2_paged_attention_host(const B2PagedAttnArgs* a, const B2AttnHostIO* io, void* ws, size_t ws_bytes,
                             b2_stream_t stream) {
     using namespace b2;
@@ -731,14 +788,46 @@ int b2_paged_attention_host(const B2PagedAttnArgs* a, const B2AttnHostIO* io, vo
             up[n++] = {reinterpret_cast<char*>(const_cast<int32_t*>(a->seq_lens)),
                        reinterpret_cast<const char*>(io->seq_lens), static_cast<size_t>(a->batch) * sizeof(int32_t)};
     }
-    // One copy per run of uploads that are contiguous on both sides.
-    for (int i = 0; i < n;) {
-        Up c = up[i++];
-        while (i < n && up[i].dst == c.dst + c.bytes && up[i].src == c.src + c.bytes) c.bytes += up[i++].bytes;
-        const cudaError_t e = cudaMemcpyAsync(c.dst, c.src, c.bytes, cudaMemcpyHostToDevice, s);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            return fail(static_cast<int>(e), cudaGetErrorString(e));
+    // Every upload from mapped page-locked memory: one small kernel reads them
+    // all over the bus (pull_host_inputs_kernel).  Otherwise one copy per run
+    // of uploads that are contiguous on both sides.
+    const char* mapped_src[3] = {nullptr, nullptr, nullptr};
+    bool pull = n > 0;
+    for (int i = 0; i < n && pull; ++i) pull = (mapped_src[i] = mapped_host_address(up[i].src)) != nullptr;
+    if (pull) {
+        HostPieces g{};
+        for (int i = 0; i < n; ++i) {
+            size_t head = 0;
+            if (aligned16(up[i].dst) && aligned16(mapped_src[i]) && up[i].bytes >= 16) {
+                head = up[i].bytes & ~static_cast<size_t>(15);
+                g.dst[g.n] = up[i].dst;
+                g.src[g.n] = mapped_src[i];
+                g.units[g.n] = head / 16;
+                g.wide[g.n++] = 1;
+            }
+            if (up[i].bytes > head) {
+                g.dst[g.n] = up[i].dst + head;
+                g.src[g.n] = mapped_src[i] + head;
+                g.units[g.n] = up[i].bytes - head;
+                g.wide[g.n++] = 0;
+            }
+        }
+        for (int i = 0; i < g.n; ++i) g.total += g.units[i];
+        if (g.total > 0) {
+            const unsigned long long blocks = std::min<unsigned long long>((g.total + 255) / 256, 4096);
+            pull_host_inputs_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(g);
+            rc = launch_status();
+            if (rc != B2_OK) return rc;
+        }
+    } else {
+        for (int i = 0; i < n;) {
+            Up c = up[i++];
+            while (i < n && up[i].dst == c.dst + c.bytes && up[i].src == c.src + c.bytes) c.bytes += up[i++].bytes;
+            const cudaError_t e = cudaMemcpyAsync(c.dst, c.src, c.bytes, cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return fail(static_cast<int>(e), cudaGetErrorString(e));
+            }
         }
     }
     // Output straight into the caller's buffer when it is page-locked host
@@ -751,6 +840,14 @@ int b2_paged_attention_host(const B2PagedAttnArgs* a, const B2AttnHostIO* io, vo
             mapped_out = pa.devicePointer;
         cudaGetLastError();
     }
+    // The inputs are written by the pull kernel: a launch that reads them
+    // before griddepcontrol.wait (a nonzero flags value) must not start until
+    // that kernel has completed.
+    struct FullDependency {
+        bool prev;
+        explicit FullDependency(bool on) : prev(t_full_dependency) { t_full_dependency = on; }
+        ~FullDependency() { t_full_dependency = prev; }
+    } full_dependency(pull && a->flags != 0);
     if (mapped_out != nullptr && aligned16(mapped_out)) {
         B2PagedAttnArgs direct = *a;
         direct.out = mapped_out;

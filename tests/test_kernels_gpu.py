@@ -148,14 +148,17 @@ def test_paged_attention_native_output_and_bias(b2, cuda, dt):
     assert np.all(np.abs(got - ref) <= bound)
 
 
-@pytest.mark.parametrize("dt,Dh,H,Hkv,packed", [(O.F16, 64, 12, 12, True), (O.F16, 64, 12, 12, False),
-                                                 (O.BF16, 128, 32, 8, True), (O.F32, 64, 8, 4, False)])
-def test_paged_attention_host_buffers(b2, cuda, dt, Dh, H, Hkv, packed):
-    """b2_paged_attention_host: uploads from pinned host memory (one copy when
-    q | block tables | seq_lens are back to back on both sides), launch,
-    output to the host (stored by the kernel into pinned memory, or copied into
-    pageable memory), sync -- two calls with different inputs through the same
-    device buffers, each against the oracle."""
+@pytest.mark.parametrize("dt,Dh,H,Hkv,packed,pinned_in,flags", [
+    (O.F16, 64, 12, 12, True, True, 0), (O.F16, 64, 12, 12, False, True, 1), (O.F16, 64, 12, 12, True, False, 1),
+    (O.BF16, 128, 32, 8, True, True, 0), (O.F32, 64, 8, 4, False, False, 0)])
+def test_paged_attention_host_buffers(b2, cuda, dt, Dh, H, Hkv, packed, pinned_in, flags):
+    """b2_paged_attention_host: uploads from host memory (page-locked: read by
+    a kernel over the bus; pageable: copies, one when q | block tables |
+    seq_lens are back to back on both sides), launch, output to the host
+    (stored by the kernel into pinned memory, or copied into pageable memory),
+    sync -- two calls with different inputs through the same device buffers,
+    each against the oracle.  With B2_ATTN_INPUTS_READY set the call must
+    still wait for its own uploads."""
     torch = _torch()
     rng = np.random.Generator(np.random.PCG64(11 + Dh + H))
     L, layer, B = 2, 1, 9
@@ -179,6 +182,7 @@ def test_paged_attention_host_buffers(b2, cuda, dt, Dh, H, Hkv, packed):
     args = b2.attn_args(qd, q_stride, pd, btd.view(torch.int32).view(B, mbps), sld.view(torch.int32), out,
                         n_head=H, n_kv_head=Hkv, head_dim=Dh, max_blocks_per_seq=mbps, layer_idx=layer, n_layer=L,
                         num_blocks=nb)
+    args.flags = flags
     ws = b2.attention_workspace(args)
     perm = rng.permutation(nb).astype(np.int32)
     for ctx in (ctx_a, ctx_b):
@@ -190,7 +194,9 @@ def test_paged_attention_host_buffers(b2, cuda, dt, Dh, H, Hkv, packed):
             o += n
         q = O.round_to(dt, rng.standard_normal(qn, dtype=np.float32))
         host = torch.from_numpy(np.concatenate([np.ascontiguousarray(q).view(np.uint8), bt.view(np.uint8).reshape(-1),
-                                                np.asarray(ctx, np.int32).view(np.uint8)])).pin_memory()
+                                                np.asarray(ctx, np.int32).view(np.uint8)]))
+        if pinned_in:
+            host = host.pin_memory()
         # pinned (mapped) output: the kernel stores into it; pageable: copied from args.out
         hout = torch.empty(B, H, Dh, dtype=torch.float32)
         if packed:
