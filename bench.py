@@ -335,6 +335,26 @@ def b2_workload(b2, device, seed: int, n_sets: int, pool_blocks: int, batch: int
                                    pool_blocks=pool_blocks, dtype=torch_dtype(), log_uniform=WL.log_uniform)
 
 
+def reduce_over_ranks(dist, x: float, op: str, device) -> float:
+    """x combined over every rank ("max" or "sum"); x itself without a process
+    group.  The tensor lives on `device` (CUDA for NCCL, CPU for gloo).  Every
+    rank must make the same calls in the same order."""
+    if dist is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "sum": dist.ReduceOp.SUM}[op])
+    return float(t.item())
+
+
+def job_rate(dist, units: float, ms: float, device) -> tuple[float, float, float]:
+    """Whole-job throughput of a weak- or strong-scaled run: (units of all
+    ranks, the slowest rank's time in ms, units per second)."""
+    total = reduce_over_ranks(dist, units, "sum", device)
+    t_max = reduce_over_ranks(dist, ms, "max", device)
+    return total, t_max, total / (t_max * 1e-3)
+
+
 def run_ours(args, rank: int, world: int, dist) -> dict | None:
     import torch
     b2 = import_package()
@@ -365,18 +385,10 @@ def run_ours(args, rank: int, world: int, dist) -> dict | None:
         torch.cuda.synchronize(dev)
 
     def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_over_ranks(dist, x, "max", dev)
 
     def sum_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+        return reduce_over_ranks(dist, x, "sum", dev)
 
     # --------------------------------------------------- device-resident timing
     # The launches are replayed from a CUDA graph holding one launch per input
@@ -601,21 +613,11 @@ def engine_result(args, name: str, rank: int, world: int, dist, steps: int, warm
     for extra in samplers[1:]:
         clk.samples.extend(extra.samples)
 
-    def reduce(x: float, op) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=op)
-        return float(t.item())
-
-    import torch.distributed as tdist
-    t_max = reduce(r["ms"], tdist.ReduceOp.MAX if dist else None)
-    tokens = reduce(float(r["tokens"]), tdist.ReduceOp.SUM if dist else None)
-    nbytes = reduce(r["bytes"], tdist.ReduceOp.SUM if dist else None)
+    tokens, t_max, value = job_rate(dist, float(r["tokens"]), r["ms"], dev)
+    nbytes = reduce_over_ranks(dist, r["bytes"], "sum", dev)
     if rank != 0:
         return None
     peak, peak_kind = measured_peak()
-    value = tokens / (t_max * 1e-3)
     achieved = nbytes / (t_max * 1e-3) / 1e9  # whole job, GB/s
     frac = achieved / (peak * world)
     steps_total = steps * r["waves"]

@@ -91,6 +91,40 @@ def step_bytes(w: EngineWorkload, ctx: np.ndarray, world: int = 1) -> float:
     return float(weights * es + (ctx.astype(np.float64) + 1).sum() * kv_row)
 
 
+@dataclass(frozen=True)
+class ShardPlan:
+    """One rank's share of an engine workload."""
+    sharded: bool    # head-sharded: every rank holds every sequence and a slice of the heads
+    per_rank: int    # sequences this rank decodes
+    wave: int        # sequences per wave (one engine batch)
+    waves: int       # waves this rank runs one after the other
+    seed: int        # contexts and last tokens of this rank's sequences
+    token_div: int   # ranks that produce each of this rank's tokens (a head-sharded token counts once)
+
+    def tokens(self, steps: int) -> float:
+        """Tokens of the job this rank accounts for over `steps` steps of every wave."""
+        return self.per_rank * steps / self.token_div
+
+
+def shard_plan(w: EngineWorkload, rank: int, world: int, per_rank_batch: int | None = None) -> ShardPlan:
+    """Sequence-sharded: the global batch split evenly, each rank its own
+    sequences (its own seed); head-sharded: every rank the whole batch (the
+    same seed on every rank) and its slice of the heads.  per_rank_batch
+    overrides the sequences per rank (profiling one GPU's share of a larger
+    job).  A rank runs its sequences in waves of at most w.wave_cap."""
+    sharded = w.head_sharded and world > 1
+    if w.head_sharded and world == 1:
+        raise ValueError("the head-sharded workload needs 2 or more GPUs")
+    if w.global_batch % world:
+        raise ValueError(f"global batch {w.global_batch} does not split over {world} ranks")
+    per_rank = w.global_batch if sharded else w.global_batch // world
+    if per_rank_batch:
+        per_rank = per_rank_batch
+    wave = min(per_rank, w.wave_cap)
+    return ShardPlan(sharded=sharded, per_rank=per_rank, wave=wave, waves=(per_rank + wave - 1) // wave,
+                     seed=20_000 + (0 if sharded else rank), token_div=world if sharded else 1)
+
+
 def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist, device, timed_region=None,
         per_rank_batch: int | None = None, allgather: int = 0, linear: bool = False, gemm_mode: int = 0) -> dict:
     """Runs the workload's waves on this rank; timed_region() (optional) gives a
@@ -102,20 +136,12 @@ def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist,
 
     from . import engine as E
 
-    sharded = w.head_sharded and world > 1
-    if w.head_sharded and world == 1:
-        raise ValueError("the head-sharded workload needs 2 or more GPUs")
-    if w.global_batch % world:
-        raise ValueError(f"global batch {w.global_batch} does not split over {world} ranks")
-    per_rank = w.global_batch if sharded else w.global_batch // world
-    if per_rank_batch:
-        per_rank = per_rank_batch
-    wave = min(per_rank, w.wave_cap)
-    n_waves = (per_rank + wave - 1) // wave
+    plan = shard_plan(w, rank, world, per_rank_batch)
+    sharded, per_rank, wave, n_waves = plan.sharded, plan.per_rank, plan.wave, plan.waves
     total = warmup + steps
     if w.ctx_lo + total > w.n_ctx:
         raise ValueError("too many steps for the context range")
-    rng = np.random.Generator(np.random.PCG64(20_000 + (0 if sharded else rank)))  # shards see the same batch
+    rng = np.random.Generator(np.random.PCG64(plan.seed))
     ctx = rng.integers(w.ctx_lo, w.n_ctx - total + 1, size=per_rank)
     last_tok = rng.integers(0, w.vocab, size=per_rank)
     blocks_needed = max(int(((ctx[i:i + wave] + total + BLOCK_TOKENS - 1) // BLOCK_TOKENS).sum())
@@ -171,7 +197,5 @@ def run(w: EngineWorkload, steps: int, warmup: int, rank: int, world: int, dist,
         for i in ids:
             eng.free_sequence(i)
     eng.close()
-    # a head-sharded job produces each sequence's token once (every rank holds a copy)
-    tokens = per_rank * steps / (world if sharded else 1)
-    return {"ms": timed_ms, "tokens": tokens, "bytes": bytes_timed, "waves": n_waves, "wave": wave,
+    return {"ms": timed_ms, "tokens": plan.tokens(steps), "bytes": bytes_timed, "waves": n_waves, "wave": wave,
             "per_rank": per_rank}
