@@ -833,13 +833,7 @@ int b2_paged_attention_host(const B2PagedAttnArgs* a, const B2AttnHostIO* io, vo
     // Output straight into the caller's buffer when it is page-locked host
     // memory mapped into the device's address space: the stores cross PCIe
     // while the kernel runs instead of in a copy after it.
-    void* mapped_out = nullptr;
-    if (io->out) {
-        cudaPointerAttributes pa;
-        if (cudaPointerGetAttributes(&pa, io->out) == cudaSuccess && pa.type == cudaMemoryTypeHost)
-            mapped_out = pa.devicePointer;
-        cudaGetLastError();
-    }
+    void* mapped_out = io->out ? const_cast<char*>(mapped_host_address(io->out)) : nullptr;
     // The inputs are written by the pull kernel: a launch that reads them
     // before griddepcontrol.wait (a nonzero flags value) must not start until
     // that kernel has completed.
