@@ -5,8 +5,10 @@ engine workload's global batch is spread over the ranks (sequence-sharded:
 disjoint shares that add up to the batch, one seed per rank; head-sharded: the
 whole batch on every rank, one seed, each token counted once), the cross-rank
 reductions (slowest rank's time, units of all ranks) and the job rate made
-from them, and the reference arm under torchrun (rank 0 alone works and prints
-one line; the other rank exits 0 without output).  CPU only."""
+from them, the reference arm under torchrun (rank 0 alone works and prints
+one line; the other rank exits 0 without output), and a rank that leaves
+between steps: the next reduction on the rank that stays ends in an error
+within the group's short timeout instead of waiting.  CPU only."""
 from __future__ import annotations
 
 import json
@@ -68,6 +70,43 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
             json.dump(got, f)
     finally:
         dist.destroy_process_group()
+
+
+def _rank_leaves_early(rank: int, world: int, port: int, out_dir: str) -> None:
+    """Rank 1 leaves between steps (exits before the step's reduction); rank 0's
+    reduction must end with an error within the group's short timeout."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import time
+
+    import torch.distributed as dist
+    sys.path.insert(0, str(ROOT))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    bench = _load_bench()
+    bench.reduce_over_ranks(dist, 1.0, "sum", "cpu")  # step 1: both ranks
+    if rank == 1:
+        os._exit(0)  # gone before step 2, with nothing in flight
+    t0 = time.perf_counter()
+    try:
+        bench.reduce_over_ranks(dist, 1.0, "sum", "cpu")
+        outcome = "returned"
+    except Exception as e:  # noqa: BLE001 -- any error is the detection
+        outcome = type(e).__name__
+    with open(os.path.join(out_dir, "rank0.json"), "w") as f:
+        json.dump({"outcome": outcome, "waited_s": time.perf_counter() - t0}, f)
+    os._exit(0)  # the group cannot be torn down cleanly without its peer
+
+
+def test_a_rank_that_leaves_is_detected_by_the_next_reduction(tmp_path):
+    import torch.multiprocessing as mp
+    ctx = mp.start_processes(_rank_leaves_early, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    r = json.loads((tmp_path / "rank0.json").read_text())
+    assert r["outcome"] != "returned"
+    assert r["waited_s"] < 60
 
 
 def test_two_gloo_ranks_shard_and_reduce(tmp_path):
